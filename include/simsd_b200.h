@@ -1,0 +1,164 @@
+/*
+ * simsd_b200.h - C ABI of the B200 (sm_100a) matmul hot path of SimSD.
+ *
+ * Plain pointers and sizes only: no torch or C++ types cross this boundary.
+ * All device pointers must belong to the device that is current on the calling
+ * thread; `stream` is a cudaStream_t (NULL = legacy default stream).  Every
+ * call is asynchronous on `stream`, performs no host synchronisation and no
+ * allocation, and is safe inside CUDA-graph capture.
+ *
+ * Workspaces are owned by the caller.  The first 256 KiB of every workspace
+ * hold per-tile counters and a device error word: zero them once when the
+ * workspace is created (simsd_workspace_init); the kernels leave them zero.
+ * Calls that share a workspace must be ordered on one stream (overlapping calls
+ * on different streams race on it), which is how the reference shares its
+ * split-K staging buffer (kernels/thin_linear_fused.py:173-190).
+ *
+ * Return value: SIMSD_OK or a negative SIMSD_ERR_* code.  Device-side faults
+ * that a kernel can detect (a bounded wait that ran out, an out-of-range expert
+ * id) are OR-ed into the workspace's error word; read it with
+ * simsd_workspace_error().
+ */
+#ifndef SIMSD_B200_H
+#define SIMSD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes */
+#define SIMSD_OK 0
+#define SIMSD_ERR_SHAPE -1        /* bad rank / size / K mismatch            -> ValueError */
+#define SIMSD_ERR_DTYPE -2        /* unsupported or mismatched dtype         -> TypeError  */
+#define SIMSD_ERR_WORKSPACE -3    /* workspace missing or too small                         */
+#define SIMSD_ERR_LAUNCH -4       /* CUDA launch / attribute error                          */
+#define SIMSD_ERR_ALIGN -5        /* pointer or stride unusable by the requested path       */
+#define SIMSD_ERR_DEVICE -6       /* no usable CUDA device / driver entry point             */
+#define SIMSD_ERR_UNSUPPORTED -7  /* valid request outside this build's limits              */
+
+/* ---- element types */
+#define SIMSD_BF16 0
+#define SIMSD_F16 1
+#define SIMSD_F32 2
+
+/* ---- thin linear epilogues */
+#define SIMSD_EPI_NONE 0     /* y = x w^T (+ bias)                                   */
+#define SIMSD_EPI_SILU_MUL 1 /* y = silu(x w_gate^T) * (x w_up^T), N = intermediate  */
+
+/* ---- thin linear paths */
+#define SIMSD_PATH_AUTO 0    /* tensor cores where the layout allows, else CUDA cores */
+#define SIMSD_PATH_TC 1      /* force the tcgen05/TMA kernel (SIMSD_ERR_ALIGN if not possible) */
+#define SIMSD_PATH_SIMT 2    /* force the CUDA-core kernel                            */
+
+/* Library version string. */
+const char* simsd_version(void);
+
+/* Human-readable name of a status code. */
+const char* simsd_status_string(int status);
+
+/* Number of SMs of the current device (0 if there is none). */
+int simsd_device_sm_count(void);
+
+/* Bytes every workspace reserves at its head for counters and the error word. */
+size_t simsd_workspace_header_bytes(void);
+
+/* Zero a workspace's header on `stream` (asynchronous; call once per new workspace). */
+int simsd_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
+
+/* Copy the workspace's device error word to *out (synchronises `stream`; not for the hot path). */
+int simsd_workspace_error(const void* workspace, void* stream, int* out);
+
+/*
+ * Workspace bytes simsd_thin_linear needs for this shape (header included).
+ * `split` as in simsd_thin_linear.
+ */
+size_t simsd_thin_linear_workspace_size(int M, int N, int K, int dtype, int epilogue, int split);
+
+/*
+ * Thin-M linear:  y[m, n] = sum_k x[m, k] * w[n, k]  (+ bias[n]),  fp32 accumulate.
+ * Replaces thin_linear(x, w, bias, config) - kernels/thin_linear_fused.py:265-345
+ * (kernels _thin_gemv_kernel :67-136 and _thin_gemv_reduce :139-167).
+ *
+ *   x    [M, K]  element (m, k) at x + m*ldx_m + k*ldx_k   (strided views allowed)
+ *   w    [N, K]  element (n, k) at w + n*ldw_n + k*ldw_k   (nn.Linear weight layout)
+ *   w_up [N, K]  same strides as w; SIMSD_EPI_SILU_MUL only (w is then the gate weight)
+ *   bias [N]     or NULL (same dtype as x; SIMSD_EPI_NONE only)
+ *   y    [M, N]  element (m, n) at y + m*ldy_m + n
+ *   dtype        SIMSD_BF16 | SIMSD_F16 | SIMSD_F32 (x, w, bias and y share it;
+ *                fp32 is accumulated in IEEE fp32, never TF32)
+ *   split        0: balance the K reduction over all SMs (deterministic stream-K);
+ *                s > 0: exactly s K-segments per output tile (the reference's
+ *                config SPLIT_K); the sum order is fixed either way, so repeated
+ *                calls are bit-identical.
+ *   path         SIMSD_PATH_*.
+ * M, N, K >= 1.  Any M is accepted; the tensor-core path reads w once per 256 rows of x.
+ */
+int simsd_thin_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w, int64_t ldw_n,
+                      int64_t ldw_k, const void* w_up, const void* bias, void* y, int64_t ldy_m, int M,
+                      int N, int K, int dtype, int epilogue, int split, int path, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/*
+ * MoE router: logits = x wr^T (fp32, fixed summation order), score = sigmoid(logits),
+ * top-k by score + bias (ties to the lower expert id), weights = score of the chosen
+ * experts, renormalised to sum 1 (+1e-20) when `renorm` and k > 1, then times `scale`.
+ * Restates the synthetic router of kernels/workspace/moe_dispatch/build_oracle.py:71-90
+ * with the selection bias of the LLaDA2 gate (remote code, absent from the reference).
+ *
+ *   x [T, H] (row stride ldx, x_dtype), wr [E, H] (row stride ldw, w_dtype),
+ *   bias [E] fp32 or NULL -> topk_ids [T, k] int64, topk_weight [T, k] fp32,
+ *   logits [T, E] fp32 or NULL (optional copy of the logits).
+ * 1 <= k <= min(E, 32), E <= 1024.
+ */
+int simsd_moe_route(const void* x, int64_t ldx, int x_dtype, const void* wr, int64_t ldw,
+                    int w_dtype, const float* bias, int T, int H, int E, int k, int renorm,
+                    float scale, int64_t* topk_ids, float* topk_weight, float* logits,
+                    void* stream);
+
+/*
+ * Expert align: per-expert counts, offsets and the stable slot permutation.
+ * Replaces _align - kernels/moe_dispatch_fused.py:93-132 (bit-exact).
+ *
+ *   topk_ids [S] int64 (S = T*k, slot s = t*k + j), 0 <= id < E <= 1024
+ *   counts [E], offsets [E+1] (exclusive prefix of counts), sorted_slots [S]
+ *   (= argsort(ids, stable=True)), slot_to_row [S] (its inverse; -1 for an invalid id)
+ *   slots_padded [num_tiles*block_m] and tile_expert [num_tiles]: optional (both NULL
+ *   or both set) copies in the reference's padded layout (`slots`, `tile_expert`).
+ *   `err_word`: device int that receives SIMSD_DEV_ERR bits, or NULL.
+ */
+int simsd_moe_align(const int64_t* topk_ids, int S, int E, int32_t* counts, int32_t* offsets,
+                    int32_t* sorted_slots, int32_t* slot_to_row, int block_m, int num_tiles,
+                    int32_t* slots_padded, int32_t* tile_expert, int* err_word, void* stream);
+
+/* Workspace bytes simsd_moe_dispatch needs (header included). */
+size_t simsd_moe_workspace_size(int T, int k, int E, int H, int I, int dtype);
+
+/*
+ * Fused MoE expert dispatch, CUDA-graph capturable (no host sync):
+ *   out[t] = cast( sum_j fp32(down_e(silu(gate_e(x_t)) * up_e(x_t))) * topk_weight[t, j] )
+ * with e = topk_ids[t, j]; when `add` is not NULL, out[t] = cast(cast(that sum) + add[t])
+ * (the shared expert's output added in x.dtype, as the model does).
+ * Replaces moe_dispatch(x, topk_ids, topk_weight, w_gate, w_up, w_down) -
+ * kernels/moe_dispatch_fused.py:165-192 (stock moe_infer, transcribed at
+ * kernels/workspace/moe_dispatch/build_oracle.py:34-67).
+ *
+ *   x [T, H] (row stride ldx), topk_ids [T, k] int64, topk_weight [T, k] fp32,
+ *   w_gate, w_up [E, I, H]: element (e, i, h) at base + e*ldg_e + i*ldg_i + h
+ *   w_down [E, H, I]:       element (e, h, i) at base + e*ldd_e + h*ldd_h + i
+ *   out [T, H] (row stride ld_out), add [T, H] (row stride ld_add) or NULL.
+ *   dtype: x, weights, out and add share it (SIMSD_BF16 | SIMSD_F16 | SIMSD_F32).
+ */
+int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids,
+                       const float* topk_weight, const void* w_gate, const void* w_up,
+                       int64_t ldg_e, int64_t ldg_i, const void* w_down, int64_t ldd_e,
+                       int64_t ldd_h, void* out, int64_t ld_out, const void* add,
+                       int64_t ld_add, int T, int k, int E, int H, int I, int dtype,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SIMSD_B200_H */

@@ -1,0 +1,555 @@
+// extern "C" entry points of libsimsd_b200.so (declared in include/simsd_b200.h).
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <mutex>
+
+#include "moe.cuh"
+#include "simsd_b200.h"
+#include "simt_gemm.cuh"
+#include "tc_gemm.cuh"
+
+using namespace simsd;
+
+namespace {
+
+constexpr int kMaxDev = 64;
+std::mutex g_mu;
+int g_sm_count[kMaxDev];
+bool g_smem_attr[kMaxDev][16];
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+inline int esize(int dtype) { return dtype == SIMSD_F32 ? 4 : 2; }
+inline long long cdiv(long long a, long long b) { return (a + b - 1) / b; }
+
+int current_device() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return -1;
+  return dev;
+}
+
+int sm_count_of(int dev) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_sm_count[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n = 0;
+    g_sm_count[dev] = n;
+  }
+  return g_sm_count[dev];
+}
+
+int ensure_encode() {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_encode) return SIMSD_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) !=
+          cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || fn == nullptr)
+    return SIMSD_ERR_DEVICE;
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return SIMSD_OK;
+}
+
+// 128-byte-swizzled tiled map: box = {64 elements, box_rows[, 1]}.
+int encode_map(CUtensorMap* m, const void* base, int dtype, int rank, const uint64_t* dims,
+               const uint64_t* stride_bytes, uint32_t box_rows) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return SIMSD_ERR_ALIGN;
+  for (int i = 0; i + 1 < rank; ++i)
+    if ((stride_bytes[i] & 15) != 0 || stride_bytes[i] == 0) return SIMSD_ERR_ALIGN;
+  cuuint64_t gdim[3];
+  cuuint64_t gstride[2];
+  cuuint32_t box[3] = {64, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) gdim[i] = dims[i];
+  for (int i = 0; i + 1 < rank; ++i) gstride[i] = stride_bytes[i];
+  const CUtensorMapDataType dt =
+      dtype == SIMSD_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUresult r = g_encode(m, dt, rank, const_cast<void*>(base), gdim, gstride, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? SIMSD_OK : SIMSD_ERR_ALIGN;
+}
+
+int pick_bmax_rows(long long rows) {
+  if (rows <= 16) return 16;
+  if (rows <= 32) return 32;
+  if (rows <= 64) return 64;
+  if (rows <= 128) return 128;
+  return 256;
+}
+
+template <int BMAX>
+int launch_tc_b(const TcGemmArgs& a, int grid, cudaStream_t s, int dev) {
+  constexpr int smem = TcConfig<BMAX>::SMEM_BYTES;
+  constexpr int idx = BMAX == 16 ? 0 : BMAX == 32 ? 1 : BMAX == 64 ? 2 : BMAX == 128 ? 3 : 4;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_smem_attr[dev][idx]) {
+      if (cudaFuncSetAttribute(tc_gemm_kernel<BMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+          cudaSuccess)
+        return SIMSD_ERR_LAUNCH;
+      g_smem_attr[dev][idx] = true;
+    }
+  }
+  tc_gemm_kernel<BMAX><<<grid, TC_THREADS, smem, s>>>(a);
+  return cudaGetLastError() == cudaSuccess ? SIMSD_OK : SIMSD_ERR_LAUNCH;
+}
+
+int launch_tc(int bmax, const TcGemmArgs& a, int grid, cudaStream_t s, int dev) {
+  switch (bmax) {
+    case 16: return launch_tc_b<16>(a, grid, s, dev);
+    case 32: return launch_tc_b<32>(a, grid, s, dev);
+    case 64: return launch_tc_b<64>(a, grid, s, dev);
+    case 128: return launch_tc_b<128>(a, grid, s, dev);
+    case 256: return launch_tc_b<256>(a, grid, s, dev);
+  }
+  return SIMSD_ERR_UNSUPPORTED;
+}
+
+// ---------------------------------------------------------------- thin linear plan
+struct ThinPlan {
+  int bmax, row_tiles, kb, grid;
+  long long tiles, iters;
+  size_t ws_bytes;
+};
+
+ThinPlan plan_thin(int M, int N, int K, int epilogue, int split, int sms) {
+  ThinPlan p{};
+  p.bmax = pick_bmax_rows(M);
+  p.row_tiles = (int)(epilogue == SIMSD_EPI_SILU_MUL ? cdiv(N, 64) : cdiv(N, 128));
+  p.kb = (int)cdiv(K, 64);
+  p.tiles = cdiv(M, p.bmax) * p.row_tiles;
+  p.iters = p.tiles * p.kb;
+  long long g;
+  if (split > 0) g = std::min<long long>(p.tiles * split, p.iters);
+  else g = std::min<long long>(sms > 0 ? sms : 148, p.iters);
+  g = std::max<long long>(1, std::min<long long>(g, TC_MAX_GRID));
+  p.grid = (int)g;
+  p.ws_bytes = WS_COUNTER_BYTES + align256((size_t)2 * p.grid * p.bmax * 128 * sizeof(float));
+  return p;
+}
+
+int thin_tc_possible(const void* x, long long ldx_m, long long ldx_k, const void* w, long long ldw_n,
+                     long long ldw_k, const void* w_up, int M, int N, int K, int dtype) {
+  if (dtype != SIMSD_BF16 && dtype != SIMSD_F16) return 0;
+  if (ldx_k != 1 || ldw_k != 1) return 0;
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!al(x) || !al(w) || (w_up && !al(w_up))) return 0;
+  if (M > 1 && (ldx_m < K || ((ldx_m * 2) & 15) != 0)) return 0;
+  if (N > 1 && (ldw_n < K || ((ldw_n * 2) & 15) != 0)) return 0;
+  return 1;
+}
+
+}  // namespace
+
+// ======================================================================== API
+extern "C" {
+
+const char* simsd_version(void) { return "simsd_b200 0.1 (sm_100a)"; }
+
+const char* simsd_status_string(int s) {
+  switch (s) {
+    case SIMSD_OK: return "ok";
+    case SIMSD_ERR_SHAPE: return "bad shape";
+    case SIMSD_ERR_DTYPE: return "bad dtype";
+    case SIMSD_ERR_WORKSPACE: return "workspace missing or too small";
+    case SIMSD_ERR_LAUNCH: return "CUDA launch failed";
+    case SIMSD_ERR_ALIGN: return "pointer or stride not usable by this path";
+    case SIMSD_ERR_DEVICE: return "no usable CUDA device";
+    case SIMSD_ERR_UNSUPPORTED: return "outside this build's limits";
+  }
+  return "unknown status";
+}
+
+int simsd_device_sm_count(void) {
+  const int dev = current_device();
+  return dev < 0 ? 0 : sm_count_of(dev);
+}
+
+size_t simsd_workspace_header_bytes(void) { return WS_COUNTER_BYTES; }
+
+int simsd_workspace_init(void* ws, size_t bytes, void* stream) {
+  if (ws == nullptr || bytes < (size_t)WS_COUNTER_BYTES) return SIMSD_ERR_WORKSPACE;
+  return cudaMemsetAsync(ws, 0, WS_COUNTER_BYTES, (cudaStream_t)stream) == cudaSuccess ? SIMSD_OK
+                                                                                      : SIMSD_ERR_LAUNCH;
+}
+
+int simsd_workspace_error(const void* ws, void* stream, int* out) {
+  if (ws == nullptr || out == nullptr) return SIMSD_ERR_WORKSPACE;
+  int v = 0;
+  if (cudaMemcpyAsync(&v, reinterpret_cast<const char*>(ws) + WS_ERR_OFFSET, sizeof(int), cudaMemcpyDeviceToHost,
+                      (cudaStream_t)stream) != cudaSuccess)
+    return SIMSD_ERR_LAUNCH;
+  if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return SIMSD_ERR_LAUNCH;
+  *out = v;
+  return SIMSD_OK;
+}
+
+size_t simsd_thin_linear_workspace_size(int M, int N, int K, int dtype, int epilogue, int split) {
+  if (M < 1 || N < 1 || K < 1) return WS_COUNTER_BYTES;
+  (void)dtype;
+  const int dev = current_device();
+  const int sms = dev < 0 ? 148 : sm_count_of(dev);
+  return plan_thin(M, N, K, epilogue, split, sms).ws_bytes;
+}
+
+int simsd_thin_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w, int64_t ldw_n, int64_t ldw_k,
+                      const void* w_up, const void* bias, void* y, int64_t ldy_m, int M, int N, int K, int dtype,
+                      int epilogue, int split, int path, void* workspace, size_t workspace_bytes, void* stream) {
+  if (M < 1 || N < 1 || K < 1 || split < 0) return SIMSD_ERR_SHAPE;
+  if (dtype != SIMSD_BF16 && dtype != SIMSD_F16 && dtype != SIMSD_F32) return SIMSD_ERR_DTYPE;
+  if (epilogue != SIMSD_EPI_NONE && epilogue != SIMSD_EPI_SILU_MUL) return SIMSD_ERR_UNSUPPORTED;
+  const bool silu = epilogue == SIMSD_EPI_SILU_MUL;
+  if (silu && (w_up == nullptr || bias != nullptr)) return SIMSD_ERR_UNSUPPORTED;
+  if (x == nullptr || w == nullptr || y == nullptr) return SIMSD_ERR_SHAPE;
+  if (workspace == nullptr || workspace_bytes < (size_t)WS_COUNTER_BYTES) return SIMSD_ERR_WORKSPACE;
+  const int dev = current_device();
+  if (dev < 0) return SIMSD_ERR_DEVICE;
+  cudaStream_t s = (cudaStream_t)stream;
+  int* err = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + WS_ERR_OFFSET);
+
+  const bool tc_ok = thin_tc_possible(x, ldx_m, ldx_k, w, ldw_n, ldw_k, w_up, M, N, K, dtype) != 0;
+  bool use_tc;
+  if (path == SIMSD_PATH_TC) {
+    if (!tc_ok) return SIMSD_ERR_ALIGN;
+    use_tc = true;
+  } else if (path == SIMSD_PATH_SIMT) {
+    use_tc = false;
+  } else {
+    use_tc = tc_ok && K >= 64;
+  }
+
+  if (use_tc) {
+    if (ensure_encode() != SIMSD_OK) return SIMSD_ERR_DEVICE;
+    const ThinPlan pl = plan_thin(M, N, K, epilogue, split, sm_count_of(dev));
+    if (workspace_bytes < pl.ws_bytes) return SIMSD_ERR_WORKSPACE;
+    if (pl.tiles > WS_MAX_COUNTERS) return SIMSD_ERR_UNSUPPORTED;
+    TcGemmArgs a;
+    memset(&a, 0, sizeof(a));
+    const long long lx = (M > 1) ? ldx_m : ((K * 2 + 15) / 16) * 8;
+    const long long lw = (N > 1) ? ldw_n : ((K * 2 + 15) / 16) * 8;
+    const uint64_t xd[2] = {(uint64_t)K, (uint64_t)M}, xs[1] = {(uint64_t)lx * 2};
+    const uint64_t wd[2] = {(uint64_t)K, (uint64_t)N}, wsb[1] = {(uint64_t)lw * 2};
+    int rc = encode_map(&a.tmB, x, dtype, 2, xd, xs, TC_BOX_ROWS);
+    if (rc == SIMSD_OK) rc = encode_map(&a.tmA0, w, dtype, 2, wd, wsb, silu ? 64 : 128);
+    if (rc == SIMSD_OK && silu) rc = encode_map(&a.tmA1, w_up, dtype, 2, wd, wsb, 64);
+    if (rc != SIMSD_OK) return rc;
+    a.out = y;
+    a.ld_out = ldy_m;
+    a.bias = bias;
+    a.partials = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + WS_COUNTER_BYTES);
+    a.tile_counters = reinterpret_cast<int*>(workspace);
+    a.err = err;
+    a.group_counts = nullptr;
+    a.num_groups = 1;
+    a.single_rows = M;
+    a.kb = pl.kb;
+    a.rows_out = N;
+    a.row_tiles = pl.row_tiles;
+    a.silu = silu ? 1 : 0;
+    a.three_d = 0;
+    a.is_bf16 = dtype == SIMSD_BF16 ? 1 : 0;
+    a.max_tiles = WS_MAX_COUNTERS;
+    return launch_tc(pl.bmax, a, pl.grid, s, dev);
+  }
+
+  SimtGemmArgs a;
+  memset(&a, 0, sizeof(a));
+  a.a = x;
+  a.w = w;
+  a.w_up = w_up;
+  a.bias = bias;
+  a.out = y;
+  a.group_counts = nullptr;
+  a.err = err;
+  a.lda_m = ldx_m;
+  a.lda_k = ldx_k;
+  a.ldw_n = ldw_n;
+  a.ldw_k = ldw_k;
+  a.ldw_g = 0;
+  a.ld_out = ldy_m;
+  a.rows = M;
+  a.num_groups = 1;
+  a.N = N;
+  a.K = K;
+  a.dtype = dtype;
+  a.silu = silu ? 1 : 0;
+  const long long gy = cdiv(M, SIMT_ROWS);
+  if (gy > 65535) return SIMSD_ERR_UNSUPPORTED;
+  dim3 grid((unsigned)cdiv(N, SIMT_WARPS), (unsigned)gy);
+  simt_gemm_kernel<<<grid, SIMT_WARPS * 32, 0, s>>>(a);
+  return cudaGetLastError() == cudaSuccess ? SIMSD_OK : SIMSD_ERR_LAUNCH;
+}
+
+// ---------------------------------------------------------------- MoE
+int simsd_moe_route(const void* x, int64_t ldx, int x_dtype, const void* wr, int64_t ldw, int w_dtype,
+                    const float* bias, int T, int H, int E, int k, int renorm, float scale, int64_t* topk_ids,
+                    float* topk_weight, float* logits, void* stream) {
+  if (T < 0 || H < 1 || E < 1 || E > 1024 || k < 1 || k > 32 || k > E) return SIMSD_ERR_SHAPE;
+  if (x_dtype < 0 || x_dtype > 2 || w_dtype < 0 || w_dtype > 2) return SIMSD_ERR_DTYPE;
+  if (T == 0) return SIMSD_OK;
+  if (!x || !wr || !topk_ids || !topk_weight) return SIMSD_ERR_SHAPE;
+  RouteArgs a;
+  a.x = x;
+  a.w = wr;
+  a.bias = bias;
+  a.topk_ids = reinterpret_cast<long long*>(topk_ids);
+  a.topk_weight = topk_weight;
+  a.logits = logits;
+  a.ldx = ldx;
+  a.ldw = ldw;
+  a.T = T;
+  a.H = H;
+  a.E = E;
+  a.k = k;
+  a.x_dtype = x_dtype;
+  a.w_dtype = w_dtype;
+  a.renorm = renorm;
+  a.scale = scale;
+  const int smem = 2 * ROUTE_TOK * E * (int)sizeof(float);
+  const int dev = current_device();
+  if (dev < 0) return SIMSD_ERR_DEVICE;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_smem_attr[dev][8]) {
+      if (cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * ROUTE_TOK * 1024 * 4) !=
+          cudaSuccess)
+        return SIMSD_ERR_LAUNCH;
+      g_smem_attr[dev][8] = true;
+    }
+  }
+  route_kernel<<<(unsigned)cdiv(T, ROUTE_TOK), ROUTE_WARPS * 32, smem, (cudaStream_t)stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? SIMSD_OK : SIMSD_ERR_LAUNCH;
+}
+
+static int launch_align(const int64_t* ids, int S, int E, int32_t* counts, int32_t* offsets, int32_t* sorted,
+                        int32_t* s2r, int block_m, int num_tiles, int32_t* slots_padded, int32_t* tile_expert,
+                        int* err, cudaStream_t s, int dev) {
+  AlignArgs a;
+  a.ids = reinterpret_cast<const long long*>(ids);
+  a.counts = counts;
+  a.offsets = offsets;
+  a.sorted_slots = sorted;
+  a.slot_to_row = s2r;
+  a.slots_padded = slots_padded;
+  a.tile_expert = tile_expert;
+  a.err = err;
+  a.S = S;
+  a.E = E;
+  a.block_m = block_m;
+  a.num_tiles = num_tiles;
+  const int smem = (32 * E + 2 * (E + 1)) * (int)sizeof(int);
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_smem_attr[dev][9]) {
+      if (cudaFuncSetAttribute(align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (32 * 1024 + 2 * 1025) * 4) != cudaSuccess)
+        return SIMSD_ERR_LAUNCH;
+      g_smem_attr[dev][9] = true;
+    }
+  }
+  align_kernel<<<1, ALIGN_THREADS, smem, s>>>(a);
+  return cudaGetLastError() == cudaSuccess ? SIMSD_OK : SIMSD_ERR_LAUNCH;
+}
+
+int simsd_moe_align(const int64_t* topk_ids, int S, int E, int32_t* counts, int32_t* offsets, int32_t* sorted_slots,
+                    int32_t* slot_to_row, int block_m, int num_tiles, int32_t* slots_padded, int32_t* tile_expert,
+                    int* err_word, void* stream) {
+  if (S < 0 || E < 1 || E > 1024) return SIMSD_ERR_SHAPE;
+  if ((slots_padded == nullptr) != (tile_expert == nullptr)) return SIMSD_ERR_SHAPE;
+  if (slots_padded && (block_m < 1 || num_tiles < 0)) return SIMSD_ERR_SHAPE;
+  if (!counts || !offsets || (S > 0 && (!topk_ids || !sorted_slots || !slot_to_row))) return SIMSD_ERR_SHAPE;
+  const int dev = current_device();
+  if (dev < 0) return SIMSD_ERR_DEVICE;
+  if (err_word == nullptr) return SIMSD_ERR_WORKSPACE;
+  return launch_align(topk_ids, S, E, counts, offsets, sorted_slots, slot_to_row, block_m, num_tiles, slots_padded,
+                      tile_expert, err_word, (cudaStream_t)stream, dev);
+}
+
+namespace {
+struct MoePlan {
+  bool tc;
+  int bmax, grid;
+  size_t off_counts, off_offsets, off_sorted, off_s2r, off_xs, off_h, off_ys, off_part, total;
+  long long max_tiles;
+};
+
+MoePlan plan_moe(int T, int k, int E, int H, int I, int dtype, int sms, bool tc) {
+  MoePlan p{};
+  const long long S = (long long)T * k;
+  const int es = esize(dtype);
+  p.tc = tc;
+  const long long avg = E > 0 ? S / E : S;
+  p.bmax = avg <= 8 ? 16 : avg <= 16 ? 32 : avg <= 32 ? 64 : 128;
+  p.grid = std::max(1, std::min(sms > 0 ? sms : 148, TC_MAX_GRID));
+  size_t o = WS_COUNTER_BYTES;
+  p.off_counts = o; o = align256(o + (size_t)E * 4);
+  p.off_offsets = o; o = align256(o + (size_t)(E + 1) * 4);
+  p.off_sorted = o; o = align256(o + (size_t)S * 4);
+  p.off_s2r = o; o = align256(o + (size_t)S * 4);
+  p.off_xs = o; o = align256(o + (size_t)S * H * es);
+  p.off_h = o; o = align256(o + (size_t)S * I * es);
+  p.off_ys = o; o = align256(o + (size_t)S * H * es);
+  p.off_part = o;
+  if (tc) o = align256(o + (size_t)2 * p.grid * p.bmax * 128 * sizeof(float));
+  p.total = o;
+  const long long rt = std::max(cdiv(I, 64), cdiv(H, 128));
+  p.max_tiles = (std::min<long long>(E, S) + S / p.bmax + 1) * rt;
+  return p;
+}
+}  // namespace
+
+size_t simsd_moe_workspace_size(int T, int k, int E, int H, int I, int dtype) {
+  if (T < 0 || k < 1 || E < 1 || H < 1 || I < 1) return WS_COUNTER_BYTES;
+  const int dev = current_device();
+  const int sms = dev < 0 ? 148 : sm_count_of(dev);
+  return plan_moe(T, k, E, H, I, dtype, sms, dtype != SIMSD_F32).total;
+}
+
+int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, const float* topk_weight,
+                       const void* w_gate, const void* w_up, int64_t ldg_e, int64_t ldg_i, const void* w_down,
+                       int64_t ldd_e, int64_t ldd_h, void* out, int64_t ld_out, const void* add, int64_t ld_add,
+                       int T, int k, int E, int H, int I, int dtype, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  if (T < 0 || k < 1 || E < 1 || E > 1024 || H < 1 || I < 1) return SIMSD_ERR_SHAPE;
+  if (dtype != SIMSD_BF16 && dtype != SIMSD_F16 && dtype != SIMSD_F32) return SIMSD_ERR_DTYPE;
+  if (workspace == nullptr || workspace_bytes < (size_t)WS_COUNTER_BYTES) return SIMSD_ERR_WORKSPACE;
+  if (T == 0) return SIMSD_OK;
+  if (!x || !topk_ids || !topk_weight || !w_gate || !w_up || !w_down || !out) return SIMSD_ERR_SHAPE;
+  const int dev = current_device();
+  if (dev < 0) return SIMSD_ERR_DEVICE;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int es = esize(dtype);
+  const long long S = (long long)T * k;
+  if (S > (1LL << 30)) return SIMSD_ERR_UNSUPPORTED;
+
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  bool tc = dtype != SIMSD_F32 && H >= 64 && I >= 64 && (H % 8) == 0 && (I % 8) == 0 && al(w_gate) && al(w_up) &&
+            al(w_down) && (ldg_e % 8) == 0 && (ldg_i % 8) == 0 && (ldd_e % 8) == 0 && (ldd_h % 8) == 0 &&
+            ldg_i >= H && ldd_h >= I;
+  const MoePlan pl = plan_moe(T, k, E, H, I, dtype, sm_count_of(dev), tc);
+  if (tc && pl.max_tiles > WS_MAX_COUNTERS) tc = false;
+  const MoePlan plan = tc ? pl : plan_moe(T, k, E, H, I, dtype, sm_count_of(dev), false);
+  if (workspace_bytes < plan.total) return SIMSD_ERR_WORKSPACE;
+
+  char* ws = reinterpret_cast<char*>(workspace);
+  int* err = reinterpret_cast<int*>(ws + WS_ERR_OFFSET);
+  int32_t* counts = reinterpret_cast<int32_t*>(ws + plan.off_counts);
+  int32_t* offsets = reinterpret_cast<int32_t*>(ws + plan.off_offsets);
+  int32_t* sorted = reinterpret_cast<int32_t*>(ws + plan.off_sorted);
+  int32_t* s2r = reinterpret_cast<int32_t*>(ws + plan.off_s2r);
+  void* xs = ws + plan.off_xs;
+  void* hbuf = ws + plan.off_h;
+  void* ys = ws + plan.off_ys;
+
+  int rc = launch_align(topk_ids, (int)S, E, counts, offsets, sorted, s2r, 16, 0, nullptr, nullptr, err, s, dev);
+  if (rc != SIMSD_OK) return rc;
+  gather_rows_kernel<<<(unsigned)S, 256, 0, s>>>(x, ldx, sorted, xs, H, (int)S, k, H, es);
+  if (cudaGetLastError() != cudaSuccess) return SIMSD_ERR_LAUNCH;
+
+  if (plan.tc) {
+    if (ensure_encode() != SIMSD_OK) return SIMSD_ERR_DEVICE;
+    // gate/up: out[row, i] = silu(xs[row] . w_gate[e, i]) * (xs[row] . w_up[e, i])
+    TcGemmArgs a;
+    memset(&a, 0, sizeof(a));
+    {
+      const uint64_t gd[3] = {(uint64_t)H, (uint64_t)I, (uint64_t)E};
+      const uint64_t gs[2] = {(uint64_t)ldg_i * es, (uint64_t)ldg_e * es};
+      const uint64_t bd[2] = {(uint64_t)H, (uint64_t)S};
+      const uint64_t bs[1] = {(uint64_t)H * es};
+      rc = encode_map(&a.tmA0, w_gate, dtype, 3, gd, gs, 64);
+      if (rc == SIMSD_OK) rc = encode_map(&a.tmA1, w_up, dtype, 3, gd, gs, 64);
+      if (rc == SIMSD_OK) rc = encode_map(&a.tmB, xs, dtype, 2, bd, bs, TC_BOX_ROWS);
+      if (rc != SIMSD_OK) return rc;
+    }
+    a.out = hbuf;
+    a.ld_out = I;
+    a.partials = reinterpret_cast<float*>(ws + plan.off_part);
+    a.tile_counters = reinterpret_cast<int*>(ws);
+    a.err = err;
+    a.group_counts = counts;
+    a.num_groups = E;
+    a.kb = (int)cdiv(H, 64);
+    a.rows_out = I;
+    a.row_tiles = (int)cdiv(I, 64);
+    a.silu = 1;
+    a.three_d = 1;
+    a.is_bf16 = dtype == SIMSD_BF16 ? 1 : 0;
+    a.max_tiles = WS_MAX_COUNTERS;
+    rc = launch_tc(plan.bmax, a, plan.grid, s, dev);
+    if (rc != SIMSD_OK) return rc;
+    // down: ys[row, h] = hbuf[row] . w_down[e, h]
+    TcGemmArgs d;
+    memset(&d, 0, sizeof(d));
+    {
+      const uint64_t dd[3] = {(uint64_t)I, (uint64_t)H, (uint64_t)E};
+      const uint64_t ds[2] = {(uint64_t)ldd_h * es, (uint64_t)ldd_e * es};
+      const uint64_t bd[2] = {(uint64_t)I, (uint64_t)S};
+      const uint64_t bs[1] = {(uint64_t)I * es};
+      rc = encode_map(&d.tmA0, w_down, dtype, 3, dd, ds, 128);
+      if (rc == SIMSD_OK) rc = encode_map(&d.tmB, hbuf, dtype, 2, bd, bs, TC_BOX_ROWS);
+      if (rc != SIMSD_OK) return rc;
+    }
+    d.out = ys;
+    d.ld_out = H;
+    d.partials = a.partials;
+    d.tile_counters = a.tile_counters;
+    d.err = err;
+    d.group_counts = counts;
+    d.num_groups = E;
+    d.kb = (int)cdiv(I, 64);
+    d.rows_out = H;
+    d.row_tiles = (int)cdiv(H, 128);
+    d.silu = 0;
+    d.three_d = 1;
+    d.is_bf16 = a.is_bf16;
+    d.max_tiles = WS_MAX_COUNTERS;
+    rc = launch_tc(plan.bmax, d, plan.grid, s, dev);
+    if (rc != SIMSD_OK) return rc;
+  } else {
+    const long long max_chunks = std::min<long long>(E, S) + S / SIMT_ROWS + 1;
+    if (max_chunks > 65535) return SIMSD_ERR_UNSUPPORTED;
+    SimtGemmArgs a;
+    memset(&a, 0, sizeof(a));
+    a.a = xs;
+    a.w = w_gate;
+    a.w_up = w_up;
+    a.out = hbuf;
+    a.group_counts = counts;
+    a.err = err;
+    a.lda_m = H;
+    a.lda_k = 1;
+    a.ldw_n = ldg_i;
+    a.ldw_k = 1;
+    a.ldw_g = ldg_e;
+    a.ld_out = I;
+    a.num_groups = E;
+    a.N = I;
+    a.K = H;
+    a.dtype = dtype;
+    a.silu = 1;
+    simt_gemm_kernel<<<dim3((unsigned)cdiv(I, SIMT_WARPS), (unsigned)max_chunks), SIMT_WARPS * 32, 0, s>>>(a);
+    if (cudaGetLastError() != cudaSuccess) return SIMSD_ERR_LAUNCH;
+    SimtGemmArgs d = a;
+    d.a = hbuf;
+    d.w = w_down;
+    d.w_up = nullptr;
+    d.out = ys;
+    d.lda_m = I;
+    d.ldw_n = ldd_h;
+    d.ldw_g = ldd_e;
+    d.ld_out = H;
+    d.N = H;
+    d.K = I;
+    d.silu = 0;
+    simt_gemm_kernel<<<dim3((unsigned)cdiv(H, SIMT_WARPS), (unsigned)max_chunks), SIMT_WARPS * 32, 0, s>>>(d);
+    if (cudaGetLastError() != cudaSuccess) return SIMSD_ERR_LAUNCH;
+  }
+  combine_kernel<<<(unsigned)T, 256, 0, s>>>(ys, H, s2r, topk_weight, out, ld_out, add, ld_add, T, k, H, dtype);
+  return cudaGetLastError() == cudaSuccess ? SIMSD_OK : SIMSD_ERR_LAUNCH;
+}
+
+}  // extern "C"

@@ -1,0 +1,406 @@
+// MoE dispatch kernels: top-k router, expert align (histogram, offsets, stable
+// permutation), token-row gather and the fp32 weighted combine.
+//
+// Reference: kernels/moe_dispatch_fused.py:93-132 (`_align`), :165-192
+// (`moe_dispatch`), and the synthetic router of
+// kernels/workspace/moe_dispatch/build_oracle.py:71-90 (sigmoid scores, top-k,
+// renormalise, routed scale).  The real LLaDA2 gate is remote code that is not
+// part of the reference; the router here selects on sigmoid(logit) + bias.
+//
+// Routing is integer work downstream of fp32 logits, so it can only be
+// bit-exact against a checker that computes the same logits bit for bit.  The
+// router therefore fixes its arithmetic completely:
+//   logit[t,e]: lane l (0..31) of a warp accumulates, with fp32 fma, the
+//     8-element chunks c = l, l+32, l+64, ... of x[t,:] . w[e,:] in increasing
+//     element order; the 32 lane sums are combined by the xor butterfly
+//     (16, 8, 4, 2, 1), v_l <- v_l + v_{l^m};
+//   score = 1 / (1 + exp(-logit)) with exp_fixed() below;
+//   choice = score + bias[e]; top-k by choice, ties to the lower expert id,
+//     NaN ranked below every number;
+//   weight_j = score[id_j]; if renormalising and k > 1:
+//     weight_j /= (((w_0 + w_1) + w_2) + ...) + 1e-20; then weight_j *= scale.
+// Every operation is an explicitly rounded fp32 op, so the C oracle
+// (oracle/simsd_oracle.c) reproduces it exactly.
+#pragma once
+#include "sm100.cuh"
+
+namespace simsd {
+
+// exp(x) in fp32 by Cody-Waite reduction x = n ln2 + r (ln2 split into a high
+// part with 11 trailing zero bits and the remainder), |r| <= ln2/2, and the
+// degree-7 Taylor polynomial of e^r in Horner form (truncation error below
+// 2^-24 relative); 2^n is applied in two exact power-of-two steps.
+__device__ __forceinline__ float exp_fixed(float x) {
+  if (!(x == x)) return x;
+  if (x > 88.72283935546875f) return __int_as_float(0x7f800000);
+  if (x < -103.97208404541015625f) return 0.0f;
+  const float n = rintf(__fmul_rn(x, 1.44269502162933349609375f));
+  float r = __fmaf_rn(n, -0.693145751953125f, x);
+  r = __fmaf_rn(n, -1.428606765330187045037746429443359375e-06f, r);
+  float q = 1.98412701138295233249664306640625e-04f;  // 1/5040
+  q = __fmaf_rn(q, r, 1.3888889225199818611145019531250e-03f);  // 1/720
+  q = __fmaf_rn(q, r, 8.3333337679505348205566406250000e-03f);  // 1/120
+  q = __fmaf_rn(q, r, 4.1666667908430099487304687500000e-02f);  // 1/24
+  q = __fmaf_rn(q, r, 1.6666667163372039794921875000000e-01f);  // 1/6
+  q = __fmaf_rn(q, r, 0.5f);
+  q = __fmaf_rn(q, r, 1.0f);
+  q = __fmaf_rn(q, r, 1.0f);
+  const int ni = (int)n;
+  const int n1 = ni >> 1;   // floor(n/2)
+  const int n2 = ni - n1;
+  q = __fmul_rn(q, __int_as_float((n1 + 127) << 23));
+  q = __fmul_rn(q, __int_as_float((n2 + 127) << 23));
+  return q;
+}
+
+__device__ __forceinline__ float sigmoid_fixed(float z) {
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_fixed(-z)));
+}
+
+// ------------------------------------------------------------------ router
+struct RouteArgs {
+  const void* x;          // [T, H], row stride ldx
+  const void* w;          // [E, H], row stride ldw
+  const float* bias;      // [E] or nullptr
+  long long* topk_ids;    // [T, k]
+  float* topk_weight;     // [T, k]
+  float* logits;          // [T, E] or nullptr (debug / parity)
+  long long ldx, ldw;
+  int T, H, E, k;
+  int x_dtype, w_dtype;   // 0 bf16, 1 fp16, 2 fp32
+  int renorm;
+  float scale;
+};
+
+constexpr int ROUTE_TOK = 16;    // tokens per CTA
+constexpr int ROUTE_EXP = 4;     // experts per warp pass
+constexpr int ROUTE_WARPS = 8;
+
+__device__ __forceinline__ void load8(const void* base, long long idx, int dtype, int n_valid, float (&v)[8]) {
+  if (n_valid == 8 && dtype != 2 && ((reinterpret_cast<uintptr_t>(base) + idx * 2) & 15) == 0) {
+    const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(base) + idx * 2);
+    const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (dtype == 0) {
+        v[2 * i] = __uint_as_float(w4[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w4[i] & 0xffff0000u);
+      } else {
+        __half2 h = *reinterpret_cast<const __half2*>(&w4[i]);
+        const float2 f = __half22float2(h);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+      }
+    }
+    return;
+  }
+  if (n_valid == 8 && dtype == 2 && ((reinterpret_cast<uintptr_t>(base) + idx * 4) & 15) == 0) {
+    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + idx);
+    const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + idx + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = (i < n_valid) ? load_f(base, idx + i, dtype) : 0.0f;
+}
+
+__global__ void __launch_bounds__(ROUTE_WARPS * 32) route_kernel(const RouteArgs p) {
+  extern __shared__ float sh[];
+  float* s_score = sh;                          // [ROUTE_TOK][E]
+  float* s_choice = sh + ROUTE_TOK * p.E;       // [ROUTE_TOK][E]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.x * ROUTE_TOK;
+  const int ntok = min(ROUTE_TOK, p.T - t0);
+  const int nchunks = (p.H + 7) / 8;
+
+  for (int e0 = warp * ROUTE_EXP; e0 < p.E; e0 += ROUTE_WARPS * ROUTE_EXP) {
+    float acc[ROUTE_TOK][ROUTE_EXP];
+#pragma unroll
+    for (int t = 0; t < ROUTE_TOK; ++t)
+#pragma unroll
+      for (int j = 0; j < ROUTE_EXP; ++j) acc[t][j] = 0.0f;
+    for (int c = lane; c < nchunks; c += 32) {
+      const int k0 = c * 8;
+      const int nv = min(8, p.H - k0);
+      float wv[ROUTE_EXP][8];
+#pragma unroll
+      for (int j = 0; j < ROUTE_EXP; ++j) {
+        if (e0 + j < p.E) load8(p.w, (long long)(e0 + j) * p.ldw + k0, p.w_dtype, nv, wv[j]);
+        else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) wv[j][i] = 0.0f;
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < ROUTE_TOK; ++t) {
+        if (t < ntok) {
+          float xv[8];
+          load8(p.x, (long long)(t0 + t) * p.ldx + k0, p.x_dtype, nv, xv);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < ROUTE_EXP; ++j) acc[t][j] = __fmaf_rn(xv[i], wv[j][i], acc[t][j]);
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < ROUTE_TOK; ++t)
+#pragma unroll
+      for (int j = 0; j < ROUTE_EXP; ++j) {
+        float v = acc[t][j];
+#pragma unroll
+        for (int m = 16; m > 0; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
+        acc[t][j] = v;
+      }
+    if (lane == 0) {
+#pragma unroll
+      for (int t = 0; t < ROUTE_TOK; ++t)
+#pragma unroll
+        for (int j = 0; j < ROUTE_EXP; ++j)
+          if (t < ntok && e0 + j < p.E) {
+            const int e = e0 + j;
+            const float lg = acc[t][j];
+            if (p.logits) p.logits[(long long)(t0 + t) * p.E + e] = lg;
+            const float s = sigmoid_fixed(lg);
+            s_score[t * p.E + e] = s;
+            s_choice[t * p.E + e] = p.bias ? __fadd_rn(s, p.bias[e]) : s;
+          }
+    }
+  }
+  __syncthreads();
+
+  // top-k per token, one warp per token; lane l owns experts l, l+32, ...
+  for (int t = warp; t < ntok; t += ROUTE_WARPS) {
+    const float* ch = s_choice + t * p.E;
+    float wsel[32];
+    int isel[32];
+    unsigned taken = 0u;
+    for (int j = 0; j < p.k; ++j) {
+      float bb = 0.0f;
+      int be = -1;
+      int i = 0;
+      for (int e = lane; e < p.E; e += 32, ++i) {
+        if ((taken >> i) & 1u) continue;
+        float v = ch[e];
+        if (v != v) v = -__int_as_float(0x7f800000);
+        if (be < 0 || v > bb) { bb = v; be = e; }
+      }
+#pragma unroll
+      for (int m = 16; m > 0; m >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, bb, m);
+        const int oe = __shfl_xor_sync(0xffffffffu, be, m);
+        const bool take = (be < 0) || (oe >= 0 && (ob > bb || (ob == bb && oe < be)));
+        if (take) { bb = ob; be = oe; }
+      }
+      if (be >= 0 && (be & 31) == lane) taken |= 1u << (be >> 5);
+      isel[j] = be;
+      wsel[j] = (be >= 0) ? s_score[t * p.E + be] : 0.0f;
+    }
+    if (lane == 0) {
+      const bool norm = p.renorm && p.k > 1;
+      float denom = 1.0f;
+      if (norm) {
+        float sum = wsel[0];
+        for (int j = 1; j < p.k; ++j) sum = __fadd_rn(sum, wsel[j]);
+        denom = __fadd_rn(sum, 1e-20f);
+      }
+      for (int j = 0; j < p.k; ++j) {
+        float wj = wsel[j];
+        if (norm) wj = __fdiv_rn(wj, denom);
+        wj = __fmul_rn(wj, p.scale);
+        p.topk_ids[(long long)(t0 + t) * p.k + j] = isel[j];
+        p.topk_weight[(long long)(t0 + t) * p.k + j] = wj;
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// ------------------------------------------------------------------ align
+// Stable counting sort of the T*k slots (slot = t*k + j) by expert, in one CTA:
+// per-warp histograms over contiguous slot ranges, a scan over (warp, expert),
+// then each warp re-walks its range in order and ranks equal experts inside
+// each 32-slot step with __match_any_sync.  The permutation equals
+// torch.argsort(ids.flatten(), stable=True) (kernels/moe_dispatch_fused.py:121).
+struct AlignArgs {
+  const long long* ids;   // [S]
+  int* counts;            // [E]
+  int* offsets;           // [E+1]
+  int* sorted_slots;      // [S]  row -> slot
+  int* slot_to_row;       // [S]  slot -> row, -1 for an invalid id
+  int* slots_padded;      // reference layout [num_tiles*block_m] or nullptr
+  int* tile_expert;       // reference layout [num_tiles] or nullptr
+  int* err;
+  int S, E, block_m, num_tiles;
+};
+
+constexpr int ALIGN_THREADS = 1024;
+
+__global__ void __launch_bounds__(ALIGN_THREADS, 1) align_kernel(const AlignArgs p) {
+  extern __shared__ int ash[];
+  int* hist = ash;                       // [32][E]
+  int* s_off = ash + 32 * p.E;           // [E+1]
+  int* s_pad = s_off + p.E + 1;          // [E+1] padded ends (reference layout)
+  __shared__ int s_wsum[32];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int E = p.E, S = p.S;
+  const int L = (S + 31) / 32;
+  const int lo = warp * L, hi = min(S, lo + L);
+
+  for (int i = tid; i < 32 * E; i += ALIGN_THREADS) hist[i] = 0;
+  __syncthreads();
+  for (int s = lo + lane; s < hi; s += 32) {
+    const long long e = p.ids[s];
+    if (e >= 0 && e < E) atomicAdd(&hist[warp * E + (int)e], 1);
+  }
+  __syncthreads();
+  // per expert: exclusive scan over warps; counts
+  for (int e = tid; e < E; e += ALIGN_THREADS) {
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int v = hist[w * E + e];
+      hist[w * E + e] = run;
+      run += v;
+    }
+    s_off[e + 1] = run;
+    p.counts[e] = run;
+  }
+  __syncthreads();
+  // exclusive scan of counts over experts (E <= 1024 = one element per thread)
+  {
+    int v = (tid < E) ? s_off[tid + 1] : 0;
+    int x = v;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) s_wsum[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      int w = s_wsum[lane];
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      s_wsum[lane] = w;  // inclusive
+    }
+    __syncthreads();
+    const int incl = x + (warp > 0 ? s_wsum[warp - 1] : 0);
+    __syncthreads();
+    if (tid < E) s_off[tid + 1] = incl;
+    if (tid == 0) s_off[0] = 0;
+    __syncthreads();
+  }
+  for (int e = tid; e <= E; e += ALIGN_THREADS) p.offsets[e] = s_off[e];
+  for (int i = tid; i < 32 * E; i += ALIGN_THREADS) hist[i] += s_off[i % E];
+  __syncthreads();
+  // stable scatter
+  const unsigned lt = (1u << lane) - 1u;
+  for (int base = lo; base < hi; base += 32) {
+    const int s = base + lane;
+    int e = -2;
+    bool valid = false;
+    if (s < hi) {
+      const long long ev = p.ids[s];
+      if (ev >= 0 && ev < E) { e = (int)ev; valid = true; }
+      else { e = -1; }
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    int row = -1;
+    if (valid) row = hist[warp * E + e] + __popc(peers & lt);
+    __syncwarp();
+    if (valid && lane == __ffs(peers) - 1) hist[warp * E + e] += __popc(peers);
+    __syncwarp();
+    if (s < hi) {
+      p.slot_to_row[s] = row;
+      if (valid) p.sorted_slots[row] = s;
+      else atomicOr(p.err, SIMSD_DEV_ERR_BAD_INDEX);
+    }
+  }
+  if (p.slots_padded == nullptr) return;
+  __syncthreads();
+  // reference layout: groups padded to block_m rows, -1 = padding
+  const int bm = p.block_m;
+  if (tid == 0) {
+    int run = 0;
+    for (int e = 0; e < E; ++e) {
+      const int c = s_off[e + 1] - s_off[e];
+      run += ((c + bm - 1) / bm) * bm;
+      s_pad[e + 1] = run;
+    }
+    s_pad[0] = 0;
+  }
+  const long long npad = (long long)p.num_tiles * bm;
+  for (long long i = tid; i < npad; i += ALIGN_THREADS) p.slots_padded[i] = -1;
+  __syncthreads();
+  for (int row = tid; row < s_off[E]; row += ALIGN_THREADS) {
+    // expert of this sorted row: largest e with s_off[e] <= row
+    int a = 0, b = E - 1;
+    while (a < b) {
+      const int mid = (a + b + 1) >> 1;
+      if (s_off[mid] <= row) a = mid; else b = mid - 1;
+    }
+    const long long dst = (long long)s_pad[a] + (row - s_off[a]);
+    if (dst < npad) p.slots_padded[dst] = p.sorted_slots[row];
+    else atomicOr(p.err, SIMSD_DEV_ERR_BAD_INDEX);
+  }
+  for (int t = tid; t < p.num_tiles; t += ALIGN_THREADS) {
+    const long long v = (long long)t * bm;
+    // number of padded group ends <= v  (torch.searchsorted(..., right=True))
+    int a = 0, b = E;
+    while (a < b) {
+      const int mid = (a + b) >> 1;
+      if (s_pad[mid + 1] <= v) a = mid + 1; else b = mid;
+    }
+    p.tile_expert[t] = a;
+  }
+}
+
+// ------------------------------------------------------------------ gather
+// xs[row, :] = x[sorted_slots[row] / k, :]
+__global__ void gather_rows_kernel(const void* x, long long ldx, const int* sorted_slots, void* xs, long long ldxs,
+                                   int S, int k, int H, int esz) {
+  const int row = blockIdx.x;
+  if (row >= S) return;
+  const int slot = sorted_slots[row];
+  const int tok = slot / k;
+  const char* src = reinterpret_cast<const char*>(x) + (long long)tok * ldx * esz;
+  char* dst = reinterpret_cast<char*>(xs) + (long long)row * ldxs * esz;
+  const long long nbytes = (long long)H * esz;
+  if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0 && (nbytes & 15) == 0) {
+    for (long long i = threadIdx.x; i < nbytes / 16; i += blockDim.x)
+      reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+  } else {
+    for (long long i = threadIdx.x; i < nbytes; i += blockDim.x) dst[i] = src[i];
+  }
+}
+
+// ------------------------------------------------------------------ combine
+// out[t, h] = cast( sum_j  fp32(ys[row(t,j), h]) * w[t, j] )  (j in order, each
+// product rounded to fp32 before the add, as `.mul_(w).sum(dim=1)` does:
+// kernels/moe_dispatch_fused.py:189-192); with `add` (the shared expert's
+// output) the result is cast(fp32(cast(sum)) + fp32(add[t, h])), i.e. the
+// x.dtype addition `moe_out + shared_out`.
+__global__ void combine_kernel(const void* ys, long long ldys, const int* slot_to_row, const float* w, void* out,
+                               long long ld_out, const void* add, long long ld_add, int T, int k, int H, int dtype) {
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  for (int h = threadIdx.x; h < H; h += blockDim.x) {
+    float acc = 0.0f;
+    for (int j = 0; j < k; ++j) {
+      const int row = slot_to_row[(long long)t * k + j];
+      if (row < 0) continue;
+      const float y = load_f(ys, (long long)row * ldys + h, dtype);
+      acc = __fadd_rn(acc, __fmul_rn(y, w[(long long)t * k + j]));
+    }
+    if (add) {
+      float r = acc;
+      if (dtype == 0) r = __bfloat162float(__float2bfloat16_rn(acc));
+      else if (dtype == 1) r = __half2float(__float2half_rn(acc));
+      acc = __fadd_rn(r, load_f(add, (long long)t * ld_add + h, dtype));
+    }
+    store_f(out, (long long)t * ld_out + h, acc, dtype);
+  }
+}
+
+}  // namespace simsd

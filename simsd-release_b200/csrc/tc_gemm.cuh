@@ -1,0 +1,466 @@
+// Weight-streaming tcgen05 GEMM for thin activations (the B200 path of
+// `_thin_gemv_kernel` in kernels/thin_linear_fused.py:67-136 and of
+// `_grouped_gemm_kernel` in kernels/moe_dispatch_fused.py:32-90).
+//
+//   out[row, col] = sum_k  B[row, k] * A[col, k]          (y = x W^T, nn.Linear layout)
+//
+// The weight A is the large operand and the activation B has 1..256 rows, so
+// the roles are swapped relative to a square GEMM: 128 weight rows fill the
+// MMA's M dimension and the activation rows are the MMA's N dimension
+// (16..BMAX, a runtime field of the instruction descriptor).  Weight tiles
+// (128 rows x 64 K, 16 KiB, 128-byte swizzle) and activation tiles (16-row
+// boxes) are staged by TMA into a STAGES-deep shared-memory ring, one elected
+// thread issues tcgen05.mma into a double-buffered TMEM accumulator, and four
+// epilogue warps read TMEM back with tcgen05.ld.
+//
+// Work split (stream-K): the iteration space (tile, k-block) is cut into
+// gridDim.x contiguous, equal ranges, one per CTA, so every SM streams the same
+// number of weight bytes whatever the shape.  A tile whose K range is spread
+// over several CTAs is reduced deterministically: each CTA writes its fp32
+// partial into a fixed slot, bumps the tile's counter, and whichever CTA comes
+// last sums all slots in K order (never in arrival order) and runs the
+// epilogue.  No CTA ever waits on another, and the sum order depends only on
+// the shape and grid size, so results are bit-identical across calls and
+// graph replays (the property tested at kernels/thin_linear_fused_test.py:130-151).
+//
+// Grouped mode: B rows are grouped (MoE experts, rows sorted by expert);
+// group g owns rows [offset_g, offset_g + count_g) of B and of the output, and
+// A is a 3-D tensor [groups, rows, K].  Tiles never straddle groups.
+//
+// SiLU-mul mode: A rows 0-63 of a tile come from the gate weight and rows
+// 64-127 from the up weight (same output columns), so the epilogue writes
+// silu(x Wg^T) * (x Wu^T) without a DRAM round trip for the two halves.
+#pragma once
+#include "sm100.cuh"
+
+namespace simsd {
+
+constexpr int TC_THREADS = 192;            // warps 0-3 epilogue, 4 TMA, 5 MMA
+constexpr int TC_A_BYTES = 128 * 128;      // 128 weight rows x 64 bf16
+constexpr int TC_BOX_ROWS = 16;            // activation rows per TMA box
+constexpr int TC_BOX_BYTES = TC_BOX_ROWS * 128;
+constexpr int TC_MAX_GROUPS = 1024;
+constexpr int TC_MAX_GRID = 1024;          // CTAs per launch (segments per tile <= this)
+constexpr int WS_COUNTER_BYTES = 256 * 1024;          // head of every workspace
+constexpr int WS_ERR_OFFSET = WS_COUNTER_BYTES - 64;  // device error word
+constexpr int WS_MAX_COUNTERS = (WS_COUNTER_BYTES - 256) / 4;
+
+struct alignas(64) TcGemmArgs {
+  CUtensorMap tmA0;          // weights (gate weights in SiLU-mul mode)
+  CUtensorMap tmA1;          // up weights (SiLU-mul mode only)
+  CUtensorMap tmB;           // activations: 2-D {K, rows}
+  void* out;                 // output, row stride ld_out elements
+  const void* bias;          // [rows_out] or nullptr (single mode only)
+  float* partials;           // [2 * gridDim.x][BMAX][128]
+  int* tile_counters;        // [max_tiles], zero on entry and on exit
+  int* err;                  // device error word
+  const int* group_counts;   // grouped mode: rows per group; nullptr = single mode
+  long long ld_out;
+  int num_groups;
+  int single_rows;           // single mode: rows of B (M)
+  int kb;                    // number of 64-wide K blocks
+  int rows_out;              // valid output columns (N, or I in SiLU-mul mode)
+  int row_tiles;             // output-column tiles per group
+  int silu;
+  int three_d;
+  int is_bf16;
+  int max_tiles;
+};
+
+template <int BMAX>
+struct TcConfig {
+  static constexpr int B_BYTES = BMAX * 128;
+  static constexpr int STAGE_BYTES = TC_A_BYTES + B_BYTES;
+  static constexpr int STAGES_RAW = (196 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 10 ? 10 : STAGES_RAW;
+  static constexpr int TMEM_COLS = (2 * BMAX) < 32 ? 32 : 2 * BMAX;
+  // tail: barriers (2*STAGES + 5) x 8, misc ints 16, prefixes 2 x (MAX_GROUPS+1), xbuf 64x16 fp32
+  static constexpr int TAIL_BYTES =
+      (2 * STAGES + 5) * 8 + 64 + 2 * (TC_MAX_GROUPS + 1) * 4 + 16 + 64 * 16 * 4 + TC_MAX_GRID * 4;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + TAIL_BYTES;
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+};
+
+struct TileInfo {
+  int group, rtile, row0, nrows;
+};
+
+// Tile j -> (group, output-column tile, first B row, B rows).  Tiles are
+// ordered (group, row chunk, column tile) so a CTA's consecutive tiles reuse
+// the same activation rows.
+template <int BMAX>
+__device__ __forceinline__ TileInfo decode_tile(long long j, const TcGemmArgs& p,
+                                                const int* row_prefix, const int* chunk_prefix) {
+  TileInfo ti;
+  const int chunk = (int)(j / p.row_tiles);
+  ti.rtile = (int)(j - (long long)chunk * p.row_tiles);
+  if (p.group_counts == nullptr) {
+    ti.group = 0;
+    ti.row0 = chunk * BMAX;
+    ti.nrows = min(BMAX, p.single_rows - ti.row0);
+  } else {
+    // largest g with chunk_prefix[g] <= chunk (groups with zero chunks are skipped)
+    int lo = 0, hi = p.num_groups - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (chunk_prefix[mid] <= chunk) lo = mid; else hi = mid - 1;
+    }
+    ti.group = lo;
+    const int lc = chunk - chunk_prefix[lo];
+    ti.row0 = row_prefix[lo] + lc * BMAX;
+    ti.nrows = min(BMAX, row_prefix[lo + 1] - ti.row0);
+  }
+  return ti;
+}
+
+__device__ __forceinline__ long long sk_start(long long c, long long iters, long long G) {
+  return (c * iters) / G;
+}
+// CTA whose range holds iteration i.
+__device__ __forceinline__ long long sk_owner(long long i, long long iters, long long G) {
+  return ((i + 1) * G + iters - 1) / iters - 1;
+}
+
+template <int BMAX>
+__global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcGemmArgs p) {
+  using Cfg = TcConfig<BMAX>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * TC_A_BYTES;
+  uint8_t* tail = sB + STAGES * Cfg::B_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(tail);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* accf_bar = empty_bar + STAGES;  // [2]
+  uint64_t* acce_bar = accf_bar + 2;        // [2]
+  uint64_t* drain_bar = acce_bar + 2;       // [1]
+  int* misc = reinterpret_cast<int*>(drain_bar + 1);  // 16 ints
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc);
+  volatile int* abort_flag = misc + 1;
+  volatile int* sh_last = misc + 2;
+  int* sh_total_chunks = misc + 3;
+  int* row_prefix = misc + 16;                       // [num_groups + 1]
+  int* chunk_prefix = row_prefix + (TC_MAX_GROUPS + 1);
+  float* xbuf = reinterpret_cast<float*>(chunk_prefix + (TC_MAX_GROUPS + 1) + 4);  // [16][64]
+  int* seg_slot = reinterpret_cast<int*>(xbuf + 16 * 64);                          // [TC_MAX_GRID]
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+
+  // ---- set-up: barriers, TMEM, group tables
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&accf_bar[a]), 1);
+      mbar_init(smem_u32(&acce_bar[a]), 128);
+    }
+    mbar_init(smem_u32(drain_bar), 1);
+    *abort_flag = 0;
+    *sh_last = 0;
+    fence_mbar_init();
+  }
+  if (warp == 4 && lane == 0) {
+    prefetch_tmap(&p.tmA0);
+    if (p.silu) prefetch_tmap(&p.tmA1);
+    prefetch_tmap(&p.tmB);
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  long long total_tiles;
+  if (p.group_counts != nullptr) {
+    const int G = p.num_groups;
+    for (int g = tid; g < G; g += TC_THREADS) row_prefix[g + 1] = p.group_counts[g];
+    __syncthreads();
+    if (warp == 0) {
+      // inclusive scans of counts and of chunk counts, 32 groups at a time
+      int run_rows = 0, run_chunks = 0;
+      for (int base = 0; base < G; base += 32) {
+        const int g = base + lane;
+        int c = (g < G) ? row_prefix[g + 1] : 0;
+        int ch = (c + BMAX - 1) / BMAX;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int c2 = __shfl_up_sync(0xffffffffu, c, o);
+          const int h2 = __shfl_up_sync(0xffffffffu, ch, o);
+          if (lane >= o) { c += c2; ch += h2; }
+        }
+        if (g < G) {
+          row_prefix[g + 1] = run_rows + c;
+          chunk_prefix[g + 1] = run_chunks + ch;
+        }
+        run_rows += __shfl_sync(0xffffffffu, c, 31);
+        run_chunks += __shfl_sync(0xffffffffu, ch, 31);
+      }
+      if (lane == 0) {
+        row_prefix[0] = 0;
+        chunk_prefix[0] = 0;
+        *sh_total_chunks = run_chunks;
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+    total_tiles = (long long)(*sh_total_chunks) * p.row_tiles;
+  } else {
+    tc_fence_before();
+    __syncthreads();
+    total_tiles = (long long)((p.single_rows + BMAX - 1) / BMAX) * p.row_tiles;
+  }
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  // Partition over G = min(gridDim.x, iters) CTAs so that every partition is
+  // non-empty (the tile count is data-dependent in grouped mode); CTAs beyond
+  // G have no work.
+  const long long kb = p.kb;
+  const long long iters = total_tiles * kb;
+  const long long G = min((long long)gridDim.x, iters);
+  const long long c = blockIdx.x;
+  const long long it_begin = (c < G) ? sk_start(c, iters, G) : 0;
+  const long long it_end = (c < G) ? sk_start(c + 1, iters, G) : 0;
+
+  if (warp == 4) {
+    // ================= TMA producer
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_x = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0;        // stages that have ever been armed
+      uint32_t last_parity = 0;        // parity of each stage's last arming
+      bool ok = true;
+      for (long long it = it_begin; ok && it < it_end;) {
+        const long long tile = it / kb;
+        const int kb0 = (int)(it - tile * kb);
+        const int kb1 = (int)min(kb, it_end - tile * kb);
+        const TileInfo ti = decode_tile<BMAX>(tile, p, row_prefix, chunk_prefix);
+        const int nb = (ti.nrows + TC_BOX_ROWS - 1) / TC_BOX_ROWS;
+        for (int k = kb0; k < kb1; ++k) {
+          if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, abort_flag, p.err)) { ok = false; break; }
+          const uint32_t fb = smem_u32(&full_bar[stage]);
+          mbar_arrive_expect_tx(fb, TC_A_BYTES + nb * TC_BOX_BYTES);
+          issued_mask |= 1u << stage;
+          last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+          const uint32_t a_dst = smem_u32(sA + stage * TC_A_BYTES);
+          const int k0 = k * 64;
+          if (p.silu) {
+            const int r0 = ti.rtile * 64;
+            if (p.three_d) {
+              tma_load_3d(a_dst, &p.tmA0, fb, k0, r0, ti.group, pol_w);
+              tma_load_3d(a_dst + 8192, &p.tmA1, fb, k0, r0, ti.group, pol_w);
+            } else {
+              tma_load_2d(a_dst, &p.tmA0, fb, k0, r0, pol_w);
+              tma_load_2d(a_dst + 8192, &p.tmA1, fb, k0, r0, pol_w);
+            }
+          } else {
+            const int r0 = ti.rtile * 128;
+            if (p.three_d) tma_load_3d(a_dst, &p.tmA0, fb, k0, r0, ti.group, pol_w);
+            else tma_load_2d(a_dst, &p.tmA0, fb, k0, r0, pol_w);
+          }
+          const uint32_t b_dst = smem_u32(sB + stage * Cfg::B_BYTES);
+          for (int b = 0; b < nb; ++b)
+            tma_load_2d(b_dst + b * TC_BOX_BYTES, &p.tmB, fb, k0, ti.row0 + b * TC_BOX_ROWS, pol_x);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        it = tile * kb + kb1;
+      }
+      if (!ok) {
+        // aborting: make sure no TMA copy is still landing in shared memory
+        for (int s = 0; s < STAGES; ++s)
+          if (issued_mask & (1u << s))
+            mbar_wait_drain(smem_u32(&full_bar[s]), (last_parity >> s) & 1u, 100000000ull);
+      }
+    }
+  } else if (warp == 5) {
+    // ================= MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc_iter = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (long long it = it_begin; ok && it < it_end;) {
+        const long long tile = it / kb;
+        const int kb0 = (int)(it - tile * kb);
+        const int kb1 = (int)min(kb, it_end - tile * kb);
+        const TileInfo ti = decode_tile<BMAX>(tile, p, row_prefix, chunk_prefix);
+        const int nb = (ti.nrows + TC_BOX_ROWS - 1) / TC_BOX_ROWS;
+        const uint32_t idesc = make_idesc_f16(p.is_bf16, 128, nb * TC_BOX_ROWS);
+        const int a = acc_iter & 1;
+        const uint32_t aphase = (acc_iter >> 1) & 1;
+        if (!mbar_wait(smem_u32(&acce_bar[a]), aphase ^ 1, abort_flag, p.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + a * BMAX;
+        for (int k = kb0; k < kb1; ++k) {
+          if (!mbar_wait(smem_u32(&full_bar[stage]), phase, abort_flag, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t adesc = make_sw128_desc(smem_u32(sA + stage * TC_A_BYTES));
+          const uint64_t bdesc = make_sw128_desc(smem_u32(sB + stage * Cfg::B_BYTES));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma_f16(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (k > kb0 || kk > 0) ? 1u : 0u);
+          issued_any = true;
+          tc_commit(smem_u32(&empty_bar[stage]));
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(smem_u32(&accf_bar[a]));
+        ++acc_iter;
+        it = tile * kb + kb1;
+      }
+      if (!ok && issued_any) {
+        // aborting: wait for the MMAs already issued before TMEM is released
+        tc_commit(smem_u32(drain_bar));
+        mbar_wait_drain(smem_u32(drain_bar), 0, 100000000ull);
+      }
+    }
+  } else {
+    // ================= epilogue warps 0-3: TMEM lanes 32*warp .. 32*warp+31
+    const int row = tid;  // 0..127 == TMEM lane == tile row
+    int acc_iter = 0;
+    for (long long it = it_begin; it < it_end;) {
+      const long long tile = it / kb;
+      const int kb0 = (int)(it - tile * kb);
+      const int kb1 = (int)min(kb, it_end - tile * kb);
+      const TileInfo ti = decode_tile<BMAX>(tile, p, row_prefix, chunk_prefix);
+      const int nb = (ti.nrows + TC_BOX_ROWS - 1) / TC_BOX_ROWS;
+      const int a = acc_iter & 1;
+      const uint32_t aphase = (acc_iter >> 1) & 1;
+      // One decision for all 128 epilogue threads (they share named barriers
+      // below, and tcgen05.ld is .sync.aligned): leave together if any gave up.
+      const bool got = named_bar_and(1, 128, mbar_wait(smem_u32(&accf_bar[a]), aphase, abort_flag, p.err));
+      if (!got) break;
+      tc_fence_after();
+      const uint32_t t_base = tmem_base + ((uint32_t)(warp * 32) << 16) + a * BMAX;
+      const bool whole = (kb0 == 0 && kb1 == kb);
+      const int out_col0 = p.silu ? ti.rtile * 64 : ti.rtile * 128;
+      char* outp = reinterpret_cast<char*>(p.out);
+
+      if (whole) {
+        for (int ch = 0; ch < nb; ++ch) {
+          float v[16];
+          tmem_ld16(t_base + ch * 16, v);
+          tmem_wait_ld();
+          if (ch == nb - 1) {
+            tc_fence_before();
+            mbar_arrive(smem_u32(&acce_bar[a]));
+          }
+          if (!p.silu) {
+            const int col = out_col0 + row;
+            if (col < p.rows_out) {
+              const float bv = p.bias ? load_f(p.bias, col, p.is_bf16 ? 0 : 1) : 0.0f;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const int t = ch * 16 + j;
+                if (t < ti.nrows)
+                  store_f(outp, (long long)(ti.row0 + t) * p.ld_out + col, __fadd_rn(v[j], bv), p.is_bf16 ? 0 : 1);
+              }
+            }
+          } else {
+            if (row >= 64) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) xbuf[j * 64 + (row - 64)] = v[j];
+            }
+            named_bar_sync(1, 128);
+            if (row < 64) {
+              const int col = out_col0 + row;
+              if (col < p.rows_out) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const int t = ch * 16 + j;
+                  if (t < ti.nrows)
+                    store_f(outp, (long long)(ti.row0 + t) * p.ld_out + col, silu_mul(v[j], xbuf[j * 64 + row]),
+                            p.is_bf16 ? 0 : 1);
+                }
+              }
+            }
+            named_bar_sync(1, 128);
+          }
+        }
+      } else {
+        // partial K range of this tile: park the fp32 partial in this CTA's slot
+        const long long first_tile_of_cta = it_begin / kb;
+        const long long slot = 2 * c + (tile == first_tile_of_cta ? 0 : 1);
+        float* P = p.partials + slot * (long long)(BMAX * 128);
+        for (int ch = 0; ch < nb; ++ch) {
+          float v[16];
+          tmem_ld16(t_base + ch * 16, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) __stcg(&P[(ch * 16 + j) * 128 + row], v[j]);
+        }
+        tc_fence_before();
+        mbar_arrive(smem_u32(&acce_bar[a]));
+        __threadfence();
+        named_bar_sync(1, 128);
+        const long long c_first = sk_owner(tile * kb, iters, G);
+        const long long c_last = sk_owner(tile * kb + kb - 1, iters, G);
+        if (row == 0) {
+          int last = 0;
+          if (tile < p.max_tiles) {
+            const int old = atomicAdd(&p.tile_counters[tile], 1);
+            last = (old == (int)(c_last - c_first));
+          } else {
+            atomicOr(p.err, SIMSD_DEV_ERR_BAD_INDEX);
+          }
+          *sh_last = last;
+        }
+        named_bar_sync(1, 128);
+        const int nseg = (int)(c_last - c_first + 1);
+        if (*sh_last) {
+          __threadfence();
+          // slot of every contributing CTA, in K order
+          for (int i = row; i < nseg; i += 128) {
+            const long long cc = c_first + i;
+            seg_slot[i] = (int)(2 * cc + ((tile == sk_start(cc, iters, G) / kb) ? 0 : 1));
+          }
+          named_bar_sync(1, 128);
+          if (!p.silu) {
+            const int col = out_col0 + row;
+            if (col < p.rows_out) {
+              const float bv = p.bias ? load_f(p.bias, col, p.is_bf16 ? 0 : 1) : 0.0f;
+              for (int t = 0; t < ti.nrows; ++t) {
+                float s = 0.0f;
+                for (int i = 0; i < nseg; ++i)
+                  s = __fadd_rn(s, __ldcg(&p.partials[(long long)seg_slot[i] * (BMAX * 128) + t * 128 + row]));
+                store_f(outp, (long long)(ti.row0 + t) * p.ld_out + col, __fadd_rn(s, bv), p.is_bf16 ? 0 : 1);
+              }
+            }
+          } else {
+            const int i = row & 63;
+            const int col = out_col0 + i;
+            if (col < p.rows_out) {
+              for (int t = row >> 6; t < ti.nrows; t += 2) {
+                float g = 0.0f, u = 0.0f;
+                for (int q = 0; q < nseg; ++q) {
+                  const float* Q = p.partials + (long long)seg_slot[q] * (BMAX * 128) + t * 128;
+                  g = __fadd_rn(g, __ldcg(&Q[i]));
+                  u = __fadd_rn(u, __ldcg(&Q[64 + i]));
+                }
+                store_f(outp, (long long)(ti.row0 + t) * p.ld_out + col, silu_mul(g, u), p.is_bf16 ? 0 : 1);
+              }
+            }
+          }
+          if (row == 0) p.tile_counters[tile] = 0;
+        }
+        named_bar_sync(1, 128);
+      }
+      ++acc_iter;
+      it = tile * kb + kb1;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace simsd

@@ -1,0 +1,206 @@
+"""Opt-in switch that routes a model's linears and MoE blocks through libsimsd_b200.
+
+Same entry points and behaviour as the reference's kernels/fused_toggle.py:
+  apply_to_model(model, enable=True, targets=DEFAULT_TARGETS, config=None) -> int   (:52-79)
+  is_applied(model)                                                             (:82)
+  fused_linear(model, enable=True, **kw)   context manager                     (:86-104)
+  warmup(model, block_length=4, extra_M=())                                    (:107-133)
+  apply_moe_to_model(model, enable=True) -> int                                (:151-198)
+  is_moe_applied(model)                                                         (:201)
+
+Leaf `nn.Linear`s whose name is in `targets` become `ThinLinear` modules that
+alias the original parameters (no copy; `state_dict()` unchanged).  It is
+idempotent, returns the number of modules swapped or restored, and must run
+before CUDA-graph capture, which freezes whatever forward is installed.
+
+One addition: `apply_to_model(..., fuse_gate_up=True)` also patches SwiGLU MLP
+modules (attributes gate_proj / up_proj / down_proj and a SiLU `act_fn`, as
+`SDARMLP` in sdar/modeling_sdar.py:99-119) so gate and up run as one kernel
+reading both weights once, with the SiLU*mul applied before the single rounding.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from ._lib import reset_workspace
+from .thin_linear_fused import ThinLinear, should_fuse, thin_linear_silu_mul
+
+DEFAULT_TARGETS = (
+    "q_proj", "k_proj", "v_proj", "o_proj",
+    "gate_proj", "up_proj", "down_proj",
+)
+ALL_TARGETS = DEFAULT_TARGETS + ("lm_head",)
+
+_ORIGINALS: dict[int, dict[str, nn.Module]] = {}
+_MLP_PATCHED: dict[int, list[nn.Module]] = {}
+
+
+def _iter_targets(model: nn.Module, targets):
+    for name, mod in model.named_modules():
+        leaf = name.rsplit(".", 1)[-1]
+        if leaf in targets and isinstance(mod, nn.Linear):
+            yield name, mod
+
+
+def _set_submodule(model: nn.Module, qualified: str, new: nn.Module) -> None:
+    parent_path, _, leaf = qualified.rpartition(".")
+    parent = model.get_submodule(parent_path) if parent_path else model
+    setattr(parent, leaf, new)
+
+
+def _is_silu(act) -> bool:
+    return isinstance(act, nn.SiLU) or getattr(act, "__name__", "") == "silu" or \
+        act is torch.nn.functional.silu
+
+
+def _gate_up_forward(self, x):
+    gate, up = self.gate_proj, self.up_proj
+    M = x.numel() // x.shape[-1] if x.shape[-1] else 0
+    if (getattr(gate, "bias", None) is None and getattr(up, "bias", None) is None
+            and should_fuse(M, gate.out_features, gate.in_features)
+            and gate.weight.stride() == up.weight.stride()):
+        return self.down_proj(thin_linear_silu_mul(x, gate.weight, up.weight))
+    return self.down_proj(self.act_fn(gate(x)) * up(x))
+
+
+def _patch_mlps(model: nn.Module) -> list[nn.Module]:
+    patched = []
+    for mod in model.modules():
+        if all(hasattr(mod, a) for a in ("gate_proj", "up_proj", "down_proj", "act_fn")) \
+                and _is_silu(mod.act_fn) and "forward" not in mod.__dict__:
+            mod.forward = _gate_up_forward.__get__(mod)
+            patched.append(mod)
+    return patched
+
+
+def apply_to_model(model: nn.Module, enable: bool = True,
+                   targets=DEFAULT_TARGETS,
+                   config: tuple[int, int, int, int] | None = None,
+                   fuse_gate_up: bool = False) -> int:
+    """Swap the target `nn.Linear` modules for `ThinLinear` (or restore them).
+
+    Idempotent in both directions.  Returns the number of modules swapped (or
+    restored).  `ThinLinear` aliases the original parameters.
+    """
+    key = id(model)
+    if not enable:
+        saved = _ORIGINALS.pop(key, None)
+        for mod in _MLP_PATCHED.pop(key, []):
+            mod.__dict__.pop("forward", None)
+        if not saved:
+            return 0
+        for path, orig in saved.items():
+            _set_submodule(model, path, orig)
+        reset_workspace()
+        return len(saved)
+
+    if key in _ORIGINALS:
+        return 0
+    saved: dict[str, nn.Module] = {}
+    for path, mod in list(_iter_targets(model, targets)):
+        saved[path] = mod
+        _set_submodule(model, path, ThinLinear(mod, config=config))
+    if saved:
+        _ORIGINALS[key] = saved
+        if fuse_gate_up:
+            _MLP_PATCHED[key] = _patch_mlps(model)
+    return len(saved)
+
+
+def is_applied(model: nn.Module) -> bool:
+    return id(model) in _ORIGINALS
+
+
+class fused_linear:
+    """Context manager form, for tests:  with fused_toggle.fused_linear(model): ..."""
+
+    def __init__(self, model: nn.Module, enable: bool = True, **kw):
+        self.model, self.enable, self.kw = model, enable, kw
+        self.n = 0
+
+    def __enter__(self):
+        self.n = apply_to_model(self.model, self.enable, **self.kw)
+        return self
+
+    def __exit__(self, *exc):
+        if self.enable:
+            apply_to_model(self.model, False)
+        return False
+
+
+def warmup(model: nn.Module, block_length: int = 4, extra_M=()) -> None:
+    """Run every patched module once per M the pipeline uses, before graph capture.
+
+    Nothing is JIT-compiled here (the kernels are built ahead of time), but the
+    first call per device sizes the cached workspace, sets the kernels'
+    shared-memory limits and resolves the driver's tensor-map entry point; doing
+    that outside capture keeps the captured graph free of allocations.
+    """
+    Ms = {1, block_length, 2 * block_length, 96, 97, *extra_M}
+    mods = [m for _, m in model.named_modules() if isinstance(m, ThinLinear)]
+    devs = set()
+    with torch.inference_mode():
+        for mod in mods:
+            devs.add(mod.weight.device)
+            for M in sorted(Ms):
+                mod(torch.zeros(M, mod.in_features, device=mod.weight.device, dtype=mod.weight.dtype))
+        for mlp in _MLP_PATCHED.get(id(model), []):
+            w = mlp.gate_proj.weight
+            for M in sorted(Ms):
+                mlp(torch.zeros(M, w.shape[1], device=w.device, dtype=w.dtype))
+    for d in devs:
+        torch.cuda.synchronize(d)
+
+
+# ─────────────────────────────────────────────────────────────────────
+# LLaDA2 MoE expert dispatch  (moe_dispatch_fused.py)
+# ─────────────────────────────────────────────────────────────────────
+_MOE_ATTR = "_simsd_fused_moe"
+
+
+def apply_moe_to_model(model: nn.Module, enable: bool = True) -> int:
+    """Switch LLaDA2 MoE blocks to the fused dispatch.  Idempotent.
+
+    Stacks each block's expert weights (releasing the per-expert copies) and
+    patches the block class's `moe_infer` once.  Disabling is not supported
+    (the per-expert weights are gone): it raises NotImplementedError, as the
+    reference does.  Must run before any CUDA-graph capture.
+    """
+    from .moe_dispatch_fused import moe_dispatch, stack_expert_weights
+
+    n = 0
+    for mod in model.modules():
+        if mod.__class__.__name__ != "LLaDA2MoeSparseMoeBlock":
+            continue
+        if enable:
+            if getattr(mod, _MOE_ATTR, None) is not None:
+                continue
+            setattr(mod, _MOE_ATTR, stack_expert_weights(mod.experts))
+            n += 1
+        elif getattr(mod, _MOE_ATTR, None) is not None:
+            raise NotImplementedError(
+                "apply_moe_to_model(enable=False) is not supported: stacking released "
+                "the per-expert weights; reload the checkpoint to get the stock path back.")
+    if n == 0:
+        return 0
+
+    cls = next(m.__class__ for m in model.modules()
+               if m.__class__.__name__ == "LLaDA2MoeSparseMoeBlock")
+    if not getattr(cls, "_simsd_moe_patched", False):
+        stock = cls.moe_infer
+
+        def moe_infer(self, x, topk_ids, topk_weight):
+            packed = getattr(self, _MOE_ATTR, None)
+            if packed is None:
+                return stock(self, x, topk_ids, topk_weight)
+            return moe_dispatch(x, topk_ids, topk_weight, *packed)
+
+        cls.moe_infer = moe_infer
+        cls._simsd_moe_stock = stock
+        cls._simsd_moe_patched = True
+    return n
+
+
+def is_moe_applied(model: nn.Module) -> bool:
+    return any(getattr(m, _MOE_ATTR, None) is not None for m in model.modules())

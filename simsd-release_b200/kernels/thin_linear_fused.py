@@ -1,0 +1,231 @@
+"""Thin-M linear on B200: a drop-in for `F.linear(x, w, bias)` when M is small.
+
+Mirrors the interface of the reference module kernels/thin_linear_fused.py
+(`thin_linear` :265-345, `pick_config` :217-228, `_tuned_for` :231-244,
+`should_fuse` :348-377, `ThinLinear` :380-412, `reset_workspace` :193-195,
+`make_bench_fn` :418) with the computation moved to libsimsd_b200.so:
+
+* bf16/fp16 with TMA-describable layouts run the tcgen05 kernel
+  (csrc/tc_gemm.cuh): the weight rows stream through a TMA ring into the
+  tensor cores (128 weight rows = MMA M, the activation rows = MMA N), fp32
+  accumulation in TMEM, and the K reduction is spread over every SM with a
+  deterministic fixed-order fixup (stream-K);
+* fp32 (IEEE, never TF32) and layouts TMA cannot describe (transposed views,
+  rows that are not 16-byte aligned) run the CUDA-core kernel
+  (csrc/simt_gemm.cuh).
+
+There is no CPU path: CUDA tensors only, and a missing library raises.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import reset_workspace  # noqa: F401  (reference name)
+
+# The tensor-core tile is fixed by the hardware mapping: 128 weight rows
+# (tcgen05 M) x 64 K elements (one 128-byte swizzle row) per pipeline stage;
+# the activation rows (tcgen05 N) are padded to a multiple of 16.
+TILE_N = 128
+TILE_K = 64
+
+# Dispatch guard: `ThinLinear` routes M <= FUSE_MAX_M here and larger M to
+# cuBLAS.  BASELINE's thin-M range is M = 4..64 (SDAR-8B verify runs M = 32).
+FUSE_MAX_M = 64
+
+# Kept for interface parity with the reference, where TUNED held searched
+# Triton configs keyed by (K, N).  This kernel needs no per-shape table: the
+# stream-K split balances any (K, N) over all SMs.  Entries, if a caller adds
+# them, are (BLOCK_M, BLOCK_N, BLOCK_K, SPLIT_K, num_warps, num_stages) and only
+# SPLIT_K is honoured.
+TUNED: dict[tuple[int, int], tuple[int, int, int, int, int, int]] = {}
+
+
+def _block_m(M: int) -> int:
+    for b in (16, 32, 64, 128):
+        if M <= b:
+            return b
+    return 256
+
+
+def pick_config(M: int, N: int, K: int, itemsize: int = 2) -> tuple[int, int, int, int]:
+    """(BLOCK_M, BLOCK_N, BLOCK_K, SPLIT_K) of the launch; SPLIT_K 0 = stream-K over all SMs."""
+    full = _tuned_for(M, N, K)
+    if full is not None:
+        return full[0], full[1], full[2], full[3]
+    return _heuristic_config(M, N, K)
+
+
+def _tuned_for(M: int, N: int, K: int):
+    """The TUNED entry for (K, N), only while M still fits its BLOCK_M."""
+    c = TUNED.get((K, N))
+    if c is None:
+        return None
+    return c if _block_m(max(M, 1)) == c[0] else None
+
+
+def _heuristic_config(M: int, N: int, K: int) -> tuple[int, int, int, int]:
+    return _block_m(max(M, 1)), TILE_N, TILE_K, 0
+
+
+def thin_linear(x: torch.Tensor, w: torch.Tensor,
+                bias: torch.Tensor | None = None,
+                config: tuple[int, int, int, int] | None = None,
+                num_warps: int | None = None,
+                num_stages: int | None = None) -> torch.Tensor:
+    """`F.linear(x, w, bias)` for thin x, via libsimsd_b200.
+
+    x: [..., K] (leading dims flattened, strided views allowed)
+    w: [N, K]   (nn.Linear weight layout; strided views allowed)
+    -> [..., N] in x.dtype.  `config[3]` (SPLIT_K) > 0 forces that many K
+    segments per output tile; `num_warps` / `num_stages` are accepted for
+    signature compatibility and ignored (the kernel's warp roles are fixed).
+    """
+    if torch.is_grad_enabled() and (x.requires_grad or w.requires_grad):
+        raise RuntimeError(
+            "thin_linear is a forward-only inference kernel; it has no backward. "
+            "Call it under torch.no_grad() / torch.inference_mode(), or use F.linear "
+            "for training.")
+    if x.dtype != w.dtype:
+        raise TypeError(f"dtype mismatch: x={x.dtype} w={w.dtype}")
+    if w.ndim != 2:
+        raise ValueError(f"w must be 2-D [N, K], got {tuple(w.shape)}")
+    if x.ndim < 1:
+        raise ValueError("x must have at least one dimension")
+    code = _lib.dtype_code(x.dtype)
+    N, K = w.shape
+    if x.shape[-1] != K:
+        raise ValueError(f"K mismatch: x[..., {x.shape[-1]}] vs w[{N}, {K}]")
+    if bias is not None:
+        if bias.dtype != x.dtype:
+            raise TypeError(f"dtype mismatch: x={x.dtype} bias={bias.dtype}")
+        if bias.shape != (N,):
+            raise ValueError(f"bias must be [{N}], got {tuple(bias.shape)}")
+    dev = _lib.require_cuda(x, w, bias)
+
+    out_shape = (*x.shape[:-1], N)
+    x2 = x.reshape(-1, K)
+    M = x2.shape[0]
+    y = torch.empty((M, N), device=dev, dtype=x.dtype)
+    if M == 0 or N == 0:
+        return y.view(out_shape)
+    if K == 0:
+        y.zero_()
+        if bias is not None:
+            y += bias
+        return y.view(out_shape)
+    if bias is not None and bias.stride(0) != 1:
+        bias = bias.contiguous()
+
+    split = 0
+    if config is not None:
+        split = int(config[3])
+    else:
+        tuned = _tuned_for(M, N, K)
+        if tuned is not None:
+            split = int(tuned[3])
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        nbytes = L.simsd_thin_linear_workspace_size(M, N, K, code, _lib.EPI_NONE, split)
+        ws = _lib.workspace(dev, nbytes)
+        rc = L.simsd_thin_linear(
+            x2.data_ptr(), x2.stride(0), x2.stride(1),
+            w.data_ptr(), w.stride(0), w.stride(1),
+            None, bias.data_ptr() if bias is not None else None,
+            y.data_ptr(), y.stride(0), M, N, K, code, _lib.EPI_NONE, split, _lib.PATH_AUTO,
+            ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
+    _lib.check(rc, "thin_linear")
+    return y.view(out_shape)
+
+
+def thin_linear_silu_mul(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
+                         split: int = 0) -> torch.Tensor:
+    """`F.silu(F.linear(x, w_gate)) * F.linear(x, w_up)` in one pass over both weights.
+
+    The SwiGLU front half of `SDARMLP.forward` (sdar/modeling_sdar.py:113-119)
+    with the gate and up products kept in fp32 until the single rounding of the
+    product.  w_gate and w_up: [I, K] with identical strides (they may be the two
+    halves of one fused [2I, K] gate_up weight).  -> [..., I].
+    """
+    if torch.is_grad_enabled() and (x.requires_grad or w_gate.requires_grad or w_up.requires_grad):
+        raise RuntimeError("thin_linear_silu_mul is a forward-only inference kernel.")
+    if not (x.dtype == w_gate.dtype == w_up.dtype):
+        raise TypeError(f"dtype mismatch: x={x.dtype} w_gate={w_gate.dtype} w_up={w_up.dtype}")
+    if w_gate.ndim != 2 or w_gate.shape != w_up.shape:
+        raise ValueError(f"w_gate {tuple(w_gate.shape)} and w_up {tuple(w_up.shape)} must be equal 2-D")
+    if w_gate.stride() != w_up.stride():
+        raise ValueError("w_gate and w_up must have identical strides")
+    code = _lib.dtype_code(x.dtype)
+    I, K = w_gate.shape
+    if x.shape[-1] != K:
+        raise ValueError(f"K mismatch: x[..., {x.shape[-1]}] vs w[{I}, {K}]")
+    dev = _lib.require_cuda(x, w_gate, w_up)
+    out_shape = (*x.shape[:-1], I)
+    x2 = x.reshape(-1, K)
+    M = x2.shape[0]
+    y = torch.empty((M, I), device=dev, dtype=x.dtype)
+    if M == 0 or I == 0:
+        return y.view(out_shape)
+    if K == 0:
+        return y.zero_().view(out_shape)
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        nbytes = L.simsd_thin_linear_workspace_size(M, I, K, code, _lib.EPI_SILU_MUL, split)
+        ws = _lib.workspace(dev, nbytes)
+        rc = L.simsd_thin_linear(
+            x2.data_ptr(), x2.stride(0), x2.stride(1),
+            w_gate.data_ptr(), w_gate.stride(0), w_gate.stride(1),
+            w_up.data_ptr(), None, y.data_ptr(), y.stride(0), M, I, K, code,
+            _lib.EPI_SILU_MUL, split, _lib.PATH_AUTO, ws.data_ptr(), ws.numel(),
+            _lib.stream_ptr(dev))
+    _lib.check(rc, "thin_linear_silu_mul")
+    return y.view(out_shape)
+
+
+def should_fuse(M: int, N: int, K: int) -> bool:
+    """Route this call to the thin kernel (True) or to cuBLAS `F.linear` (False).
+
+    The kernel streams the weight once per 256 activation rows and is built for
+    the decode/verify regime M <= FUSE_MAX_M; prefill-sized M goes to cuBLAS,
+    which the reference's guard also does above its searched range
+    (kernels/thin_linear_fused.py:348-377).
+    """
+    return 1 <= M <= FUSE_MAX_M
+
+
+class ThinLinear(torch.nn.Module):
+    """`nn.Linear` drop-in that routes the forward through `thin_linear`.
+
+    Holds a *reference* to the original module's parameters (no copy), so
+    swapping it in costs no memory and `state_dict()` round-trips unchanged.
+    Falls back to `F.linear` outside `should_fuse` unless `config` or
+    `always_fuse` is given.
+    """
+
+    def __init__(self, linear: torch.nn.Linear,
+                 config: tuple[int, int, int, int] | None = None,
+                 always_fuse: bool = False):
+        super().__init__()
+        self.in_features = linear.in_features
+        self.out_features = linear.out_features
+        self.weight = linear.weight
+        self.bias = linear.bias
+        self.config = config
+        self.always_fuse = always_fuse
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        M = x.numel() // x.shape[-1] if x.shape[-1] else 0
+        if (self.config is not None or self.always_fuse
+                or should_fuse(M, self.out_features, self.in_features)):
+            return thin_linear(x, self.weight, self.bias, config=self.config)
+        return torch.nn.functional.linear(x, self.weight, self.bias)
+
+    def extra_repr(self) -> str:
+        return (f"in_features={self.in_features}, out_features={self.out_features}, "
+                f"bias={self.bias is not None}, fused=tcgen05 thin GEMM "
+                f"(M<={FUSE_MAX_M} unless always_fuse)")
+
+
+def make_bench_fn(x, pool, sh):
+    """Bench hook with the reference's signature: call i reads weight pool[i]."""
+    return lambda i: thin_linear(x, pool[i])
