@@ -1,0 +1,479 @@
+#!/usr/bin/env python3
+"""Benchmark of the SimSD matmul hot path on B200 (one JSON line on rank 0).
+
+Headline workload: the SDAR-8B thin-M linear sweep,
+bf16, M in {4, 8, 16, 32, 64}:
+    QKV      K=4096  N=6144
+    O        K=4096  N=4096
+    gate_up  K=4096  N=2x12288, SiLU(gate)*up epilogue -> [M, 12288]
+    down     K=12288 N=4096
+One step = those 4 linears at all 5 M (20 kernel launches), replayed from a
+CUDA graph, cycling two distinct copies of the weights (2 x 386 MB, each
+launch reads weights untouched for ~386 MB of traffic, far above the 126 MB
+L2).  `value` = algorithmic bytes 2*(N*K + M*K + M*N_out) summed over the step
+/ step time, in GB/s (weights ~N(0,0.02), activations ~N(0,1), seeded;
+synthetic, as the reference has no dataset for this path).
+
+With --gpus N (torchrun, one rank per GPU) the linears are column-parallel:
+each rank owns N/g weight rows (gate and up split alike, so the SiLU*mul stays
+local), computes its [M, N_out/g] slice, and an NCCL all-gather assembles
+[M, N_out]; `value` counts the whole layer's bytes over the max-over-ranks time
+(strong scaling).
+
+`--impl reference` times the reference's CPU path on the host cores
+(torch eager `F.linear` in bf16 plus `silu(g)*up`, the ground truth of
+kernels/workspace/thin_linear/CONTRACT.md) on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "simsd-release_b200"))
+sys.path.insert(0, str(REPO))
+
+import torch  # noqa: E402
+import torch.nn.functional as F  # noqa: E402
+
+METRIC = "thin-M linear & MoE grouped-GEMM HBM GB/s (% peak); synthetic verify tok/s"
+SHAPES = [("qkv", 4096, 6144, False), ("o", 4096, 4096, False),
+          ("gate_up", 4096, 24576, True), ("down", 12288, 4096, False)]
+MS = [4, 8, 16, 32, 64]
+POOL = 2
+
+
+def alg_bytes(M: int, K: int, N: int, silu: bool, g: int = 1) -> int:
+    """Algorithmic HBM bytes of one thin linear: weights + activations in + out."""
+    n_out = N // 2 if silu else N
+    return 2 * (N * K // g + M * K + M * n_out // g)
+
+
+def step_bytes(g: int = 1) -> int:
+    return sum(alg_bytes(M, K, N, s, g) for M in MS for _, K, N, s in SHAPES)
+
+
+def peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "src": "fallback"}
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+        return False
+
+    def summary(self) -> dict | None:
+        rows = []
+        for line in (self.out or "").splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        mx = max(r[1] for r in rows)
+        loaded = [r[0] for r in rows if r[0] > 0.5 * mx] or [r[0] for r in rows]
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ distributed
+def dist_init(n_gpus: int):
+    if n_gpus <= 1 and "RANK" not in os.environ:
+        return 0, 1, None
+    import datetime
+    import torch.distributed as dist
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", n_gpus))
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    return rank, world, dist
+
+
+# ------------------------------------------------------------------ GPU arm
+def make_weights(rank: int, world: int, dev):
+    """POOL copies of the column shard of every SDAR-8B linear this rank owns."""
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    pool = []
+    for _ in range(POOL):
+        ws = {}
+        for name, K, N, silu in SHAPES:
+            if silu:
+                I = N // 2 // world
+                ws[name] = tuple((torch.randn(I, K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+                                 for _ in range(2))
+            else:
+                ws[name] = (torch.randn(N // world, K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        pool.append(ws)
+    return pool
+
+
+def make_inputs(dev, seed=7):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    return {M: {K: torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16) for K in (4096, 12288)}
+            for M in MS}
+
+
+def run_step(ws, xs, world, dist, outs=None):
+    from kernels.thin_linear_fused import thin_linear, thin_linear_silu_mul
+    res = []
+    for M in MS:
+        for name, K, N, silu in SHAPES:
+            x = xs[M][K]
+            y = thin_linear_silu_mul(x, *ws[name]) if silu else thin_linear(x, ws[name])
+            if world > 1:
+                gathered = torch.empty((world, *y.shape), dtype=y.dtype, device=y.device)
+                dist.all_gather_into_tensor(gathered, y)
+                y = gathered.permute(1, 0, 2).reshape(M, -1)
+            res.append(y)
+    return res
+
+
+def per_launch_timing(pool, xs, reps: int = 6):
+    """Device time of every thin-linear launch, back to back behind a sleep so the
+    host never gates the GPU; returns {(name, M): mean_us} and the bytes-weighted
+    aggregate."""
+    from kernels.thin_linear_fused import thin_linear, thin_linear_silu_mul
+    stream = torch.cuda.current_stream()
+    plan = []
+    for r in range(reps):
+        for M in MS:
+            for name, K, N, silu in SHAPES:
+                plan.append((name, M, K, N, silu, pool[r % POOL]))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in plan]
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int(2e8))
+    for (name, M, K, N, silu, ws), (e0, e1) in zip(plan, evs):
+        e0.record(stream)
+        if silu:
+            thin_linear_silu_mul(xs[M][K], *ws[name])
+        else:
+            thin_linear(xs[M][K], ws[name])
+        e1.record(stream)
+    torch.cuda.synchronize()
+    acc: dict = {}
+    for (name, M, K, N, silu, _), (e0, e1) in zip(plan, evs):
+        acc.setdefault((name, M, K, N, silu), []).append(e0.elapsed_time(e1) * 1e3)
+    out = {}
+    tot_b = tot_us = 0.0
+    for (name, M, K, N, silu), v in acc.items():
+        us = statistics.mean(v[1:] if len(v) > 2 else v)
+        b = alg_bytes(M, K, N, silu)
+        out[f"{name}_M{M}"] = {"us": round(us, 2), "gbs": round(b / us / 1e3, 1)}
+        tot_b += b
+        tot_us += us
+    return out, tot_b / tot_us / 1e3, tot_us / len(acc)
+
+
+def soak(graphs, seconds: float, dist) -> None:
+    """Untimed replays for about `seconds` (same count on every rank)."""
+    t0 = time.perf_counter()
+    torch.cuda.synchronize()
+    graphs[0].replay()
+    torch.cuda.synchronize()
+    one = max(time.perf_counter() - t0, 1e-4)
+    n = torch.tensor([int(seconds / one) + 1], device=torch.device("cuda", torch.cuda.current_device()))
+    if dist:
+        dist.all_reduce(n, op=dist.ReduceOp.MIN)
+    for i in range(int(n.item())):
+        graphs[i % len(graphs)].replay()
+    torch.cuda.synchronize()
+
+
+def gpu_arm(args):
+    rank, world, dist = dist_init(args.gpus)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    from kernels import _lib
+    _lib.lib()
+    pool = make_weights(rank, world, dev)
+    xs = make_inputs(dev)
+
+    with torch.inference_mode():
+        for _ in range(max(3, args.warmup)):
+            run_step(pool[0], xs, world, dist)
+        torch.cuda.synchronize()
+        graphs = []
+        for p in range(POOL):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                run_step(pool[p], xs, world, dist)
+            graphs.append(gr)
+        for i in range(max(3, args.warmup)):
+            graphs[i % POOL].replay()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        # nvidia-smi samples every 100 ms, so the sampler runs over a loaded
+        # window (1 s of untimed replays, the timed steps, 0.3 s more) that
+        # contains the timed region.
+        with ClockSampler(dev.index) as clk:
+            soak(graphs, 1.0, dist)
+            e0.record()
+            for i in range(args.steps):
+                graphs[i % POOL].replay()
+            e1.record()
+            torch.cuda.synchronize()
+            soak(graphs, 0.3, dist)
+        if dist:
+            dist.barrier()
+        ms = e0.elapsed_time(e1) / args.steps
+        if dist:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        launches_per_step = len(MS) * len(SHAPES)
+
+        # per-launch device time of the dominant kernel (tc_gemm) at N=1
+        per, agg_gbs, avg_us = (None, None, None)
+        if world == 1:
+            per, agg_gbs, avg_us = per_launch_timing(pool, xs)
+
+        # end to end through the public API: pinned host inputs -> device -> host outputs
+        hx = {M: {K: xs[M][K].cpu().pin_memory() for K in (4096, 12288)} for M in MS}
+        houts = None
+        h2d = sum(hx[M][K].numel() * 2 for M in MS for K in (4096, 12288))
+        d2h = 0
+        for M in MS:
+            for _, K, N, silu in SHAPES:
+                d2h += M * ((N // 2) if silu else N) * 2
+        for _ in range(3):
+            dxs = {M: {K: hx[M][K].to(dev, non_blocking=True) for K in (4096, 12288)} for M in MS}
+            res = run_step(pool[0], dxs, world, dist)
+            houts = [r.to("cpu", non_blocking=True) for r in res]
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2e_steps = max(3, min(args.steps, 20))
+        e2.record()
+        for i in range(e2e_steps):
+            dxs = {M: {K: hx[M][K].to(dev, non_blocking=True) for K in (4096, 12288)} for M in MS}
+            res = run_step(pool[i % POOL], dxs, world, dist)
+            houts = [r.to("cpu", non_blocking=True) for r in res]
+        e3.record()
+        torch.cuda.synchronize()
+        e2e_ms = e2.elapsed_time(e3) / e2e_steps
+        if dist:
+            t = torch.tensor([e2e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        del houts
+        graphs.clear()
+
+    total_bytes = step_bytes(1)
+    value = total_bytes / (ms * 1e-3) / 1e9
+    pk = peaks()
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights; no dataset exists for this path)",
+        "config": {"workload": "SDAR-8B thin-M linear sweep (BASELINE configs[1])",
+                   "shapes": {n: [K, N] for n, K, N, _ in SHAPES}, "M": MS,
+                   "gate_up_epilogue": "SiLU(gate)*up -> [M,12288]",
+                   "parallelism": f"column-parallel x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                   "l2": "inputs larger than L2: 2 weight copies x 386 MB cycled per step",
+                   "timing": "CUDA-graph replay, CUDA events, max over ranks"},
+        "frac_of_hbm_peak": round(value / world / pk["hbm_gbs"], 4),
+        "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "path": "kernels.thin_linear_fused public API -> libsimsd_b200 C ABI, pinned host buffers"},
+        "gpu_launches": args.steps * launches_per_step,
+    }
+    if per is not None:
+        prof = _traffic_summary()
+        line["roofline"] = {
+            "bound": "hbm", "kernel": "simsd::tc_gemm_kernel", "achieved": round(agg_gbs, 1),
+            "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(agg_gbs / pk["hbm_gbs"], 4),
+            "peak_src": pk["src"], "avg_launch_us": round(avg_us, 2),
+            "traffic": prof.get("traffic_bytes_per_launch") if prof else None,
+            "traffic_note": prof.get("note") if prof else "no ncu capture summary committed",
+        }
+        line["per_launch"] = per
+    clk_summary = clk.summary()
+    line["clocks"] = clk_summary
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _traffic_summary() -> dict | None:
+    p = REPO / "profiles" / "tc_gemm_traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except ValueError:
+            return None
+    return None
+
+
+# ------------------------------------------------------------------ CPU path
+def cpu_step(ws, xs):
+    """The reference's CPU path for one step: torch eager F.linear in bf16, silu(g)*u."""
+    out = []
+    for M in MS:
+        for name, K, N, silu in SHAPES:
+            x = xs[M][K]
+            if silu:
+                gu = F.linear(x, ws[name])
+                out.append(F.silu(gu[:, : N // 2]) * gu[:, N // 2:])
+            else:
+                out.append(F.linear(x, ws[name]))
+    return out
+
+
+def cpu_setup():
+    g = torch.Generator().manual_seed(1234)
+    ws = {}
+    for name, K, N, _ in SHAPES:
+        ws[name] = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+    xs = {M: {K: torch.randn(M, K, generator=g).to(torch.bfloat16) for K in (4096, 12288)} for M in MS}
+    return ws, xs
+
+
+def cpu_baseline(seconds: float) -> dict:
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    ws, xs = cpu_setup()
+    cpu_step(ws, xs)
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        cpu_step(ws, xs)
+        n += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = (time.perf_counter() - t0) / n
+    return {"value": round(step_bytes() / dt / 1e9, 2), "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{n} full steps (20 bf16 F.linear + silu*mul on the SDAR-8B shapes, M=4..64), "
+                      f"{dt * 1e3:.1f} ms/step, torch {torch.__version__} eager on {threads} host threads"}
+
+
+def reference_arm(args):
+    rank = int(os.environ.get("RANK", 0))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    ws, xs = cpu_setup()
+    for _ in range(args.warmup):
+        cpu_step(ws, xs)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_step(ws, xs)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = round(step_bytes() / dt / 1e9, 2)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
+        "config": {"workload": "SDAR-8B thin-M linear sweep (BASELINE configs[1])",
+                   "shapes": {n: [K, N] for n, K, N, _ in SHAPES}, "M": MS,
+                   "parallelism": "host CPU (rank 0 only)"},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": "each step = the full sweep (20 bf16 F.linear + silu*mul), torch eager CPU"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def profile_case(args):
+    """A few launches of one SDAR-8B linear (for ncu captures on a small case)."""
+    from kernels.thin_linear_fused import thin_linear, thin_linear_silu_mul
+    dev = torch.device("cuda", 0)
+    name, K, N, silu = next(s for s in SHAPES if s[0] == args.profile_case)
+    g = torch.Generator(device=dev).manual_seed(3)
+    M = args.profile_m
+    x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+    ws = []
+    for _ in range(2):
+        if silu:
+            ws.append(tuple((torch.randn(N // 2, K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+                            for _ in range(2)))
+        else:
+            ws.append((torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16))
+    with torch.inference_mode():
+        for i in range(args.profile_launches + 1):
+            w = ws[i % 2]
+            y = thin_linear_silu_mul(x, *w) if silu else thin_linear(x, w)
+        torch.cuda.synchronize()
+    print(f"profile case {name} M={M}: {args.profile_launches + 1} launches, out {tuple(y.shape)}")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--profile-case", default=None, choices=[s[0] for s in SHAPES])
+    ap.add_argument("--profile-m", type=int, default=16)
+    ap.add_argument("--profile-launches", type=int, default=3)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.profile_case:
+        profile_case(args)
+    elif args.impl == "reference":
+        reference_arm(args)
+    else:
+        gpu_arm(args)
+
+
+if __name__ == "__main__":
+    main()

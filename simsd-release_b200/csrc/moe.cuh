@@ -317,6 +317,8 @@ __global__ void __launch_bounds__(ALIGN_THREADS, 1) align_kernel(const AlignArgs
       else atomicOr(p.err, SIMSD_DEV_ERR_BAD_INDEX);
     }
   }
+  // rows left over by invalid ids hold no slot
+  for (int row = s_off[E] + tid; row < S; row += ALIGN_THREADS) p.sorted_slots[row] = -1;
   if (p.slots_padded == nullptr) return;
   __syncthreads();
   // reference layout: groups padded to block_m rows, -1 = padding
@@ -363,6 +365,7 @@ __global__ void gather_rows_kernel(const void* x, long long ldx, const int* sort
   const int row = blockIdx.x;
   if (row >= S) return;
   const int slot = sorted_slots[row];
+  if (slot < 0) return;  // no token (an invalid expert id left this row empty)
   const int tok = slot / k;
   const char* src = reinterpret_cast<const char*>(x) + (long long)tok * ldx * esz;
   char* dst = reinterpret_cast<char*>(xs) + (long long)row * ldxs * esz;

@@ -143,3 +143,14 @@ def device_error(dev: torch.device | None = None) -> int:
         check(lib().simsd_workspace_error(buf.data_ptr(), stream_ptr(dev), ctypes.byref(out)),
               "simsd_workspace_error")
     return out.value
+
+
+def clear_device_error(dev: torch.device | None = None) -> None:
+    """Zero `dev`'s workspace header (error word and tile counters), stream-ordered."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if dev is None else dev
+    buf = _WORKSPACES.get(dev)
+    if buf is None:
+        return
+    with torch.cuda.device(dev):
+        check(lib().simsd_workspace_init(buf.data_ptr(), buf.numel(), stream_ptr(dev)),
+              "simsd_workspace_init")
