@@ -232,6 +232,9 @@ def gpu_arm(args):
     _lib.lib()
     pool = make_weights(rank, world, dev)
     xs = make_inputs(dev)
+    # Inference weights are fixed, so every launch may stream its weights while
+    # the previous kernel drains (programmatic dependent launch).
+    _lib.set_pdl(not args.no_pdl)
 
     with torch.inference_mode():
         for _ in range(max(3, args.warmup)):
@@ -320,6 +323,7 @@ def gpu_arm(args):
                    "gate_up_epilogue": "SiLU(gate)*up -> [M,12288]",
                    "parallelism": f"column-parallel x{world}" + (" + NCCL all-gather" if world > 1 else ""),
                    "l2": "inputs larger than L2: 2 weight copies x 386 MB cycled per step",
+                   "launch": "no PDL" if args.no_pdl else "programmatic dependent launch (weights static)",
                    "timing": "CUDA-graph replay, CUDA events, max over ranks"},
         "frac_of_hbm_peak": round(value / world / pk["hbm_gbs"], 4),
         "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
@@ -464,6 +468,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -53,11 +53,30 @@ extern "C" {
 #define SIMSD_PATH_TC 1      /* force the tcgen05/TMA kernel (SIMSD_ERR_ALIGN if not possible) */
 #define SIMSD_PATH_SIMT 2    /* force the CUDA-core kernel                            */
 
+/* ---- launch flags (process-wide) */
+#define SIMSD_LAUNCH_PDL 1   /* programmatic dependent launch, see simsd_set_launch_flags */
+
 /* Library version string. */
 const char* simsd_version(void);
 
 /* Human-readable name of a status code. */
 const char* simsd_status_string(int status);
+
+/*
+ * Set the process-wide launch flags; returns the previous ones.  No counterpart
+ * in the reference (its Triton launches have no such option).
+ * SIMSD_LAUNCH_PDL: launch every kernel as a programmatic dependent of the
+ * previous kernel on its stream, so its set-up and, for simsd_thin_linear, the
+ * first ring of weight tiles overlap that kernel's tail; activations are read
+ * and outputs written only after the previous kernel has completed.  Only set
+ * it when the weights passed to simsd_thin_linear are not written by the kernel
+ * launched just before it on the same stream (true for inference with fixed
+ * weights).
+ */
+int simsd_set_launch_flags(int flags);
+
+/* Current launch flags. */
+int simsd_get_launch_flags(void);
 
 /* Number of SMs of the current device (0 if there is none). */
 int simsd_device_sm_count(void);

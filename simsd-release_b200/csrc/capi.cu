@@ -2,6 +2,8 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
+#include <utility>
 #include <cstdio>
 #include <mutex>
 
@@ -20,7 +22,32 @@ int g_sm_count[kMaxDev];
 bool g_smem_attr[kMaxDev][16];
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
+std::atomic<int> g_launch_flags{0};
+
 inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+inline bool pdl_on() { return (g_launch_flags.load(std::memory_order_relaxed) & SIMSD_LAUNCH_PDL) != 0; }
+
+// Launch `kern` on `s`, as a programmatic dependent of the previous kernel on
+// the stream when SIMSD_LAUNCH_PDL is set (every kernel here starts with
+// griddepcontrol.wait before it reads anything another kernel produced).
+template <typename... KArgs, typename... Args>
+int launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  if (pdl_on()) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  if (cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...) != cudaSuccess) return SIMSD_ERR_LAUNCH;
+  return cudaGetLastError() == cudaSuccess ? SIMSD_OK : SIMSD_ERR_LAUNCH;
+}
 inline int esize(int dtype) { return dtype == SIMSD_F32 ? 4 : 2; }
 inline long long cdiv(long long a, long long b) { return (a + b - 1) / b; }
 
@@ -94,8 +121,9 @@ int launch_tc_b(const TcGemmArgs& a, int grid, cudaStream_t s, int dev) {
       g_smem_attr[dev][idx] = true;
     }
   }
-  tc_gemm_kernel<BMAX><<<grid, TC_THREADS, smem, s>>>(a);
-  return cudaGetLastError() == cudaSuccess ? SIMSD_OK : SIMSD_ERR_LAUNCH;
+  TcGemmArgs args = a;
+  args.pdl = pdl_on() ? 1 : 0;
+  return launch(tc_gemm_kernel<BMAX>, dim3(grid), dim3(TC_THREADS), smem, s, args);
 }
 
 int launch_tc(int bmax, const TcGemmArgs& a, int grid, cudaStream_t s, int dev) {
@@ -163,6 +191,12 @@ const char* simsd_status_string(int s) {
   }
   return "unknown status";
 }
+
+int simsd_set_launch_flags(int flags) {
+  return g_launch_flags.exchange(flags & SIMSD_LAUNCH_PDL);
+}
+
+int simsd_get_launch_flags(void) { return g_launch_flags.load(); }
 
 int simsd_device_sm_count(void) {
   const int dev = current_device();
@@ -280,8 +314,7 @@ int simsd_thin_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w
   const long long gy = cdiv(M, SIMT_ROWS);
   if (gy > 65535) return SIMSD_ERR_UNSUPPORTED;
   dim3 grid((unsigned)cdiv(N, SIMT_WARPS), (unsigned)gy);
-  simt_gemm_kernel<<<grid, SIMT_WARPS * 32, 0, s>>>(a);
-  return cudaGetLastError() == cudaSuccess ? SIMSD_OK : SIMSD_ERR_LAUNCH;
+  return launch(simt_gemm_kernel, grid, dim3(SIMT_WARPS * 32), 0, s, a);
 }
 
 // ---------------------------------------------------------------- MoE
@@ -321,8 +354,8 @@ int simsd_moe_route(const void* x, int64_t ldx, int x_dtype, const void* wr, int
       g_smem_attr[dev][8] = true;
     }
   }
-  route_kernel<<<(unsigned)cdiv(T, ROUTE_TOK), ROUTE_WARPS * 32, smem, (cudaStream_t)stream>>>(a);
-  return cudaGetLastError() == cudaSuccess ? SIMSD_OK : SIMSD_ERR_LAUNCH;
+  return launch(route_kernel, dim3((unsigned)cdiv(T, ROUTE_TOK)), dim3(ROUTE_WARPS * 32), smem,
+                (cudaStream_t)stream, a);
 }
 
 static int launch_align(const int64_t* ids, int S, int E, int32_t* counts, int32_t* offsets, int32_t* sorted,
@@ -351,8 +384,7 @@ static int launch_align(const int64_t* ids, int S, int E, int32_t* counts, int32
       g_smem_attr[dev][9] = true;
     }
   }
-  align_kernel<<<1, ALIGN_THREADS, smem, s>>>(a);
-  return cudaGetLastError() == cudaSuccess ? SIMSD_OK : SIMSD_ERR_LAUNCH;
+  return launch(align_kernel, dim3(1), dim3(ALIGN_THREADS), smem, s, a);
 }
 
 int simsd_moe_align(const int64_t* topk_ids, int S, int E, int32_t* counts, int32_t* offsets, int32_t* sorted_slots,
@@ -447,8 +479,9 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
 
   int rc = launch_align(topk_ids, (int)S, E, counts, offsets, sorted, s2r, 16, 0, nullptr, nullptr, err, s, dev);
   if (rc != SIMSD_OK) return rc;
-  gather_rows_kernel<<<(unsigned)S, 256, 0, s>>>(x, ldx, sorted, xs, H, (int)S, k, H, es);
-  if (cudaGetLastError() != cudaSuccess) return SIMSD_ERR_LAUNCH;
+  rc = launch(gather_rows_kernel, dim3((unsigned)S), dim3(256), 0, s, x, (long long)ldx, (const int*)sorted, xs,
+              (long long)H, (int)S, k, H, es);
+  if (rc != SIMSD_OK) return rc;
 
   if (plan.tc) {
     if (ensure_encode() != SIMSD_OK) return SIMSD_ERR_DEVICE;
@@ -531,8 +564,9 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
     a.K = H;
     a.dtype = dtype;
     a.silu = 1;
-    simt_gemm_kernel<<<dim3((unsigned)cdiv(I, SIMT_WARPS), (unsigned)max_chunks), SIMT_WARPS * 32, 0, s>>>(a);
-    if (cudaGetLastError() != cudaSuccess) return SIMSD_ERR_LAUNCH;
+    rc = launch(simt_gemm_kernel, dim3((unsigned)cdiv(I, SIMT_WARPS), (unsigned)max_chunks), dim3(SIMT_WARPS * 32),
+                0, s, a);
+    if (rc != SIMSD_OK) return rc;
     SimtGemmArgs d = a;
     d.a = hbuf;
     d.w = w_down;
@@ -545,11 +579,12 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
     d.N = H;
     d.K = I;
     d.silu = 0;
-    simt_gemm_kernel<<<dim3((unsigned)cdiv(H, SIMT_WARPS), (unsigned)max_chunks), SIMT_WARPS * 32, 0, s>>>(d);
-    if (cudaGetLastError() != cudaSuccess) return SIMSD_ERR_LAUNCH;
+    rc = launch(simt_gemm_kernel, dim3((unsigned)cdiv(H, SIMT_WARPS), (unsigned)max_chunks), dim3(SIMT_WARPS * 32),
+                0, s, d);
+    if (rc != SIMSD_OK) return rc;
   }
-  combine_kernel<<<(unsigned)T, 256, 0, s>>>(ys, H, s2r, topk_weight, out, ld_out, add, ld_add, T, k, H, dtype);
-  return cudaGetLastError() == cudaSuccess ? SIMSD_OK : SIMSD_ERR_LAUNCH;
+  return launch(combine_kernel, dim3((unsigned)T), dim3(256), 0, s, (const void*)ys, (long long)H, (const int*)s2r,
+                topk_weight, out, (long long)ld_out, add, (long long)ld_add, T, k, H, dtype);
 }
 
 }  // extern "C"

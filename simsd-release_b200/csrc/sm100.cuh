@@ -199,6 +199,17 @@ __host__ __device__ __forceinline__ uint32_t make_idesc_f16(int is_bf16, int M, 
   return d;
 }
 
+// ---------------------------------------------------------------- PDL
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start before the previous kernel on its stream finishes;
+// griddep_wait() blocks until that kernel has completed and its writes are
+// visible (a no-op when the launch had no such dependency), and
+// griddep_launch_dependents() lets the next kernel begin launching early.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- misc
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

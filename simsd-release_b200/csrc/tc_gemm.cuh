@@ -51,7 +51,7 @@ struct alignas(64) TcGemmArgs {
   CUtensorMap tmB;           // activations: 2-D {K, rows}
   void* out;                 // output, row stride ld_out elements
   const void* bias;          // [rows_out] or nullptr (single mode only)
-  float* partials;           // [2 * gridDim.x][BMAX][128]
+  float* partials;           // [2 * gridDim.x][128 weight rows][BMAX activation rows] fp32
   int* tile_counters;        // [max_tiles], zero on entry and on exit
   int* err;                  // device error word
   const int* group_counts;   // grouped mode: rows per group; nullptr = single mode
@@ -65,6 +65,7 @@ struct alignas(64) TcGemmArgs {
   int three_d;
   int is_bf16;
   int max_tiles;
+  int pdl;                   // launched as a programmatic dependent (see griddep_wait)
 };
 
 template <int BMAX>
@@ -173,8 +174,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     tmem_alloc(smem_u32(tmem_slot), Cfg::TMEM_COLS);
     tmem_relinquish();
   }
+  if (tid == 0) griddep_launch_dependents();
   long long total_tiles;
   if (p.group_counts != nullptr) {
+    // the counts come from the align kernel just before this one
+    if (p.pdl) griddep_wait();
     const int G = p.num_groups;
     for (int g = tid; g < G; g += TC_THREADS) row_prefix[g + 1] = p.group_counts[g];
     __syncthreads();
@@ -235,6 +239,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
       uint32_t issued_mask = 0;        // stages that have ever been armed
       uint32_t last_parity = 0;        // parity of each stage's last arming
       bool ok = true;
+      // Programmatic dependent launch, single mode: the weights are not written
+      // by the kernel before this one, so the first ring of weight tiles is
+      // fetched before griddep_wait(); the activation boxes of those stages are
+      // issued right after the wait.  Everything that reads the activations or
+      // writes memory (MMA, epilogue, fixup) sits behind those loads.
+      bool dep_ready = !(p.pdl && p.group_counts == nullptr);
+      int npend = 0;
+      uint32_t pend_dst[Cfg::STAGES], pend_bar[Cfg::STAGES];
+      int pend_k0[Cfg::STAGES], pend_row0[Cfg::STAGES], pend_nb[Cfg::STAGES];
+      auto flush_pending = [&]() {
+        griddep_wait();
+        dep_ready = true;
+        for (int q = 0; q < npend; ++q)
+          for (int b = 0; b < pend_nb[q]; ++b)
+            tma_load_2d(pend_dst[q] + b * TC_BOX_BYTES, &p.tmB, pend_bar[q], pend_k0[q],
+                        pend_row0[q] + b * TC_BOX_ROWS, pol_x);
+        npend = 0;
+      };
       for (long long it = it_begin; ok && it < it_end;) {
         const long long tile = it / kb;
         const int kb0 = (int)(it - tile * kb);
@@ -242,6 +264,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         const TileInfo ti = decode_tile<BMAX>(tile, p, row_prefix, chunk_prefix);
         const int nb = (ti.nrows + TC_BOX_ROWS - 1) / TC_BOX_ROWS;
         for (int k = kb0; k < kb1; ++k) {
+          if (!dep_ready && npend == STAGES) flush_pending();
           if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, abort_flag, p.err)) { ok = false; break; }
           const uint32_t fb = smem_u32(&full_bar[stage]);
           mbar_arrive_expect_tx(fb, TC_A_BYTES + nb * TC_BOX_BYTES);
@@ -264,12 +287,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
             else tma_load_2d(a_dst, &p.tmA0, fb, k0, r0, pol_w);
           }
           const uint32_t b_dst = smem_u32(sB + stage * Cfg::B_BYTES);
-          for (int b = 0; b < nb; ++b)
-            tma_load_2d(b_dst + b * TC_BOX_BYTES, &p.tmB, fb, k0, ti.row0 + b * TC_BOX_ROWS, pol_x);
+          if (dep_ready) {
+            for (int b = 0; b < nb; ++b)
+              tma_load_2d(b_dst + b * TC_BOX_BYTES, &p.tmB, fb, k0, ti.row0 + b * TC_BOX_ROWS, pol_x);
+          } else {
+            pend_dst[npend] = b_dst;
+            pend_bar[npend] = fb;
+            pend_k0[npend] = k0;
+            pend_row0[npend] = ti.row0;
+            pend_nb[npend] = nb;
+            ++npend;
+          }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
         it = tile * kb + kb1;
       }
+      // fewer iterations than ring stages, or aborting with weight-only stages
+      // armed: their activation boxes still have to land
+      if (!dep_ready) flush_pending();
       if (!ok) {
         // aborting: make sure no TMA copy is still landing in shared memory
         for (int s = 0; s < STAGES; ++s)
@@ -384,16 +419,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
           }
         }
       } else {
-        // partial K range of this tile: park the fp32 partial in this CTA's slot
+        // partial K range of this tile: park the fp32 partial in this CTA's slot,
+        // laid out [weight row][activation row] so the fixup reads 16-float runs
         const long long first_tile_of_cta = it_begin / kb;
         const long long slot = 2 * c + (tile == first_tile_of_cta ? 0 : 1);
-        float* P = p.partials + slot * (long long)(BMAX * 128);
+        float* P = p.partials + slot * (long long)(BMAX * 128) + (long long)row * BMAX;
         for (int ch = 0; ch < nb; ++ch) {
           float v[16];
           tmem_ld16(t_base + ch * 16, v);
           tmem_wait_ld();
+          float4* d = reinterpret_cast<float4*>(P + ch * 16);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) __stcg(&P[(ch * 16 + j) * 128 + row], v[j]);
+          for (int u = 0; u < 4; ++u) __stcg(d + u, make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]));
         }
         tc_fence_before();
         mbar_arrive(smem_u32(&acce_bar[a]));
@@ -421,29 +458,91 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
             seg_slot[i] = (int)(2 * cc + ((tile == sk_start(cc, iters, G) / kb) ? 0 : 1));
           }
           named_bar_sync(1, 128);
+          // Sum the segments in K order.  All loads of a batch of segments are
+          // issued before any add, so the batch costs one L2 round trip.
           if (!p.silu) {
             const int col = out_col0 + row;
-            if (col < p.rows_out) {
-              const float bv = p.bias ? load_f(p.bias, col, p.is_bf16 ? 0 : 1) : 0.0f;
-              for (int t = 0; t < ti.nrows; ++t) {
-                float s = 0.0f;
-                for (int i = 0; i < nseg; ++i)
-                  s = __fadd_rn(s, __ldcg(&p.partials[(long long)seg_slot[i] * (BMAX * 128) + t * 128 + row]));
-                store_f(outp, (long long)(ti.row0 + t) * p.ld_out + col, __fadd_rn(s, bv), p.is_bf16 ? 0 : 1);
+            const float bv = (p.bias && col < p.rows_out) ? load_f(p.bias, col, p.is_bf16 ? 0 : 1) : 0.0f;
+            for (int ch = 0; ch < nb; ++ch) {
+              float acc[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
+              for (int i0 = 0; i0 < nseg; i0 += 4) {
+                float4 buf[4][4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  if (i0 + q < nseg) {
+                    const float4* src = reinterpret_cast<const float4*>(
+                        p.partials + (long long)seg_slot[i0 + q] * (BMAX * 128) + (long long)row * BMAX + ch * 16);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) buf[q][u] = __ldcg(src + u);
+                  }
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  if (i0 + q < nseg) {
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                      acc[4 * u] = __fadd_rn(acc[4 * u], buf[q][u].x);
+                      acc[4 * u + 1] = __fadd_rn(acc[4 * u + 1], buf[q][u].y);
+                      acc[4 * u + 2] = __fadd_rn(acc[4 * u + 2], buf[q][u].z);
+                      acc[4 * u + 3] = __fadd_rn(acc[4 * u + 3], buf[q][u].w);
+                    }
+                  }
+                }
+              }
+              if (col < p.rows_out) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const int t = ch * 16 + j;
+                  if (t < ti.nrows)
+                    store_f(outp, (long long)(ti.row0 + t) * p.ld_out + col, __fadd_rn(acc[j], bv), p.is_bf16 ? 0 : 1);
+                }
               }
             }
           } else {
             const int i = row & 63;
             const int col = out_col0 + i;
-            if (col < p.rows_out) {
-              for (int t = row >> 6; t < ti.nrows; t += 2) {
-                float g = 0.0f, u = 0.0f;
-                for (int q = 0; q < nseg; ++q) {
-                  const float* Q = p.partials + (long long)seg_slot[q] * (BMAX * 128) + t * 128;
-                  g = __fadd_rn(g, __ldcg(&Q[i]));
-                  u = __fadd_rn(u, __ldcg(&Q[64 + i]));
+            for (int ch = row >> 6; ch < nb; ch += 2) {
+              float ag[16], au[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) { ag[j] = 0.0f; au[j] = 0.0f; }
+              for (int i0 = 0; i0 < nseg; i0 += 2) {
+                float4 bg[2][4], bu[2][4];
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                  if (i0 + q < nseg) {
+                    const float* base = p.partials + (long long)seg_slot[i0 + q] * (BMAX * 128) + ch * 16;
+                    const float4* sg = reinterpret_cast<const float4*>(base + (long long)i * BMAX);
+                    const float4* su = reinterpret_cast<const float4*>(base + (long long)(64 + i) * BMAX);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) { bg[q][u] = __ldcg(sg + u); bu[q][u] = __ldcg(su + u); }
+                  }
                 }
-                store_f(outp, (long long)(ti.row0 + t) * p.ld_out + col, silu_mul(g, u), p.is_bf16 ? 0 : 1);
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                  if (i0 + q < nseg) {
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                      ag[4 * u] = __fadd_rn(ag[4 * u], bg[q][u].x);
+                      ag[4 * u + 1] = __fadd_rn(ag[4 * u + 1], bg[q][u].y);
+                      ag[4 * u + 2] = __fadd_rn(ag[4 * u + 2], bg[q][u].z);
+                      ag[4 * u + 3] = __fadd_rn(ag[4 * u + 3], bg[q][u].w);
+                      au[4 * u] = __fadd_rn(au[4 * u], bu[q][u].x);
+                      au[4 * u + 1] = __fadd_rn(au[4 * u + 1], bu[q][u].y);
+                      au[4 * u + 2] = __fadd_rn(au[4 * u + 2], bu[q][u].z);
+                      au[4 * u + 3] = __fadd_rn(au[4 * u + 3], bu[q][u].w);
+                    }
+                  }
+                }
+              }
+              if (col < p.rows_out) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const int t = ch * 16 + j;
+                  if (t < ti.nrows)
+                    store_f(outp, (long long)(ti.row0 + t) * p.ld_out + col, silu_mul(ag[j], au[j]), p.is_bf16 ? 0 : 1);
+                }
               }
             }
           }

@@ -28,6 +28,8 @@ SIMSD_BF16, SIMSD_F16, SIMSD_F32 = 0, 1, 2
 EPI_NONE, EPI_SILU_MUL = 0, 1
 PATH_AUTO, PATH_TC, PATH_SIMT = 0, 1, 2
 
+LAUNCH_PDL = 1
+
 DEV_ERR_TIMEOUT = 1
 DEV_ERR_BAD_INDEX = 2
 
@@ -39,6 +41,8 @@ SIGNATURES: dict[str, tuple] = {
     "simsd_version": (ctypes.c_char_p, []),
     "simsd_status_string": (ctypes.c_char_p, [_I]),
     "simsd_device_sm_count": (_I, []),
+    "simsd_set_launch_flags": (_I, [_I]),
+    "simsd_get_launch_flags": (_I, []),
     "simsd_workspace_header_bytes": (_S, []),
     "simsd_workspace_init": (_I, [_P, _S, _P]),
     "simsd_workspace_error": (_I, [_P, _P, ctypes.POINTER(_I)]),
@@ -154,3 +158,24 @@ def clear_device_error(dev: torch.device | None = None) -> None:
     with torch.cuda.device(dev):
         check(lib().simsd_workspace_init(buf.data_ptr(), buf.numel(), stream_ptr(dev)),
               "simsd_workspace_init")
+
+
+def set_pdl(enable: bool) -> bool:
+    """Launch kernels as programmatic dependents (weights must not be written by the
+    kernel right before each call on the same stream).  Returns the previous setting."""
+    return bool(lib().simsd_set_launch_flags(LAUNCH_PDL if enable else 0) & LAUNCH_PDL)
+
+
+class weights_static:
+    """Context manager enabling programmatic dependent launch for its body."""
+
+    def __init__(self, enable: bool = True):
+        self.enable = enable
+
+    def __enter__(self):
+        self.prev = set_pdl(self.enable)
+        return self
+
+    def __exit__(self, *exc):
+        set_pdl(self.prev)
+        return False

@@ -104,8 +104,9 @@ def thin_linear(x: torch.Tensor, w: torch.Tensor,
     dev = _lib.require_cuda(x, w, bias)
 
     out_shape = (*x.shape[:-1], N)
-    x2 = x.reshape(-1, K)
-    M = x2.shape[0]
+    M = 1
+    for d in x.shape[:-1]:
+        M *= d
     y = torch.empty((M, N), device=dev, dtype=x.dtype)
     if M == 0 or N == 0:
         return y.view(out_shape)
@@ -114,6 +115,7 @@ def thin_linear(x: torch.Tensor, w: torch.Tensor,
         if bias is not None:
             y += bias
         return y.view(out_shape)
+    x2 = x.reshape(M, K)
     if bias is not None and bias.stride(0) != 1:
         bias = bias.contiguous()
 
@@ -161,13 +163,15 @@ def thin_linear_silu_mul(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tens
         raise ValueError(f"K mismatch: x[..., {x.shape[-1]}] vs w[{I}, {K}]")
     dev = _lib.require_cuda(x, w_gate, w_up)
     out_shape = (*x.shape[:-1], I)
-    x2 = x.reshape(-1, K)
-    M = x2.shape[0]
+    M = 1
+    for d in x.shape[:-1]:
+        M *= d
     y = torch.empty((M, I), device=dev, dtype=x.dtype)
     if M == 0 or I == 0:
         return y.view(out_shape)
     if K == 0:
         return y.zero_().view(out_shape)
+    x2 = x.reshape(M, K)
     L = _lib.lib()
     with torch.cuda.device(dev):
         nbytes = L.simsd_thin_linear_workspace_size(M, I, K, code, _lib.EPI_SILU_MUL, split)

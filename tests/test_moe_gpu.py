@@ -336,5 +336,23 @@ def test_moe_layer_router_experts_shared():
     assert np.array_equal(ids.cpu().numpy(), oi)
 
 
+def test_programmatic_dependent_launch_moe_chain_is_exact():
+    T, H, E, k, I = 64, 2048, 256, 8, 512
+    g = torch.Generator(device=DEV).manual_seed(71)
+    x = torch.randn(T, H, device=DEV, generator=g).to(torch.bfloat16)
+    wr = (torch.randn(E, H, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+    b = torch.randn(E, device=DEV, generator=g) * 0.1
+    wg, wu, wd = experts(E, H, I, torch.bfloat16, seed=72)
+    sg, su, sd = (t[0] for t in experts(1, H, I, torch.bfloat16, seed=73))
+    with torch.inference_mode():
+        ref = moe_layer(x, wr, b, k, wg, wu, wd, shared=(sg, su, sd))
+        with _lib.weights_static():
+            got = moe_layer(x, wr, b, k, wg, wu, wd, shared=(sg, su, sd))
+            got2 = moe_layer(got, wr, b, k, wg, wu, wd)
+        ref2 = moe_layer(ref, wr, b, k, wg, wu, wd)
+        torch.cuda.synchronize()
+    assert torch.equal(got, ref) and torch.equal(got2, ref2)
+
+
 def test_no_device_errors_recorded():
     assert _lib.device_error(torch.device(DEV, torch.cuda.current_device())) == 0

@@ -382,5 +382,48 @@ def test_toggle_fused_gate_up_mlp():
     assert float((got.float() - ref.float()).abs().max()) <= 2 ** -6 * float(ref.abs().max()) + 1e-3
 
 
+def _chain(x, ws):
+    h = x
+    for i, w in enumerate(ws):
+        h = thin_linear(h, w)
+        if i % 3 == 2:
+            h = h * 0.5                  # a torch kernel between two of ours
+    return h
+
+
+def test_programmatic_dependent_launch_chain_is_exact():
+    """With PDL each launch streams its weights before the previous kernel ends;
+    a dependent chain must still see every activation, bit for bit."""
+    ws = [rnd(2048, 2048, scale=0.03, seed=70 + i) for i in range(8)]
+    x = rnd(16, 2048, seed=80)
+    with torch.inference_mode():
+        ref = _chain(x, ws)
+        with _lib.weights_static():
+            got = _chain(x, ws)
+            h = thin_linear_silu_mul(got[:4], ws[0], ws[1])
+        h_ref = thin_linear_silu_mul(ref[:4], ws[0], ws[1])
+        torch.cuda.synchronize()
+    assert torch.equal(got, ref) and torch.equal(h, h_ref)
+    assert not _lib.set_pdl(False)
+
+
+def test_programmatic_dependent_launch_in_graph():
+    ws = [rnd(4096, 2048, scale=0.02, seed=90), rnd(2048, 4096, scale=0.02, seed=91)]
+    x = rnd(8, 2048, seed=92)
+    with torch.inference_mode():
+        ref = thin_linear(thin_linear(x, ws[0]), ws[1])
+        with _lib.weights_static():
+            for _ in range(3):
+                thin_linear(thin_linear(x, ws[0]), ws[1])
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                out = thin_linear(thin_linear(x, ws[0]), ws[1])
+        for _ in range(5):
+            g.replay()
+        torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+
+
 def test_no_device_errors_recorded():
     assert _lib.device_error(torch.device(DEV, torch.cuda.current_device())) == 0
