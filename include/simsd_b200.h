@@ -78,6 +78,15 @@ int simsd_set_launch_flags(int flags);
 /* Current launch flags. */
 int simsd_get_launch_flags(void);
 
+/*
+ * Diagnostics (no counterpart in the reference): while `buf` is set, every
+ * tensor-core GEMM launch whose grid fits writes 8 %globaltimer stamps (ns) per
+ * CTA into buf[cta*8 + i]: entry, set-up done, first TMA issued, first MMA
+ * stage ready, last TMA issued, last MMA committed, SM id (not a time), exit.
+ * `bytes` >= 64 * grid.  NULL disables.  Not for concurrent use.
+ */
+int simsd_debug_set_trace(void* buf, size_t bytes);
+
 /* Number of SMs of the current device (0 if there is none). */
 int simsd_device_sm_count(void);
 

@@ -3,8 +3,10 @@
 
 #include <algorithm>
 #include <atomic>
+#include <initializer_list>
 #include <utility>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "moe.cuh"
@@ -19,7 +21,9 @@ namespace {
 constexpr int kMaxDev = 64;
 std::mutex g_mu;
 int g_sm_count[kMaxDev];
-bool g_smem_attr[kMaxDev][16];
+bool g_smem_attr[kMaxDev][40];
+unsigned long long* g_trace = nullptr;
+size_t g_trace_bytes = 0;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 std::atomic<int> g_launch_flags{0};
@@ -108,14 +112,40 @@ int pick_bmax_rows(long long rows) {
   return 256;
 }
 
-template <int BMAX>
+// K atoms per ring stage: SIMSD_TC_KS (1, 2 or 4) overrides the default; stages
+// must still fit twice in shared memory, so wide activation tiles cap it.
+// Ring budget: SIMSD_TC_RING (196 or 96, KB) overrides the default.
+int env_choice(const char* name, std::initializer_list<int> allowed, int dflt) {
+  const char* e = getenv(name);
+  if (!e) return dflt;
+  const int v = atoi(e);
+  for (int a : allowed)
+    if (a == v) return v;
+  return dflt;
+}
+
+int ring_kb() {
+  static const int v = env_choice("SIMSD_TC_RING", {196, 96}, 196);
+  return v;
+}
+
+int ks_for(int bmax) {
+  static const int req = env_choice("SIMSD_TC_KS", {1, 2, 4}, 2);
+  if (ring_kb() == 96) return std::min(req, bmax <= 32 ? 2 : 1);
+  return std::min(req, bmax <= 64 ? 4 : 2);
+}
+
+template <int BMAX, int KS, int RING>
 int launch_tc_b(const TcGemmArgs& a, int grid, cudaStream_t s, int dev) {
-  constexpr int smem = TcConfig<BMAX>::SMEM_BYTES;
-  constexpr int idx = BMAX == 16 ? 0 : BMAX == 32 ? 1 : BMAX == 64 ? 2 : BMAX == 128 ? 3 : 4;
+  constexpr int smem = TcConfig<BMAX, KS, RING>::SMEM_BYTES;
+  constexpr int bi = BMAX == 16 ? 0 : BMAX == 32 ? 1 : BMAX == 64 ? 2 : BMAX == 128 ? 3 : 4;
+  constexpr int idx = (RING == 196 ? 0 : 15) + bi * 3 + (KS == 1 ? 0 : KS == 2 ? 1 : 2);
+  static_assert(RING == 196 || 2 * (TcConfig<BMAX, KS, RING>::SMEM_BYTES + 1024) <= 228 * 1024,
+                "two CTAs of the small ring must share an SM");
   {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g_smem_attr[dev][idx]) {
-      if (cudaFuncSetAttribute(tc_gemm_kernel<BMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+      if (cudaFuncSetAttribute(tc_gemm_kernel<BMAX, KS, RING>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
           cudaSuccess)
         return SIMSD_ERR_LAUNCH;
       g_smem_attr[dev][idx] = true;
@@ -123,18 +153,84 @@ int launch_tc_b(const TcGemmArgs& a, int grid, cudaStream_t s, int dev) {
   }
   TcGemmArgs args = a;
   args.pdl = pdl_on() ? 1 : 0;
-  return launch(tc_gemm_kernel<BMAX>, dim3(grid), dim3(TC_THREADS), smem, s, args);
+  args.trace = (g_trace && g_trace_bytes >= (size_t)grid * 64) ? g_trace : nullptr;
+  return launch(tc_gemm_kernel<BMAX, KS, RING>, dim3(grid), dim3(TC_THREADS), smem, s, args);
+}
+
+template <int BMAX>
+int launch_tc_ks(const TcGemmArgs& a, int grid, cudaStream_t s, int dev) {
+  const int ks = ks_for(BMAX);
+  if (ring_kb() == 96) {
+    if constexpr (BMAX <= 32) {
+      if (ks == 2) return launch_tc_b<BMAX, 2, 96>(a, grid, s, dev);
+    }
+    if constexpr (BMAX <= 128) return launch_tc_b<BMAX, 1, 96>(a, grid, s, dev);
+  }
+  switch (ks) {
+    case 1: return launch_tc_b<BMAX, 1, 196>(a, grid, s, dev);
+    case 2: return launch_tc_b<BMAX, 2, 196>(a, grid, s, dev);
+    default:
+      if constexpr (BMAX <= 64) return launch_tc_b<BMAX, 4, 196>(a, grid, s, dev);
+      else return launch_tc_b<BMAX, 2, 196>(a, grid, s, dev);
+  }
 }
 
 int launch_tc(int bmax, const TcGemmArgs& a, int grid, cudaStream_t s, int dev) {
   switch (bmax) {
-    case 16: return launch_tc_b<16>(a, grid, s, dev);
-    case 32: return launch_tc_b<32>(a, grid, s, dev);
-    case 64: return launch_tc_b<64>(a, grid, s, dev);
-    case 128: return launch_tc_b<128>(a, grid, s, dev);
-    case 256: return launch_tc_b<256>(a, grid, s, dev);
+    case 16: return launch_tc_ks<16>(a, grid, s, dev);
+    case 32: return launch_tc_ks<32>(a, grid, s, dev);
+    case 64: return launch_tc_ks<64>(a, grid, s, dev);
+    case 128: return launch_tc_ks<128>(a, grid, s, dev);
+    case 256: return launch_tc_ks<256>(a, grid, s, dev);
   }
   return SIMSD_ERR_UNSUPPORTED;
+}
+
+template <int BMAX>
+int launch_fixup_b(const TcFixupArgs& f, long long max_tiles, cudaStream_t s) {
+  if (max_tiles <= 0) return SIMSD_OK;
+  if (max_tiles > 0x7fffffffLL) return SIMSD_ERR_UNSUPPORTED;
+  return launch(tc_fixup_kernel<BMAX>, dim3((unsigned)max_tiles, BMAX / 16), dim3(128), 0, s, f);
+}
+
+int launch_fixup(int bmax, const TcFixupArgs& f, long long max_tiles, cudaStream_t s) {
+  switch (bmax) {
+    case 16: return launch_fixup_b<16>(f, max_tiles, s);
+    case 32: return launch_fixup_b<32>(f, max_tiles, s);
+    case 64: return launch_fixup_b<64>(f, max_tiles, s);
+    case 128: return launch_fixup_b<128>(f, max_tiles, s);
+    case 256: return launch_fixup_b<256>(f, max_tiles, s);
+  }
+  return SIMSD_ERR_UNSUPPORTED;
+}
+
+TcFixupArgs fixup_args(const TcGemmArgs& a, int grid) {
+  TcFixupArgs f;
+  f.partials = a.partials;
+  f.out = a.out;
+  f.bias = a.bias;
+  f.group_counts = a.group_counts;
+  f.tables = a.tables;
+  f.ld_out = a.ld_out;
+  f.single_rows = a.single_rows;
+  f.num_groups = a.num_groups;
+  f.kb = a.kb;
+  f.rows_out = a.rows_out;
+  f.row_tiles = a.row_tiles;
+  f.silu = a.silu;
+  f.is_bf16 = a.is_bf16;
+  f.grid = grid;
+  return f;
+}
+
+// Does the stream-K split of (tiles x kb) over `grid` CTAs cut any tile?
+bool any_split_tile(long long tiles, long long kb, long long grid) {
+  const long long iters = tiles * kb;
+  const long long G = std::min(grid, iters);
+  auto owner = [&](long long i) { return ((i + 1) * G + iters - 1) / iters - 1; };
+  for (long long t = 0; t < tiles; ++t)
+    if (owner(t * kb) != owner(t * kb + kb - 1)) return true;
+  return false;
 }
 
 // ---------------------------------------------------------------- thin linear plan
@@ -198,6 +294,13 @@ int simsd_set_launch_flags(int flags) {
 
 int simsd_get_launch_flags(void) { return g_launch_flags.load(); }
 
+int simsd_debug_set_trace(void* buf, size_t bytes) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_trace = reinterpret_cast<unsigned long long*>(buf);
+  g_trace_bytes = buf ? bytes : 0;
+  return SIMSD_OK;
+}
+
 int simsd_device_sm_count(void) {
   const int dev = current_device();
   return dev < 0 ? 0 : sm_count_of(dev);
@@ -260,7 +363,6 @@ int simsd_thin_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w
     if (ensure_encode() != SIMSD_OK) return SIMSD_ERR_DEVICE;
     const ThinPlan pl = plan_thin(M, N, K, epilogue, split, sm_count_of(dev));
     if (workspace_bytes < pl.ws_bytes) return SIMSD_ERR_WORKSPACE;
-    if (pl.tiles > WS_MAX_COUNTERS) return SIMSD_ERR_UNSUPPORTED;
     TcGemmArgs a;
     memset(&a, 0, sizeof(a));
     const long long lx = (M > 1) ? ldx_m : ((K * 2 + 15) / 16) * 8;
@@ -275,7 +377,7 @@ int simsd_thin_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w
     a.ld_out = ldy_m;
     a.bias = bias;
     a.partials = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + WS_COUNTER_BYTES);
-    a.tile_counters = reinterpret_cast<int*>(workspace);
+    a.tables = nullptr;
     a.err = err;
     a.group_counts = nullptr;
     a.num_groups = 1;
@@ -286,8 +388,9 @@ int simsd_thin_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w
     a.silu = silu ? 1 : 0;
     a.three_d = 0;
     a.is_bf16 = dtype == SIMSD_BF16 ? 1 : 0;
-    a.max_tiles = WS_MAX_COUNTERS;
-    return launch_tc(pl.bmax, a, pl.grid, s, dev);
+    int rc2 = launch_tc(pl.bmax, a, pl.grid, s, dev);
+    if (rc2 != SIMSD_OK || !any_split_tile(pl.tiles, pl.kb, pl.grid)) return rc2;
+    return launch_fixup(pl.bmax, fixup_args(a, pl.grid), pl.tiles, s);
   }
 
   SimtGemmArgs a;
@@ -347,11 +450,11 @@ int simsd_moe_route(const void* x, int64_t ldx, int x_dtype, const void* wr, int
   if (dev < 0) return SIMSD_ERR_DEVICE;
   {
     std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_smem_attr[dev][8]) {
+    if (!g_smem_attr[dev][38]) {
       if (cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * ROUTE_TOK * 1024 * 4) !=
           cudaSuccess)
         return SIMSD_ERR_LAUNCH;
-      g_smem_attr[dev][8] = true;
+      g_smem_attr[dev][38] = true;
     }
   }
   return launch(route_kernel, dim3((unsigned)cdiv(T, ROUTE_TOK)), dim3(ROUTE_WARPS * 32), smem,
@@ -377,11 +480,11 @@ static int launch_align(const int64_t* ids, int S, int E, int32_t* counts, int32
   const int smem = (32 * E + 2 * (E + 1)) * (int)sizeof(int);
   {
     std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_smem_attr[dev][9]) {
+    if (!g_smem_attr[dev][39]) {
       if (cudaFuncSetAttribute(align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (32 * 1024 + 2 * 1025) * 4) != cudaSuccess)
         return SIMSD_ERR_LAUNCH;
-      g_smem_attr[dev][9] = true;
+      g_smem_attr[dev][39] = true;
     }
   }
   return launch(align_kernel, dim3(1), dim3(ALIGN_THREADS), smem, s, a);
@@ -405,8 +508,8 @@ namespace {
 struct MoePlan {
   bool tc;
   int bmax, grid;
-  size_t off_counts, off_offsets, off_sorted, off_s2r, off_xs, off_h, off_ys, off_part, total;
-  long long max_tiles;
+  size_t off_counts, off_offsets, off_sorted, off_s2r, off_xs, off_h, off_ys, off_tables, off_part, total;
+  long long max_chunks;
 };
 
 MoePlan plan_moe(int T, int k, int E, int H, int I, int dtype, int sms, bool tc) {
@@ -425,11 +528,11 @@ MoePlan plan_moe(int T, int k, int E, int H, int I, int dtype, int sms, bool tc)
   p.off_xs = o; o = align256(o + (size_t)S * H * es);
   p.off_h = o; o = align256(o + (size_t)S * I * es);
   p.off_ys = o; o = align256(o + (size_t)S * H * es);
+  p.off_tables = o; o = align256(o + (size_t)TC_TABLE_INTS * 4);
   p.off_part = o;
   if (tc) o = align256(o + (size_t)2 * p.grid * p.bmax * 128 * sizeof(float));
   p.total = o;
-  const long long rt = std::max(cdiv(I, 64), cdiv(H, 128));
-  p.max_tiles = (std::min<long long>(E, S) + S / p.bmax + 1) * rt;
+  p.max_chunks = std::min<long long>(E, S) + S / p.bmax + 1;
   return p;
 }
 }  // namespace
@@ -462,9 +565,7 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
   bool tc = dtype != SIMSD_F32 && H >= 64 && I >= 64 && (H % 8) == 0 && (I % 8) == 0 && al(w_gate) && al(w_up) &&
             al(w_down) && (ldg_e % 8) == 0 && (ldg_i % 8) == 0 && (ldd_e % 8) == 0 && (ldd_h % 8) == 0 &&
             ldg_i >= H && ldd_h >= I;
-  const MoePlan pl = plan_moe(T, k, E, H, I, dtype, sm_count_of(dev), tc);
-  if (tc && pl.max_tiles > WS_MAX_COUNTERS) tc = false;
-  const MoePlan plan = tc ? pl : plan_moe(T, k, E, H, I, dtype, sm_count_of(dev), false);
+  const MoePlan plan = plan_moe(T, k, E, H, I, dtype, sm_count_of(dev), tc);
   if (workspace_bytes < plan.total) return SIMSD_ERR_WORKSPACE;
 
   char* ws = reinterpret_cast<char*>(workspace);
@@ -501,7 +602,7 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
     a.out = hbuf;
     a.ld_out = I;
     a.partials = reinterpret_cast<float*>(ws + plan.off_part);
-    a.tile_counters = reinterpret_cast<int*>(ws);
+    a.tables = reinterpret_cast<int*>(ws + plan.off_tables);
     a.err = err;
     a.group_counts = counts;
     a.num_groups = E;
@@ -511,8 +612,8 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
     a.silu = 1;
     a.three_d = 1;
     a.is_bf16 = dtype == SIMSD_BF16 ? 1 : 0;
-    a.max_tiles = WS_MAX_COUNTERS;
     rc = launch_tc(plan.bmax, a, plan.grid, s, dev);
+    if (rc == SIMSD_OK) rc = launch_fixup(plan.bmax, fixup_args(a, plan.grid), plan.max_chunks * a.row_tiles, s);
     if (rc != SIMSD_OK) return rc;
     // down: ys[row, h] = hbuf[row] . w_down[e, h]
     TcGemmArgs d;
@@ -529,7 +630,7 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
     d.out = ys;
     d.ld_out = H;
     d.partials = a.partials;
-    d.tile_counters = a.tile_counters;
+    d.tables = a.tables;
     d.err = err;
     d.group_counts = counts;
     d.num_groups = E;
@@ -539,8 +640,8 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
     d.silu = 0;
     d.three_d = 1;
     d.is_bf16 = a.is_bf16;
-    d.max_tiles = WS_MAX_COUNTERS;
     rc = launch_tc(plan.bmax, d, plan.grid, s, dev);
+    if (rc == SIMSD_OK) rc = launch_fixup(plan.bmax, fixup_args(d, plan.grid), plan.max_chunks * d.row_tiles, s);
     if (rc != SIMSD_OK) return rc;
   } else {
     const long long max_chunks = std::min<long long>(E, S) + S / SIMT_ROWS + 1;

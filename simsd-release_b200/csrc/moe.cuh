@@ -105,8 +105,8 @@ __device__ __forceinline__ void load8(const void* base, long long idx, int dtype
 }
 
 __global__ void __launch_bounds__(ROUTE_WARPS * 32) route_kernel(const RouteArgs p) {
-  griddep_wait();
   griddep_launch_dependents();
+  griddep_wait();
   extern __shared__ float sh[];
   float* s_score = sh;                          // [ROUTE_TOK][E]
   float* s_choice = sh + ROUTE_TOK * p.E;       // [ROUTE_TOK][E]
@@ -239,8 +239,8 @@ struct AlignArgs {
 constexpr int ALIGN_THREADS = 1024;
 
 __global__ void __launch_bounds__(ALIGN_THREADS, 1) align_kernel(const AlignArgs p) {
-  griddep_wait();
   griddep_launch_dependents();
+  griddep_wait();
   extern __shared__ int ash[];
   int* hist = ash;                       // [32][E]
   int* s_off = ash + 32 * p.E;           // [E+1]
@@ -366,8 +366,8 @@ __global__ void __launch_bounds__(ALIGN_THREADS, 1) align_kernel(const AlignArgs
 // xs[row, :] = x[sorted_slots[row] / k, :]
 __global__ void gather_rows_kernel(const void* x, long long ldx, const int* sorted_slots, void* xs, long long ldxs,
                                    int S, int k, int H, int esz) {
-  griddep_wait();
   griddep_launch_dependents();
+  griddep_wait();
   const int row = blockIdx.x;
   if (row >= S) return;
   const int slot = sorted_slots[row];
@@ -392,8 +392,8 @@ __global__ void gather_rows_kernel(const void* x, long long ldx, const int* sort
 // x.dtype addition `moe_out + shared_out`.
 __global__ void combine_kernel(const void* ys, long long ldys, const int* slot_to_row, const float* w, void* out,
                                long long ld_out, const void* add, long long ld_add, int T, int k, int H, int dtype) {
-  griddep_wait();
   griddep_launch_dependents();
+  griddep_wait();
   const int t = blockIdx.x;
   if (t >= T) return;
   for (int h = threadIdx.x; h < H; h += blockDim.x) {

@@ -34,8 +34,8 @@ struct SimtGemmArgs {
 };
 
 __global__ void __launch_bounds__(SIMT_WARPS * 32) simt_gemm_kernel(const SimtGemmArgs p) {
-  griddep_wait();
   griddep_launch_dependents();
+  griddep_wait();
   __shared__ int s_row_prefix[1025];
   __shared__ int s_chunk_prefix[1025];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

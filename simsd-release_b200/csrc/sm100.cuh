@@ -205,6 +205,9 @@ __host__ __device__ __forceinline__ uint32_t make_idesc_f16(int is_bf16, int M, 
 // griddep_wait() blocks until that kernel has completed and its writes are
 // visible (a no-op when the launch had no such dependency), and
 // griddep_launch_dependents() lets the next kernel begin launching early.
+// Every kernel here triggers first and waits second: the next kernel's own
+// griddep_wait() still orders it after this one (completion is transitive),
+// so the early trigger only lets its set-up and weight prefetch overlap.
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

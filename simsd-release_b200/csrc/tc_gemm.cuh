@@ -15,13 +15,14 @@
 //
 // Work split (stream-K): the iteration space (tile, k-block) is cut into
 // gridDim.x contiguous, equal ranges, one per CTA, so every SM streams the same
-// number of weight bytes whatever the shape.  A tile whose K range is spread
-// over several CTAs is reduced deterministically: each CTA writes its fp32
-// partial into a fixed slot, bumps the tile's counter, and whichever CTA comes
-// last sums all slots in K order (never in arrival order) and runs the
-// epilogue.  No CTA ever waits on another, and the sum order depends only on
-// the shape and grid size, so results are bit-identical across calls and
-// graph replays (the property tested at kernels/thin_linear_fused_test.py:130-151).
+// number of weight bytes whatever the shape.  A tile that lies inside one CTA's
+// range is finished by that CTA's epilogue.  A tile whose K range is spread over
+// several CTAs is reduced deterministically by tc_fixup_kernel, launched right
+// after: each CTA parks its fp32 partial in a fixed slot, and the fixup sums the
+// slots of each split tile in K order, every tile in parallel.  No CTA waits on
+// another and no atomics are involved, and the sum order depends only on the
+// shape and grid size, so results are bit-identical across calls and graph
+// replays (the property tested at kernels/thin_linear_fused_test.py:130-151).
 //
 // Grouped mode: B rows are grouped (MoE experts, rows sorted by expert);
 // group g owns rows [offset_g, offset_g + count_g) of B and of the output, and
@@ -41,9 +42,9 @@ constexpr int TC_BOX_ROWS = 16;            // activation rows per TMA box
 constexpr int TC_BOX_BYTES = TC_BOX_ROWS * 128;
 constexpr int TC_MAX_GROUPS = 1024;
 constexpr int TC_MAX_GRID = 1024;          // CTAs per launch (segments per tile <= this)
-constexpr int WS_COUNTER_BYTES = 256 * 1024;          // head of every workspace
+constexpr int WS_COUNTER_BYTES = 256 * 1024;          // head of every workspace (reserved)
 constexpr int WS_ERR_OFFSET = WS_COUNTER_BYTES - 64;  // device error word
-constexpr int WS_MAX_COUNTERS = (WS_COUNTER_BYTES - 256) / 4;
+constexpr int TC_TABLE_INTS = 2 * (TC_MAX_GROUPS + 1);
 
 struct alignas(64) TcGemmArgs {
   CUtensorMap tmA0;          // weights (gate weights in SiLU-mul mode)
@@ -52,7 +53,7 @@ struct alignas(64) TcGemmArgs {
   void* out;                 // output, row stride ld_out elements
   const void* bias;          // [rows_out] or nullptr (single mode only)
   float* partials;           // [2 * gridDim.x][128 weight rows][BMAX activation rows] fp32
-  int* tile_counters;        // [max_tiles], zero on entry and on exit
+  int* tables;               // grouped mode: row and chunk prefixes for tc_fixup_kernel
   int* err;                  // device error word
   const int* group_counts;   // grouped mode: rows per group; nullptr = single mode
   long long ld_out;
@@ -64,21 +65,30 @@ struct alignas(64) TcGemmArgs {
   int silu;
   int three_d;
   int is_bf16;
-  int max_tiles;
   int pdl;                   // launched as a programmatic dependent (see griddep_wait)
+  unsigned long long* trace; // optional: 8 %globaltimer stamps per CTA (diagnostics)
 };
 
-template <int BMAX>
+// KS = 64-wide K atoms per ring stage: each stage reads KS*128 contiguous bytes
+// of every weight row it covers, which keeps HBM pages open for longer runs.
+// RING_KB bounds the ring: 196 KB gives one CTA per SM the deepest ring; 96 KB
+// lets the next launch's CTA share the SM (programmatic dependent launch
+// then overlaps its weight prefetch with this kernel's tail).
+template <int BMAX, int KS, int RING_KB = 196>
 struct TcConfig {
-  static constexpr int B_BYTES = BMAX * 128;
-  static constexpr int STAGE_BYTES = TC_A_BYTES + B_BYTES;
-  static constexpr int STAGES_RAW = (196 * 1024) / STAGE_BYTES;
+  static constexpr int A_ATOM = TC_A_BYTES;
+  static constexpr int B_ATOM = BMAX * 128;
+  static constexpr int A_STAGE = KS * A_ATOM;
+  static constexpr int B_STAGE = KS * B_ATOM;
+  static constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
+  static constexpr int STAGES_RAW = (RING_KB * 1024) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 10 ? 10 : STAGES_RAW;
   static constexpr int TMEM_COLS = (2 * BMAX) < 32 ? 32 : 2 * BMAX;
   // tail: barriers (2*STAGES + 5) x 8, misc ints 16, prefixes 2 x (MAX_GROUPS+1), xbuf 64x16 fp32
   static constexpr int TAIL_BYTES =
-      (2 * STAGES + 5) * 8 + 64 + 2 * (TC_MAX_GROUPS + 1) * 4 + 16 + 64 * 16 * 4 + TC_MAX_GRID * 4;
+      (2 * STAGES + 5) * 8 + 64 + 2 * (TC_MAX_GROUPS + 1) * 4 + 16 + 64 * 16 * 4;
   static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + TAIL_BYTES;
+  static_assert(STAGES >= 2, "ring needs two stages");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
@@ -122,15 +132,15 @@ __device__ __forceinline__ long long sk_owner(long long i, long long iters, long
   return ((i + 1) * G + iters - 1) / iters - 1;
 }
 
-template <int BMAX>
+template <int BMAX, int KS, int RING_KB>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcGemmArgs p) {
-  using Cfg = TcConfig<BMAX>;
+  using Cfg = TcConfig<BMAX, KS, RING_KB>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * TC_A_BYTES;
-  uint8_t* tail = sB + STAGES * Cfg::B_BYTES;
+  uint8_t* sB = smem + STAGES * Cfg::A_STAGE;
+  uint8_t* tail = sB + STAGES * Cfg::B_STAGE;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(tail);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* accf_bar = empty_bar + STAGES;  // [2]
@@ -139,16 +149,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
   int* misc = reinterpret_cast<int*>(drain_bar + 1);  // 16 ints
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc);
   volatile int* abort_flag = misc + 1;
-  volatile int* sh_last = misc + 2;
   int* sh_total_chunks = misc + 3;
   int* row_prefix = misc + 16;                       // [num_groups + 1]
   int* chunk_prefix = row_prefix + (TC_MAX_GROUPS + 1);
   float* xbuf = reinterpret_cast<float*>(chunk_prefix + (TC_MAX_GROUPS + 1) + 4);  // [16][64]
-  int* seg_slot = reinterpret_cast<int*>(xbuf + 16 * 64);                          // [TC_MAX_GRID]
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
+  if (p.trace && tid == 0) p.trace[blockIdx.x * 8 + 0] = globaltimer_ns();
 
   // ---- set-up: barriers, TMEM, group tables
   if (tid == 0) {
@@ -162,7 +171,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     }
     mbar_init(smem_u32(drain_bar), 1);
     *abort_flag = 0;
-    *sh_last = 0;
     fence_mbar_init();
   }
   if (warp == 4 && lane == 0) {
@@ -211,6 +219,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     tc_fence_before();
     __syncthreads();
     total_tiles = (long long)(*sh_total_chunks) * p.row_tiles;
+    if (blockIdx.x == 0 && p.tables != nullptr)
+      for (int g = tid; g <= G; g += TC_THREADS) {
+        p.tables[g] = row_prefix[g];
+        p.tables[TC_MAX_GROUPS + 1 + g] = chunk_prefix[g];
+      }
   } else {
     tc_fence_before();
     __syncthreads();
@@ -218,6 +231,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
   }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (p.trace && tid == 0) p.trace[blockIdx.x * 8 + 1] = globaltimer_ns();
 
   // Partition over G = min(gridDim.x, iters) CTAs so that every partition is
   // non-empty (the tile count is data-dependent in grouped mode); CTAs beyond
@@ -246,15 +260,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
       // writes memory (MMA, epilogue, fixup) sits behind those loads.
       bool dep_ready = !(p.pdl && p.group_counts == nullptr);
       int npend = 0;
+      bool traced_first = false;
       uint32_t pend_dst[Cfg::STAGES], pend_bar[Cfg::STAGES];
-      int pend_k0[Cfg::STAGES], pend_row0[Cfg::STAGES], pend_nb[Cfg::STAGES];
+      int pend_k0[Cfg::STAGES], pend_na[Cfg::STAGES], pend_row0[Cfg::STAGES], pend_nb[Cfg::STAGES];
       auto flush_pending = [&]() {
         griddep_wait();
         dep_ready = true;
         for (int q = 0; q < npend; ++q)
-          for (int b = 0; b < pend_nb[q]; ++b)
-            tma_load_2d(pend_dst[q] + b * TC_BOX_BYTES, &p.tmB, pend_bar[q], pend_k0[q],
-                        pend_row0[q] + b * TC_BOX_ROWS, pol_x);
+          for (int at = 0; at < pend_na[q]; ++at)
+            for (int b = 0; b < pend_nb[q]; ++b)
+              tma_load_2d(pend_dst[q] + at * Cfg::B_ATOM + b * TC_BOX_BYTES, &p.tmB, pend_bar[q],
+                          pend_k0[q] + at * 64, pend_row0[q] + b * TC_BOX_ROWS, pol_x);
         npend = 0;
       };
       for (long long it = it_begin; ok && it < it_end;) {
@@ -263,37 +279,44 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         const int kb1 = (int)min(kb, it_end - tile * kb);
         const TileInfo ti = decode_tile<BMAX>(tile, p, row_prefix, chunk_prefix);
         const int nb = (ti.nrows + TC_BOX_ROWS - 1) / TC_BOX_ROWS;
-        for (int k = kb0; k < kb1; ++k) {
+        for (int k = kb0; k < kb1; k += KS) {
+          const int na = min(KS, kb1 - k);
           if (!dep_ready && npend == STAGES) flush_pending();
           if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, abort_flag, p.err)) { ok = false; break; }
           const uint32_t fb = smem_u32(&full_bar[stage]);
-          mbar_arrive_expect_tx(fb, TC_A_BYTES + nb * TC_BOX_BYTES);
+          mbar_arrive_expect_tx(fb, na * (TC_A_BYTES + nb * TC_BOX_BYTES));
           issued_mask |= 1u << stage;
           last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
-          const uint32_t a_dst = smem_u32(sA + stage * TC_A_BYTES);
-          const int k0 = k * 64;
-          if (p.silu) {
-            const int r0 = ti.rtile * 64;
-            if (p.three_d) {
-              tma_load_3d(a_dst, &p.tmA0, fb, k0, r0, ti.group, pol_w);
-              tma_load_3d(a_dst + 8192, &p.tmA1, fb, k0, r0, ti.group, pol_w);
+          const uint32_t b_dst = smem_u32(sB + stage * Cfg::B_STAGE);
+          for (int at = 0; at < na; ++at) {
+            const uint32_t a_dst = smem_u32(sA + stage * Cfg::A_STAGE + at * Cfg::A_ATOM);
+            const int k0 = (k + at) * 64;
+            if (p.silu) {
+              const int r0 = ti.rtile * 64;
+              if (p.three_d) {
+                tma_load_3d(a_dst, &p.tmA0, fb, k0, r0, ti.group, pol_w);
+                tma_load_3d(a_dst + 8192, &p.tmA1, fb, k0, r0, ti.group, pol_w);
+              } else {
+                tma_load_2d(a_dst, &p.tmA0, fb, k0, r0, pol_w);
+                tma_load_2d(a_dst + 8192, &p.tmA1, fb, k0, r0, pol_w);
+              }
             } else {
-              tma_load_2d(a_dst, &p.tmA0, fb, k0, r0, pol_w);
-              tma_load_2d(a_dst + 8192, &p.tmA1, fb, k0, r0, pol_w);
+              const int r0 = ti.rtile * 128;
+              if (p.three_d) tma_load_3d(a_dst, &p.tmA0, fb, k0, r0, ti.group, pol_w);
+              else tma_load_2d(a_dst, &p.tmA0, fb, k0, r0, pol_w);
             }
-          } else {
-            const int r0 = ti.rtile * 128;
-            if (p.three_d) tma_load_3d(a_dst, &p.tmA0, fb, k0, r0, ti.group, pol_w);
-            else tma_load_2d(a_dst, &p.tmA0, fb, k0, r0, pol_w);
+            if (dep_ready) {
+              for (int b = 0; b < nb; ++b)
+                tma_load_2d(b_dst + at * Cfg::B_ATOM + b * TC_BOX_BYTES, &p.tmB, fb, k0, ti.row0 + b * TC_BOX_ROWS,
+                            pol_x);
+            }
           }
-          const uint32_t b_dst = smem_u32(sB + stage * Cfg::B_BYTES);
-          if (dep_ready) {
-            for (int b = 0; b < nb; ++b)
-              tma_load_2d(b_dst + b * TC_BOX_BYTES, &p.tmB, fb, k0, ti.row0 + b * TC_BOX_ROWS, pol_x);
-          } else {
+          if (p.trace && !traced_first) { p.trace[blockIdx.x * 8 + 2] = globaltimer_ns(); traced_first = true; }
+          if (!dep_ready) {
             pend_dst[npend] = b_dst;
             pend_bar[npend] = fb;
-            pend_k0[npend] = k0;
+            pend_k0[npend] = k * 64;
+            pend_na[npend] = na;
             pend_row0[npend] = ti.row0;
             pend_nb[npend] = nb;
             ++npend;
@@ -305,6 +328,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
       // fewer iterations than ring stages, or aborting with weight-only stages
       // armed: their activation boxes still have to land
       if (!dep_ready) flush_pending();
+      if (p.trace) p.trace[blockIdx.x * 8 + 4] = globaltimer_ns();
       if (!ok) {
         // aborting: make sure no TMA copy is still landing in shared memory
         for (int s = 0; s < STAGES; ++s)
@@ -332,14 +356,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         if (!mbar_wait(smem_u32(&acce_bar[a]), aphase ^ 1, abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + a * BMAX;
-        for (int k = kb0; k < kb1; ++k) {
+        for (int k = kb0; k < kb1; k += KS) {
+          const int na = min(KS, kb1 - k);
           if (!mbar_wait(smem_u32(&full_bar[stage]), phase, abort_flag, p.err)) { ok = false; break; }
           tc_fence_after();
-          const uint64_t adesc = make_sw128_desc(smem_u32(sA + stage * TC_A_BYTES));
-          const uint64_t bdesc = make_sw128_desc(smem_u32(sB + stage * Cfg::B_BYTES));
+          if (p.trace && !issued_any) p.trace[blockIdx.x * 8 + 3] = globaltimer_ns();
+          for (int at = 0; at < na; ++at) {
+            const uint64_t adesc = make_sw128_desc(smem_u32(sA + stage * Cfg::A_STAGE + at * Cfg::A_ATOM));
+            const uint64_t bdesc = make_sw128_desc(smem_u32(sB + stage * Cfg::B_STAGE + at * Cfg::B_ATOM));
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            tc_mma_f16(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (k > kb0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < 4; ++kk)
+              tc_mma_f16(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (k > kb0 || at > 0 || kk > 0) ? 1u : 0u);
+          }
           issued_any = true;
           tc_commit(smem_u32(&empty_bar[stage]));
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -349,6 +377,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         ++acc_iter;
         it = tile * kb + kb1;
       }
+      if (p.trace) p.trace[blockIdx.x * 8 + 5] = globaltimer_ns();
       if (!ok && issued_any) {
         // aborting: wait for the MMAs already issued before TMEM is released
         tc_commit(smem_u32(drain_bar));
@@ -420,7 +449,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         }
       } else {
         // partial K range of this tile: park the fp32 partial in this CTA's slot,
-        // laid out [weight row][activation row] so the fixup reads 16-float runs
+        // laid out [weight row][activation row]; tc_fixup_kernel sums the slots
+        // of every split tile in K order right after this kernel.
         const long long first_tile_of_cta = it_begin / kb;
         const long long slot = 2 * c + (tile == first_tile_of_cta ? 0 : 1);
         float* P = p.partials + slot * (long long)(BMAX * 128) + (long long)row * BMAX;
@@ -434,131 +464,157 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         }
         tc_fence_before();
         mbar_arrive(smem_u32(&acce_bar[a]));
-        __threadfence();
-        named_bar_sync(1, 128);
-        const long long c_first = sk_owner(tile * kb, iters, G);
-        const long long c_last = sk_owner(tile * kb + kb - 1, iters, G);
-        if (row == 0) {
-          int last = 0;
-          if (tile < p.max_tiles) {
-            const int old = atomicAdd(&p.tile_counters[tile], 1);
-            last = (old == (int)(c_last - c_first));
-          } else {
-            atomicOr(p.err, SIMSD_DEV_ERR_BAD_INDEX);
-          }
-          *sh_last = last;
-        }
-        named_bar_sync(1, 128);
-        const int nseg = (int)(c_last - c_first + 1);
-        if (*sh_last) {
-          __threadfence();
-          // slot of every contributing CTA, in K order
-          for (int i = row; i < nseg; i += 128) {
-            const long long cc = c_first + i;
-            seg_slot[i] = (int)(2 * cc + ((tile == sk_start(cc, iters, G) / kb) ? 0 : 1));
-          }
-          named_bar_sync(1, 128);
-          // Sum the segments in K order.  All loads of a batch of segments are
-          // issued before any add, so the batch costs one L2 round trip.
-          if (!p.silu) {
-            const int col = out_col0 + row;
-            const float bv = (p.bias && col < p.rows_out) ? load_f(p.bias, col, p.is_bf16 ? 0 : 1) : 0.0f;
-            for (int ch = 0; ch < nb; ++ch) {
-              float acc[16];
-#pragma unroll
-              for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
-              for (int i0 = 0; i0 < nseg; i0 += 4) {
-                float4 buf[4][4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                  if (i0 + q < nseg) {
-                    const float4* src = reinterpret_cast<const float4*>(
-                        p.partials + (long long)seg_slot[i0 + q] * (BMAX * 128) + (long long)row * BMAX + ch * 16);
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) buf[q][u] = __ldcg(src + u);
-                  }
-                }
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                  if (i0 + q < nseg) {
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                      acc[4 * u] = __fadd_rn(acc[4 * u], buf[q][u].x);
-                      acc[4 * u + 1] = __fadd_rn(acc[4 * u + 1], buf[q][u].y);
-                      acc[4 * u + 2] = __fadd_rn(acc[4 * u + 2], buf[q][u].z);
-                      acc[4 * u + 3] = __fadd_rn(acc[4 * u + 3], buf[q][u].w);
-                    }
-                  }
-                }
-              }
-              if (col < p.rows_out) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                  const int t = ch * 16 + j;
-                  if (t < ti.nrows)
-                    store_f(outp, (long long)(ti.row0 + t) * p.ld_out + col, __fadd_rn(acc[j], bv), p.is_bf16 ? 0 : 1);
-                }
-              }
-            }
-          } else {
-            const int i = row & 63;
-            const int col = out_col0 + i;
-            for (int ch = row >> 6; ch < nb; ch += 2) {
-              float ag[16], au[16];
-#pragma unroll
-              for (int j = 0; j < 16; ++j) { ag[j] = 0.0f; au[j] = 0.0f; }
-              for (int i0 = 0; i0 < nseg; i0 += 2) {
-                float4 bg[2][4], bu[2][4];
-#pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                  if (i0 + q < nseg) {
-                    const float* base = p.partials + (long long)seg_slot[i0 + q] * (BMAX * 128) + ch * 16;
-                    const float4* sg = reinterpret_cast<const float4*>(base + (long long)i * BMAX);
-                    const float4* su = reinterpret_cast<const float4*>(base + (long long)(64 + i) * BMAX);
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) { bg[q][u] = __ldcg(sg + u); bu[q][u] = __ldcg(su + u); }
-                  }
-                }
-#pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                  if (i0 + q < nseg) {
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                      ag[4 * u] = __fadd_rn(ag[4 * u], bg[q][u].x);
-                      ag[4 * u + 1] = __fadd_rn(ag[4 * u + 1], bg[q][u].y);
-                      ag[4 * u + 2] = __fadd_rn(ag[4 * u + 2], bg[q][u].z);
-                      ag[4 * u + 3] = __fadd_rn(ag[4 * u + 3], bg[q][u].w);
-                      au[4 * u] = __fadd_rn(au[4 * u], bu[q][u].x);
-                      au[4 * u + 1] = __fadd_rn(au[4 * u + 1], bu[q][u].y);
-                      au[4 * u + 2] = __fadd_rn(au[4 * u + 2], bu[q][u].z);
-                      au[4 * u + 3] = __fadd_rn(au[4 * u + 3], bu[q][u].w);
-                    }
-                  }
-                }
-              }
-              if (col < p.rows_out) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                  const int t = ch * 16 + j;
-                  if (t < ti.nrows)
-                    store_f(outp, (long long)(ti.row0 + t) * p.ld_out + col, silu_mul(ag[j], au[j]), p.is_bf16 ? 0 : 1);
-                }
-              }
-            }
-          }
-          if (row == 0) p.tile_counters[tile] = 0;
-        }
-        named_bar_sync(1, 128);
       }
       ++acc_iter;
       it = tile * kb + kb1;
     }
   }
 
+  if (p.trace && tid == 0) {
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    p.trace[blockIdx.x * 8 + 6] = smid;
+  }
   __syncthreads();
   if (warp == 5) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+  if (p.trace && tid == 0) p.trace[blockIdx.x * 8 + 7] = globaltimer_ns();
+}
+
+// Deterministic split-K reduction for tc_gemm_kernel: block (tile, chunk) sums
+// the fp32 partial slots of one split tile in K order for 16 activation rows
+// and applies the epilogue (bias, or SiLU*mul across the gate/up halves).
+// Whole tiles were already written by the GEMM.  The grid is sized for the
+// largest possible tile count; blocks past the actual count return at once.
+struct TcFixupArgs {
+  const float* partials;
+  void* out;
+  const void* bias;
+  const int* group_counts;   // grouped mode (tables then come from `tables`)
+  const int* tables;
+  long long ld_out;
+  int single_rows, num_groups, kb, rows_out, row_tiles, silu, is_bf16, grid;
+};
+
+template <int BMAX>
+__global__ void __launch_bounds__(128) tc_fixup_kernel(const TcFixupArgs p) {
+  griddep_launch_dependents();
+  griddep_wait();
+  __shared__ int s_total;
+  const int row = threadIdx.x;
+  const long long tile = blockIdx.x;
+  const int ch = blockIdx.y;
+  const int* row_prefix = p.tables;
+  const int* chunk_prefix = p.tables ? p.tables + TC_MAX_GROUPS + 1 : nullptr;
+  long long total_tiles;
+  if (p.group_counts != nullptr) {
+    if (row == 0) s_total = chunk_prefix[p.num_groups];
+    __syncthreads();
+    total_tiles = (long long)s_total * p.row_tiles;
+  } else {
+    total_tiles = (long long)((p.single_rows + BMAX - 1) / BMAX) * p.row_tiles;
+  }
+  if (tile >= total_tiles) return;
+  const long long kb = p.kb;
+  const long long iters = total_tiles * kb;
+  const long long G = min((long long)p.grid, iters);
+  const long long c_first = sk_owner(tile * kb, iters, G);
+  const long long c_last = sk_owner(tile * kb + kb - 1, iters, G);
+  if (c_first == c_last) return;                       // whole tile: written by the GEMM
+  TcGemmArgs ta;                                       // decode_tile reads only these fields
+  ta.group_counts = p.group_counts;
+  ta.row_tiles = p.row_tiles;
+  ta.single_rows = p.single_rows;
+  ta.num_groups = p.num_groups;
+  const TileInfo ti = decode_tile<BMAX>(tile, ta, row_prefix, chunk_prefix);
+  if (ch * 16 >= ti.nrows) return;
+  const int nseg = (int)(c_last - c_first + 1);
+  const int odt = p.is_bf16 ? 0 : 1;
+  char* outp = reinterpret_cast<char*>(p.out);
+  auto slot_of = [&](int i) -> long long {
+    const long long cc = c_first + i;
+    return 2 * cc + ((tile == sk_start(cc, iters, G) / kb) ? 0 : 1);
+  };
+  if (!p.silu) {
+    const int col = ti.rtile * 128 + row;
+    float acc[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
+    for (int i0 = 0; i0 < nseg; i0 += 8) {
+      float4 buf[8][4];
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (i0 + q < nseg) {
+          const float4* src = reinterpret_cast<const float4*>(
+              p.partials + slot_of(i0 + q) * (BMAX * 128) + (long long)row * BMAX + ch * 16);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) buf[q][u] = __ldcg(src + u);
+        }
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (i0 + q < nseg) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            acc[4 * u] = __fadd_rn(acc[4 * u], buf[q][u].x);
+            acc[4 * u + 1] = __fadd_rn(acc[4 * u + 1], buf[q][u].y);
+            acc[4 * u + 2] = __fadd_rn(acc[4 * u + 2], buf[q][u].z);
+            acc[4 * u + 3] = __fadd_rn(acc[4 * u + 3], buf[q][u].w);
+          }
+        }
+    }
+    if (col < p.rows_out) {
+      const float bv = p.bias ? load_f(p.bias, col, odt) : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int t = ch * 16 + j;
+        if (t < ti.nrows) store_f(outp, (long long)(ti.row0 + t) * p.ld_out + col, __fadd_rn(acc[j], bv), odt);
+      }
+    }
+  } else {
+    // 64 gate rows and their 64 up rows; threads 0-63 take activation rows
+    // 0-7 of the chunk, threads 64-127 rows 8-15
+    const int i = row & 63;
+    const int half = row >> 6;
+    const int col = ti.rtile * 64 + i;
+    float ag[8], au[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { ag[j] = 0.0f; au[j] = 0.0f; }
+    for (int i0 = 0; i0 < nseg; i0 += 4) {
+      float4 bg[4][2], bu[4][2];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (i0 + q < nseg) {
+          const float* base = p.partials + slot_of(i0 + q) * (BMAX * 128) + ch * 16 + half * 8;
+          const float4* sg = reinterpret_cast<const float4*>(base + (long long)i * BMAX);
+          const float4* su = reinterpret_cast<const float4*>(base + (long long)(64 + i) * BMAX);
+#pragma unroll
+          for (int u = 0; u < 2; ++u) { bg[q][u] = __ldcg(sg + u); bu[q][u] = __ldcg(su + u); }
+        }
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (i0 + q < nseg) {
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            ag[4 * u] = __fadd_rn(ag[4 * u], bg[q][u].x);
+            ag[4 * u + 1] = __fadd_rn(ag[4 * u + 1], bg[q][u].y);
+            ag[4 * u + 2] = __fadd_rn(ag[4 * u + 2], bg[q][u].z);
+            ag[4 * u + 3] = __fadd_rn(ag[4 * u + 3], bg[q][u].w);
+            au[4 * u] = __fadd_rn(au[4 * u], bu[q][u].x);
+            au[4 * u + 1] = __fadd_rn(au[4 * u + 1], bu[q][u].y);
+            au[4 * u + 2] = __fadd_rn(au[4 * u + 2], bu[q][u].z);
+            au[4 * u + 3] = __fadd_rn(au[4 * u + 3], bu[q][u].w);
+          }
+        }
+    }
+    if (col < p.rows_out) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int t = ch * 16 + half * 8 + j;
+        if (t < ti.nrows) store_f(outp, (long long)(ti.row0 + t) * p.ld_out + col, silu_mul(ag[j], au[j]), odt);
+      }
+    }
   }
 }
 
