@@ -38,6 +38,7 @@ extern "C" {
 #define SIMSD_ERR_ALIGN -5        /* pointer or stride unusable by the requested path       */
 #define SIMSD_ERR_DEVICE -6       /* no usable CUDA device / driver entry point             */
 #define SIMSD_ERR_UNSUPPORTED -7  /* valid request outside this build's limits              */
+#define SIMSD_ERR_SCRATCH_LIMIT -8 /* simsd_thin_linear_noalloc: needs more than its static scratch */
 
 /* ---- element types */
 #define SIMSD_BF16 0
@@ -128,6 +129,31 @@ int simsd_thin_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w
                       int64_t ldw_k, const void* w_up, const void* bias, void* y, int64_t ldy_m, int M,
                       int N, int K, int dtype, int epilogue, int split, int path, void* workspace,
                       size_t workspace_bytes, void* stream);
+
+/*
+ * simsd_thin_linear without a workspace: the same computation (and the same
+ * arguments minus split, path and workspace), for callers that cannot allocate
+ * device memory or own a scratch buffer - a plugin host that hands out only the
+ * tensors of the call and forbids allocation from plugins, code running inside
+ * an allocator's own callback, or a foreign-language binding that has no CUDA
+ * allocator to draw from.  No counterpart in the reference (its Triton kernel
+ * allocates a staging buffer through torch).
+ *
+ * The split-K partials live in a fixed 8 MiB device array inside this library
+ * (held by every GPU that loads it until the process exits); the call itself
+ * allocates nothing and frees nothing.  A shape whose partials do not fit is
+ * rejected with SIMSD_ERR_SCRATCH_LIMIT (on a 148-SM B200 this admits M <= 32
+ * for every N and K; layouts that take the CUDA-core path need no partials).
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current: make that first call before
+ * any stream capture.  All calls share the one array: calls that may overlap on
+ * the GPU (different streams, or different host threads) race and must be
+ * serialised by the caller.  Each call clears the array's error word first.
+ */
+int simsd_thin_linear_noalloc(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w,
+                              int64_t ldw_n, int64_t ldw_k, const void* w_up, const void* bias,
+                              void* y, int64_t ldy_m, int M, int N, int K, int dtype,
+                              int epilogue, void* stream);
 
 /*
  * MoE router: logits = x wr^T (fp32, fixed summation order), score = sigmoid(logits),

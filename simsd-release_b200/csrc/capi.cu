@@ -267,6 +267,29 @@ int thin_tc_possible(const void* x, long long ldx_m, long long ldx_k, const void
   return 1;
 }
 
+// ---------------------------------------------------------------- static scratch
+// Scratch of simsd_thin_linear_noalloc: a fixed device array that exists on every
+// GPU that loads this library, from module load until the process exits, so that
+// entry point never allocates.  Bytes [0, 256) hold its error word; the rest holds
+// the split-K partial slots.  Its name is only a host-side handle: the device
+// address comes from cudaGetSymbolAddress, once per device.
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;   // 8 MiB
+constexpr size_t kNoAllocHeader = 256;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+void* g_noalloc_ptr[kMaxDev];
+
+// Device address of g_noalloc_scratch on the current device `dev` (resolved on
+// the first call there, with `dev` current; nullptr if the runtime refuses).
+void* noalloc_scratch(int dev) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) return nullptr;
+    g_noalloc_ptr[dev] = ptr;
+  }
+  return g_noalloc_ptr[dev];
+}
+
 }  // namespace
 
 // ======================================================================== API
@@ -284,6 +307,8 @@ const char* simsd_status_string(int s) {
     case SIMSD_ERR_ALIGN: return "pointer or stride not usable by this path";
     case SIMSD_ERR_DEVICE: return "no usable CUDA device";
     case SIMSD_ERR_UNSUPPORTED: return "outside this build's limits";
+    case SIMSD_ERR_SCRATCH_LIMIT:
+      return "request needs more scratch than simsd_thin_linear_noalloc's fixed static buffer";
   }
   return "unknown status";
 }
@@ -418,6 +443,84 @@ int simsd_thin_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w
   if (gy > 65535) return SIMSD_ERR_UNSUPPORTED;
   dim3 grid((unsigned)cdiv(N, SIMT_WARPS), (unsigned)gy);
   return launch(simt_gemm_kernel, grid, dim3(SIMT_WARPS * 32), 0, s, a);
+}
+
+int simsd_thin_linear_noalloc(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w, int64_t ldw_n,
+                              int64_t ldw_k, const void* w_up, const void* bias, void* y, int64_t ldy_m, int M,
+                              int N, int K, int dtype, int epilogue, void* stream) {
+  if (M < 1 || N < 1 || K < 1) return SIMSD_ERR_SHAPE;
+  if (dtype != SIMSD_BF16 && dtype != SIMSD_F16 && dtype != SIMSD_F32) return SIMSD_ERR_DTYPE;
+  if (epilogue != SIMSD_EPI_NONE && epilogue != SIMSD_EPI_SILU_MUL) return SIMSD_ERR_UNSUPPORTED;
+  const bool silu = epilogue == SIMSD_EPI_SILU_MUL;
+  if (silu && (w_up == nullptr || bias != nullptr)) return SIMSD_ERR_UNSUPPORTED;
+  if (x == nullptr || w == nullptr || y == nullptr) return SIMSD_ERR_SHAPE;
+  const int dev = current_device();
+  if (dev < 0) return SIMSD_ERR_DEVICE;
+  char* scratch = reinterpret_cast<char*>(noalloc_scratch(dev));
+  if (scratch == nullptr) return SIMSD_ERR_DEVICE;
+  cudaStream_t s = (cudaStream_t)stream;
+  int* err = reinterpret_cast<int*>(scratch);
+  // the error word is the only scratch that must start at zero for each call
+  if (cudaMemsetAsync(err, 0, sizeof(int), s) != cudaSuccess) return SIMSD_ERR_LAUNCH;
+
+  const bool tc_ok = thin_tc_possible(x, ldx_m, ldx_k, w, ldw_n, ldw_k, w_up, M, N, K, dtype) != 0;
+  if (tc_ok && K >= 64) {
+    if (ensure_encode() != SIMSD_OK) return SIMSD_ERR_DEVICE;
+    const ThinPlan pl = plan_thin(M, N, K, epilogue, 0, sm_count_of(dev));
+    const size_t part_bytes = (size_t)2 * pl.grid * pl.bmax * 128 * sizeof(float);
+    if (part_bytes > kNoAllocScratchBytes - kNoAllocHeader) return SIMSD_ERR_SCRATCH_LIMIT;
+    TcGemmArgs a;
+    memset(&a, 0, sizeof(a));
+    const long long lx = (M > 1) ? ldx_m : ((K * 2 + 15) / 16) * 8;
+    const long long lw = (N > 1) ? ldw_n : ((K * 2 + 15) / 16) * 8;
+    const uint64_t xd[2] = {(uint64_t)K, (uint64_t)M}, xs[1] = {(uint64_t)lx * 2};
+    const uint64_t wd[2] = {(uint64_t)K, (uint64_t)N}, wsb[1] = {(uint64_t)lw * 2};
+    int rc = encode_map(&a.tmB, x, dtype, 2, xd, xs, TC_BOX_ROWS);
+    if (rc == SIMSD_OK) rc = encode_map(&a.tmA0, w, dtype, 2, wd, wsb, silu ? 64 : 128);
+    if (rc == SIMSD_OK && silu) rc = encode_map(&a.tmA1, w_up, dtype, 2, wd, wsb, 64);
+    if (rc != SIMSD_OK) return rc;
+    a.out = y;
+    a.ld_out = ldy_m;
+    a.bias = bias;
+    a.partials = reinterpret_cast<float*>(scratch + kNoAllocHeader);
+    a.tables = nullptr;
+    a.err = err;
+    a.group_counts = nullptr;
+    a.num_groups = 1;
+    a.single_rows = M;
+    a.kb = pl.kb;
+    a.rows_out = N;
+    a.row_tiles = pl.row_tiles;
+    a.silu = silu ? 1 : 0;
+    a.three_d = 0;
+    a.is_bf16 = dtype == SIMSD_BF16 ? 1 : 0;
+    rc = launch_tc(pl.bmax, a, pl.grid, s, dev);
+    if (rc != SIMSD_OK || !any_split_tile(pl.tiles, pl.kb, pl.grid)) return rc;
+    return launch_fixup(pl.bmax, fixup_args(a, pl.grid), pl.tiles, s);
+  }
+  // layouts the tensor-core kernel cannot read need no scratch beyond the error word
+  SimtGemmArgs a;
+  memset(&a, 0, sizeof(a));
+  a.a = x;
+  a.w = w;
+  a.w_up = w_up;
+  a.bias = bias;
+  a.out = y;
+  a.err = err;
+  a.lda_m = ldx_m;
+  a.lda_k = ldx_k;
+  a.ldw_n = ldw_n;
+  a.ldw_k = ldw_k;
+  a.ld_out = ldy_m;
+  a.rows = M;
+  a.num_groups = 1;
+  a.N = N;
+  a.K = K;
+  a.dtype = dtype;
+  a.silu = silu ? 1 : 0;
+  const long long gy = cdiv(M, SIMT_ROWS);
+  if (gy > 65535) return SIMSD_ERR_UNSUPPORTED;
+  return launch(simt_gemm_kernel, dim3((unsigned)cdiv(N, SIMT_WARPS), (unsigned)gy), dim3(SIMT_WARPS * 32), 0, s, a);
 }
 
 // ---------------------------------------------------------------- MoE

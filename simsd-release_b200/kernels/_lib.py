@@ -23,6 +23,7 @@ SIMSD_ERR_LAUNCH = -4
 SIMSD_ERR_ALIGN = -5
 SIMSD_ERR_DEVICE = -6
 SIMSD_ERR_UNSUPPORTED = -7
+SIMSD_ERR_SCRATCH_LIMIT = -8
 
 SIMSD_BF16, SIMSD_F16, SIMSD_F32 = 0, 1, 2
 EPI_NONE, EPI_SILU_MUL = 0, 1
@@ -50,6 +51,7 @@ SIGNATURES: dict[str, tuple] = {
     "simsd_thin_linear_workspace_size": (_S, [_I, _I, _I, _I, _I, _I]),
     "simsd_thin_linear": (_I, [_P, _L, _L, _P, _L, _L, _P, _P, _P, _L, _I, _I, _I, _I, _I, _I, _I,
                                _P, _S, _P]),
+    "simsd_thin_linear_noalloc": (_I, [_P, _L, _L, _P, _L, _L, _P, _P, _P, _L, _I, _I, _I, _I, _I, _P]),
     "simsd_moe_route": (_I, [_P, _L, _I, _P, _L, _I, _P, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P]),
     "simsd_moe_align": (_I, [_P, _I, _I, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P]),
     "simsd_moe_workspace_size": (_S, [_I, _I, _I, _I, _I, _I]),
