@@ -343,6 +343,10 @@ def gpu_arm(args):
         line["per_launch"] = per
     clk_summary = clk.summary()
     line["clocks"] = clk_summary
+    if world == 1 and "verify" in args.workload:
+        line["verify"] = verify_bench(dev, args.steps)
+    if world == 1 and "moe" in args.workload:
+        line["moe"] = moe_bench(dev, args.steps, None if args.no_cpu_baseline else min(5.0, args.cpu_seconds))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     if rank == 0:
@@ -350,6 +354,171 @@ def gpu_arm(args):
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ MoE
+MOE = dict(H=2048, E=256, k=8, I=512, bias_std=0.1, Ts=(16, 64, 256, 1024))
+
+
+def moe_bytes_flops(T: int, n_active: int) -> tuple[int, int]:
+    """Algorithmic HBM bytes and flops of one MoE layer (router + routed + shared expert)."""
+    H, E, k, I = MOE["H"], MOE["E"], MOE["k"], MOE["I"]
+    b = n_active * 3 * H * I * 2 + 3 * H * I * 2 + E * H * 2 + 2 * T * H * 2 + T * k * 12
+    f = 2 * T * (k + 1) * 3 * H * I + 2 * T * E * H
+    return b, f
+
+
+def moe_bench(dev, steps: int, cpu_seconds: float | None) -> dict:
+    from kernels.moe_dispatch_fused import moe_layer, moe_route
+    H, E, k, I = MOE["H"], MOE["E"], MOE["k"], MOE["I"]
+    g = torch.Generator(device=dev).manual_seed(2024)
+    bf = torch.bfloat16
+    wr = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(bf)
+    bias = torch.randn(E, generator=g, device=dev) * MOE["bias_std"]
+    pools = [tuple((torch.randn(*sh, generator=g, device=dev) * 0.02).to(bf)
+                   for sh in ((E, I, H), (E, I, H), (E, H, I))) for _ in range(POOL)]
+    shared = tuple((torch.randn(*sh, generator=g, device=dev) * 0.02).to(bf) for sh in ((I, H), (I, H), (H, I)))
+    pk = peaks()
+    tc_peak = float(json.loads((REPO / "MEASURED_PEAKS.json").read_text())["bf16_tflops"]) * 1e12 \
+        if (REPO / "MEASURED_PEAKS.json").exists() else 1.59e15
+    out = {}
+    tot_b = tot_t = 0.0
+    with torch.inference_mode():
+        for T in MOE["Ts"]:
+            x = torch.randn(T, H, generator=g, device=dev).to(bf)
+            ids, _ = moe_route(x, wr, bias, k=k)
+            n_active = int(torch.unique(ids).numel())
+            for _ in range(3):
+                for p in pools:
+                    moe_layer(x, wr, bias, k, *p, shared=shared)
+            torch.cuda.synchronize()
+            graphs = []
+            for p in pools:
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr):
+                    moe_layer(x, wr, bias, k, *p, shared=shared)
+                graphs.append(gr)
+            for i in range(4):
+                graphs[i % POOL].replay()
+            torch.cuda.synchronize()
+            n = max(10, min(steps, 200))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(n):
+                graphs[i % POOL].replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / n
+            b, f = moe_bytes_flops(T, n_active)
+            roof_ms = max(b / (pk["hbm_gbs"] * 1e9), f / tc_peak) * 1e3
+            out[f"T{T}"] = {"ms": round(ms, 4), "gbs": round(b / ms / 1e6, 1), "n_active_experts": n_active,
+                            "frac_hbm_peak": round(b / ms / 1e6 / pk["hbm_gbs"], 4),
+                            "frac_roofline": round(roof_ms / ms, 4), "tflops": round(f / ms / 1e9, 2)}
+            tot_b += b
+            tot_t += ms
+            del graphs
+    res = {"workload": "MoE layer, BASELINE configs[2]: H=2048, E=256, top-8 sigmoid+bias(N(0,0.1)) router, "
+                       "I=512 SiLU*mul experts + 1 shared expert, bf16, CUDA-graph replay over 2 expert-weight "
+                       "pools (2 x 1.6 GB)",
+           "metric": "MoE layer HBM GB/s (algorithmic bytes: active experts + shared + router + activations)",
+           "value": round(tot_b / tot_t / 1e6, 1), "unit": "GB/s",
+           "frac_hbm_peak": round(tot_b / tot_t / 1e6 / pk["hbm_gbs"], 4), "per_T": out}
+    if cpu_seconds:
+        res["cpu_baseline"] = moe_cpu_baseline(cpu_seconds)
+    return res
+
+
+def moe_cpu_baseline(seconds: float) -> dict:
+    """The stock moe_infer path (oracle/torch_eager.py) on the host cores, T=64."""
+    from oracle.torch_eager import moe_layer as moe_layer_ref
+    torch.set_num_threads(os.cpu_count() or 1)
+    H, E, k, I = MOE["H"], MOE["E"], MOE["k"], MOE["I"]
+    g = torch.Generator().manual_seed(2024)
+    bf = torch.bfloat16
+    wr = (torch.randn(E, H, generator=g) * 0.02).to(bf)
+    bias = torch.randn(E, generator=g) * MOE["bias_std"]
+    wg, wu, wd = ((torch.randn(*sh, generator=g) * 0.02).to(bf) for sh in ((E, I, H), (E, I, H), (E, H, I)))
+    shared = tuple((torch.randn(*sh, generator=g) * 0.02).to(bf) for sh in ((I, H), (I, H), (H, I)))
+    T = 64
+    x = torch.randn(T, H, generator=g).to(bf)
+    with torch.inference_mode():
+        moe_layer_ref(x, wr, bias, k, wg, wu, wd, shared=shared)
+        n = 0
+        t0 = time.perf_counter()
+        while n < 2 or time.perf_counter() - t0 < seconds:
+            moe_layer_ref(x, wr, bias, k, wg, wu, wd, shared=shared)
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        ids, _ = __import__("oracle.torch_eager", fromlist=["route"]).route(x, wr, bias, k)
+    b, _ = moe_bytes_flops(T, int(torch.unique(ids).numel()))
+    return {"value": round(b / dt / 1e9, 2), "unit": "GB/s", "ms": round(dt * 1e3, 2),
+            "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"T=64 MoE layer, stock moe_infer restatement, {n} runs"}
+
+
+# ------------------------------------------------------------------ verify (BASELINE configs[3])
+def verify_bench(dev, steps: int) -> dict:
+    """Synthetic SDAR-8B verify forward: K=4 blocks x bl=4 over a 2048-token prefix.
+
+    tok/s = K*bl / forward latency (CUDA-graph replay of the 32-row window
+    forward through all 36 layers + lm_head).  Measured twice on the same
+    weights: the reference path (stock nn.Linear = cuBLAS) and ours
+    (fused_toggle with the fused gate/up, PDL).  Algorithmic bytes per forward:
+    every linear weight + lm_head + the embedding rows + the KV prefix.
+    """
+    from kernels import fused_toggle
+    from kernels.sdar_verify import SDAR_8B, SDARVerifyModel, VerifyHarness
+    s = SDAR_8B
+    K, BL, P = 4, 4, 2048
+    model = SDARVerifyModel.random_init(s, dev, seed=0)
+    g = torch.Generator().manual_seed(1)
+    prompt = torch.randint(0, s.vocab, (P,), generator=g).tolist()
+    drafts = [torch.randint(0, s.vocab, (BL,), generator=g).tolist() for _ in range(K)]
+    smaps = [torch.randperm(BL, generator=g).tolist() for _ in range(K)]
+    h = VerifyHarness(model, prompt, drafts, smaps, BL)
+    kv_bytes = s.layers * 2 * P * s.kv_heads * s.head_dim * 2
+    fwd_bytes = s.linear_params * 2 + s.vocab * s.hidden * 2 + kv_bytes
+    res = {"workload": "random-init SDAR-8B-shaped target (36 layers, H=4096, 32q/8kv x 128, MLP 12288, "
+                       "vocab 151936, bf16 N(0,0.02)), K=4 draft blocks x bl=4 (32 query rows) over a "
+                       "2048-token KV prefix of uniform random ids; CUDA-graph replay",
+           "unit": "tok/s", "bytes_per_forward": fwd_bytes}
+
+    def timed(label):
+        with torch.inference_mode():
+            for _ in range(3):
+                h.window_logits()
+            torch.cuda.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                out = h.window_logits()
+            for _ in range(3):
+                gr.replay()
+            torch.cuda.synchronize()
+            n = max(10, min(steps, 50))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(n):
+                gr.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / n
+            acc = h.accept(out, drafts)
+        del gr
+        res[label] = {"ms_per_forward": round(ms, 3), "tok_s": round(K * BL / (ms * 1e-3), 1),
+                      "weight_stream_gbs": round(fwd_bytes / ms / 1e6, 1),
+                      "accepted": [a[1] for a in acc]}
+
+    timed("reference_cublas")
+    fused_toggle.apply_to_model(model, True, fuse_gate_up=True)
+    fused_toggle.warmup(model, BL, extra_M=(2 * BL * K,))
+    timed("ours")
+    fused_toggle.apply_to_model(model, False)
+    res["value"] = res["ours"]["tok_s"]
+    res["speedup_vs_cublas"] = round(res["reference_cublas"]["ms_per_forward"] / res["ours"]["ms_per_forward"], 3)
+    res["identical_accepted_tokens"] = res["ours"]["accepted"] == res["reference_cublas"]["accepted"]
+    del h, model
+    torch.cuda.empty_cache()
+    return res
 
 
 def _traffic_summary() -> dict | None:
@@ -364,17 +533,9 @@ def _traffic_summary() -> dict | None:
 
 # ------------------------------------------------------------------ CPU path
 def cpu_step(ws, xs):
-    """The reference's CPU path for one step: torch eager F.linear in bf16, silu(g)*u."""
-    out = []
-    for M in MS:
-        for name, K, N, silu in SHAPES:
-            x = xs[M][K]
-            if silu:
-                gu = F.linear(x, ws[name])
-                out.append(F.silu(gu[:, : N // 2]) * gu[:, N // 2:])
-            else:
-                out.append(F.linear(x, ws[name]))
-    return out
+    """The reference's CPU path for one step (torch eager bf16 F.linear, silu*mul)."""
+    from oracle.torch_eager import thin_sweep_step
+    return thin_sweep_step(ws, xs, SHAPES, MS)
 
 
 def cpu_setup():
@@ -457,8 +618,48 @@ def profile_case(args):
     print(f"profile case {name} M={M}: {args.profile_launches + 1} launches, out {tuple(y.shape)}")
 
 
+def profile_moe(args):
+    """A few MoE layers at T = --profile-moe (for ncu captures on a small case)."""
+    from kernels.moe_dispatch_fused import moe_layer
+    dev = torch.device("cuda", 0)
+    H, E, k, I = MOE["H"], MOE["E"], MOE["k"], MOE["I"]
+    g = torch.Generator(device=dev).manual_seed(5)
+    bf = torch.bfloat16
+    wr = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(bf)
+    bias = torch.randn(E, generator=g, device=dev) * MOE["bias_std"]
+    ws = tuple((torch.randn(*sh, generator=g, device=dev) * 0.02).to(bf) for sh in ((E, I, H), (E, I, H), (E, H, I)))
+    x = torch.randn(args.profile_moe, H, generator=g, device=dev).to(bf)
+    with torch.inference_mode():
+        for _ in range(args.profile_launches + 1):
+            y = moe_layer(x, wr, bias, k, *ws)
+        torch.cuda.synchronize()
+    print(f"profile MoE layer T={args.profile_moe}: out {tuple(y.shape)}")
+
+
+def profile_verify(args):
+    """A few eager verify forwards (for an ncu launch list)."""
+    from kernels import fused_toggle
+    from kernels.sdar_verify import SDAR_8B, SDARVerifyModel, VerifyHarness
+    dev = torch.device("cuda", 0)
+    model = SDARVerifyModel.random_init(SDAR_8B, dev, seed=0)
+    g = torch.Generator().manual_seed(1)
+    prompt = torch.randint(0, SDAR_8B.vocab, (2048,), generator=g).tolist()
+    drafts = [torch.randint(0, SDAR_8B.vocab, (4,), generator=g).tolist() for _ in range(4)]
+    smaps = [torch.randperm(4, generator=g).tolist() for _ in range(4)]
+    h = VerifyHarness(model, prompt, drafts, smaps, 4)
+    if args.profile_verify == "ours":
+        fused_toggle.apply_to_model(model, True, fuse_gate_up=True)
+    with torch.inference_mode():
+        for _ in range(args.profile_launches + 1):
+            h.window_logits()
+        torch.cuda.synchronize()
+    print(f"profile verify ({args.profile_verify}) done")
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--profile-verify", default=None, choices=["ours", "cublas"])
+    ap.add_argument("--profile-moe", type=int, default=0)
     ap.add_argument("--profile-case", default=None, choices=[s[0] for s in SHAPES])
     ap.add_argument("--profile-m", type=int, default=16)
     ap.add_argument("--profile-launches", type=int, default=3)
@@ -469,11 +670,17 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
+    ap.add_argument("--workload", default="thin,moe,verify",
+                    help="comma list of extra legs measured at N=1 besides the headline (moe, verify)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.profile_case:
         profile_case(args)
+    elif args.profile_moe:
+        profile_moe(args)
+    elif args.profile_verify:
+        profile_verify(args)
     elif args.impl == "reference":
         reference_arm(args)
     else:

@@ -6,6 +6,7 @@
 #include <initializer_list>
 #include <utility>
 #include <cstdio>
+#include <cmath>
 #include <cstdlib>
 #include <mutex>
 
@@ -186,20 +187,20 @@ int launch_tc(int bmax, const TcGemmArgs& a, int grid, cudaStream_t s, int dev) 
   return SIMSD_ERR_UNSUPPORTED;
 }
 
+// Fixup launch: one block per CTA boundary of the GEMM (grid - 1) and 16-row chunk.
 template <int BMAX>
-int launch_fixup_b(const TcFixupArgs& f, long long max_tiles, cudaStream_t s) {
-  if (max_tiles <= 0) return SIMSD_OK;
-  if (max_tiles > 0x7fffffffLL) return SIMSD_ERR_UNSUPPORTED;
-  return launch(tc_fixup_kernel<BMAX>, dim3((unsigned)max_tiles, BMAX / 16), dim3(128), 0, s, f);
+int launch_fixup_b(const TcFixupArgs& f, cudaStream_t s) {
+  if (f.grid <= 1) return SIMSD_OK;
+  return launch(tc_fixup_kernel<BMAX>, dim3((unsigned)(f.grid - 1), BMAX / 16), dim3(128), 0, s, f);
 }
 
-int launch_fixup(int bmax, const TcFixupArgs& f, long long max_tiles, cudaStream_t s) {
+int launch_fixup(int bmax, const TcFixupArgs& f, cudaStream_t s) {
   switch (bmax) {
-    case 16: return launch_fixup_b<16>(f, max_tiles, s);
-    case 32: return launch_fixup_b<32>(f, max_tiles, s);
-    case 64: return launch_fixup_b<64>(f, max_tiles, s);
-    case 128: return launch_fixup_b<128>(f, max_tiles, s);
-    case 256: return launch_fixup_b<256>(f, max_tiles, s);
+    case 16: return launch_fixup_b<16>(f, s);
+    case 32: return launch_fixup_b<32>(f, s);
+    case 64: return launch_fixup_b<64>(f, s);
+    case 128: return launch_fixup_b<128>(f, s);
+    case 256: return launch_fixup_b<256>(f, s);
   }
   return SIMSD_ERR_UNSUPPORTED;
 }
@@ -415,7 +416,7 @@ int simsd_thin_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w
     a.is_bf16 = dtype == SIMSD_BF16 ? 1 : 0;
     int rc2 = launch_tc(pl.bmax, a, pl.grid, s, dev);
     if (rc2 != SIMSD_OK || !any_split_tile(pl.tiles, pl.kb, pl.grid)) return rc2;
-    return launch_fixup(pl.bmax, fixup_args(a, pl.grid), pl.tiles, s);
+    return launch_fixup(pl.bmax, fixup_args(a, pl.grid), s);
   }
 
   SimtGemmArgs a;
@@ -496,7 +497,7 @@ int simsd_thin_linear_noalloc(const void* x, int64_t ldx_m, int64_t ldx_k, const
     a.is_bf16 = dtype == SIMSD_BF16 ? 1 : 0;
     rc = launch_tc(pl.bmax, a, pl.grid, s, dev);
     if (rc != SIMSD_OK || !any_split_tile(pl.tiles, pl.kb, pl.grid)) return rc;
-    return launch_fixup(pl.bmax, fixup_args(a, pl.grid), pl.tiles, s);
+    return launch_fixup(pl.bmax, fixup_args(a, pl.grid), s);
   }
   // layouts the tensor-core kernel cannot read need no scratch beyond the error word
   SimtGemmArgs a;
@@ -548,9 +549,36 @@ int simsd_moe_route(const void* x, int64_t ldx, int x_dtype, const void* wr, int
   a.w_dtype = w_dtype;
   a.renorm = renorm;
   a.scale = scale;
-  const int smem = 2 * ROUTE_TOK * E * (int)sizeof(float);
   const int dev = current_device();
   if (dev < 0) return SIMSD_ERR_DEVICE;
+  auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  const bool fast = (x_dtype == SIMSD_BF16 || x_dtype == SIMSD_F16) && H % 8 == 0 && ldx % 8 == 0 && al16(x) &&
+                    al16(wr) && ((w_dtype != SIMSD_F32 && ldw % 8 == 0) || (w_dtype == SIMSD_F32 && ldw % 4 == 0));
+  if (fast) {
+    const int sms = sm_count_of(dev) > 0 ? sm_count_of(dev) : 148;
+    int tt = T >= 16 * sms ? 16 : T >= 4 * sms ? 8 : 4;
+    auto smem_for = [&](int t) { return (size_t)t * H * 2 + (size_t)2 * t * E * sizeof(float); };
+    while (tt > 4 && smem_for(tt) > 200 * 1024) tt >>= 1;
+    if (smem_for(tt) <= 200 * 1024) {
+      const size_t smem = smem_for(tt);
+      const dim3 grid((unsigned)cdiv(T, tt)), block(ROUTE_WARPS * 32);
+      cudaStream_t st = (cudaStream_t)stream;
+      auto go = [&](auto kern) -> int {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess)
+          return SIMSD_ERR_LAUNCH;
+        return launch(kern, grid, block, smem, st, a);
+      };
+      if (w_dtype == SIMSD_F32) {
+        if (tt == 16) return go(route_fast_kernel<16, float>);
+        if (tt == 8) return go(route_fast_kernel<8, float>);
+        return go(route_fast_kernel<4, float>);
+      }
+      if (tt == 16) return go(route_fast_kernel<16, uint16_t>);
+      if (tt == 8) return go(route_fast_kernel<8, uint16_t>);
+      return go(route_fast_kernel<4, uint16_t>);
+    }
+  }
+  const int smem = 2 * ROUTE_TOK * E * (int)sizeof(float);
   {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g_smem_attr[dev][38]) {
@@ -580,12 +608,14 @@ static int launch_align(const int64_t* ids, int S, int E, int32_t* counts, int32
   a.E = E;
   a.block_m = block_m;
   a.num_tiles = num_tiles;
-  const int smem = (32 * E + 2 * (E + 1)) * (int)sizeof(int);
+  int smem = (32 * E + 2 * (E + 1)) * (int)sizeof(int);
+  a.ids_in_smem = (smem + (size_t)S * sizeof(int) <= 200 * 1024) ? 1 : 0;
+  if (a.ids_in_smem) smem += S * (int)sizeof(int);
   {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g_smem_attr[dev][39]) {
-      if (cudaFuncSetAttribute(align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (32 * 1024 + 2 * 1025) * 4) != cudaSuccess)
+      if (cudaFuncSetAttribute(align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
+          cudaSuccess)
         return SIMSD_ERR_LAUNCH;
       g_smem_attr[dev][39] = true;
     }
@@ -620,8 +650,12 @@ MoePlan plan_moe(int T, int k, int E, int H, int I, int dtype, int sms, bool tc)
   const long long S = (long long)T * k;
   const int es = esize(dtype);
   p.tc = tc;
-  const long long avg = E > 0 ? S / E : S;
-  p.bmax = avg <= 8 ? 16 : avg <= 16 ? 32 : avg <= 32 ? 64 : 128;
+  // Activation rows per tile: enough for a busy expert (mean + 4 sd of a
+  // Poisson count, plus slack) so it is rarely split into chunks that would each
+  // re-read its weights.
+  const double avg = E > 0 ? (double)S / E : (double)S;
+  const double want = avg + 4.0 * std::sqrt(avg) + 8.0;
+  p.bmax = want <= 16 ? 16 : want <= 32 ? 32 : want <= 64 ? 64 : 128;
   p.grid = std::max(1, std::min(sms > 0 ? sms : 148, TC_MAX_GRID));
   size_t o = WS_COUNTER_BYTES;
   p.off_counts = o; o = align256(o + (size_t)E * 4);
@@ -716,7 +750,7 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
     a.three_d = 1;
     a.is_bf16 = dtype == SIMSD_BF16 ? 1 : 0;
     rc = launch_tc(plan.bmax, a, plan.grid, s, dev);
-    if (rc == SIMSD_OK) rc = launch_fixup(plan.bmax, fixup_args(a, plan.grid), plan.max_chunks * a.row_tiles, s);
+    if (rc == SIMSD_OK) rc = launch_fixup(plan.bmax, fixup_args(a, plan.grid), s);
     if (rc != SIMSD_OK) return rc;
     // down: ys[row, h] = hbuf[row] . w_down[e, h]
     TcGemmArgs d;
@@ -744,7 +778,7 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
     d.three_d = 1;
     d.is_bf16 = a.is_bf16;
     rc = launch_tc(plan.bmax, d, plan.grid, s, dev);
-    if (rc == SIMSD_OK) rc = launch_fixup(plan.bmax, fixup_args(d, plan.grid), plan.max_chunks * d.row_tiles, s);
+    if (rc == SIMSD_OK) rc = launch_fixup(plan.bmax, fixup_args(d, plan.grid), s);
     if (rc != SIMSD_OK) return rc;
   } else {
     const long long max_chunks = std::min<long long>(E, S) + S / SIMT_ROWS + 1;
@@ -787,6 +821,10 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
                 0, s, d);
     if (rc != SIMSD_OK) return rc;
   }
+  const bool vec = dtype != SIMSD_F32 && H % 8 == 0 && ld_out % 8 == 0 && al(out) && (add == nullptr || (al(add) && ld_add % 8 == 0)) && k <= 32;
+  if (vec)
+    return launch(combine_vec_kernel, dim3((unsigned)T), dim3(128), 0, s, (const void*)ys, (long long)H, (const int*)s2r,
+                  topk_weight, out, (long long)ld_out, add, (long long)ld_add, T, k, H, dtype);
   return launch(combine_kernel, dim3((unsigned)T), dim3(256), 0, s, (const void*)ys, (long long)H, (const int*)s2r,
                 topk_weight, out, (long long)ld_out, add, (long long)ld_add, T, k, H, dtype);
 }

@@ -104,6 +104,56 @@ __device__ __forceinline__ void load8(const void* base, long long idx, int dtype
   for (int i = 0; i < 8; ++i) v[i] = (i < n_valid) ? load_f(base, idx + i, dtype) : 0.0f;
 }
 
+// top-k per token, one warp per token; lane l owns experts l, l+32, ...
+__device__ __forceinline__ void route_topk(const RouteArgs& p, const float* s_score, float* s_choice, int t0,
+                                           int ntok) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int t = warp; t < ntok; t += ROUTE_WARPS) {
+    const float* ch = s_choice + t * p.E;
+    float wsel[32];
+    int isel[32];
+    unsigned taken = 0u;
+    for (int j = 0; j < p.k; ++j) {
+      float bb = 0.0f;
+      int be = -1;
+      int i = 0;
+      for (int e = lane; e < p.E; e += 32, ++i) {
+        if ((taken >> i) & 1u) continue;
+        float v = ch[e];
+        if (v != v) v = -__int_as_float(0x7f800000);
+        if (be < 0 || v > bb) { bb = v; be = e; }
+      }
+#pragma unroll
+      for (int m = 16; m > 0; m >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, bb, m);
+        const int oe = __shfl_xor_sync(0xffffffffu, be, m);
+        const bool take = (be < 0) || (oe >= 0 && (ob > bb || (ob == bb && oe < be)));
+        if (take) { bb = ob; be = oe; }
+      }
+      if (be >= 0 && (be & 31) == lane) taken |= 1u << (be >> 5);
+      isel[j] = be;
+      wsel[j] = (be >= 0) ? s_score[t * p.E + be] : 0.0f;
+    }
+    if (lane == 0) {
+      const bool norm = p.renorm && p.k > 1;
+      float denom = 1.0f;
+      if (norm) {
+        float sum = wsel[0];
+        for (int j = 1; j < p.k; ++j) sum = __fadd_rn(sum, wsel[j]);
+        denom = __fadd_rn(sum, 1e-20f);
+      }
+      for (int j = 0; j < p.k; ++j) {
+        float wj = wsel[j];
+        if (norm) wj = __fdiv_rn(wj, denom);
+        wj = __fmul_rn(wj, p.scale);
+        p.topk_ids[(long long)(t0 + t) * p.k + j] = isel[j];
+        p.topk_weight[(long long)(t0 + t) * p.k + j] = wj;
+      }
+    }
+    __syncwarp();
+  }
+}
+
 __global__ void __launch_bounds__(ROUTE_WARPS * 32) route_kernel(const RouteArgs p) {
   griddep_launch_dependents();
   griddep_wait();
@@ -171,51 +221,140 @@ __global__ void __launch_bounds__(ROUTE_WARPS * 32) route_kernel(const RouteArgs
   }
   __syncthreads();
 
-  // top-k per token, one warp per token; lane l owns experts l, l+32, ...
-  for (int t = warp; t < ntok; t += ROUTE_WARPS) {
-    const float* ch = s_choice + t * p.E;
-    float wsel[32];
-    int isel[32];
-    unsigned taken = 0u;
-    for (int j = 0; j < p.k; ++j) {
-      float bb = 0.0f;
-      int be = -1;
-      int i = 0;
-      for (int e = lane; e < p.E; e += 32, ++i) {
-        if ((taken >> i) & 1u) continue;
-        float v = ch[e];
-        if (v != v) v = -__int_as_float(0x7f800000);
-        if (be < 0 || v > bb) { bb = v; be = e; }
+  route_topk(p, s_score, s_choice, t0, ntok);
+}
+
+// Fast router for 16-bit activations with H % 8 == 0 and 16-byte aligned rows.
+// A CTA stages TT token rows in shared memory; each warp pass computes the
+// TT x (32/TT) logits of TT tokens and 32/TT experts with the same per-lane
+// chunk order as route_kernel, then a reduce-scatter butterfly leaves logit q of
+// the pass in lane q.  Its pairing tree is the one of the xor butterfly
+// (v_l + v_{l^m} for m = 16, 8, 4, 2, 1), so the logits are bit-identical to
+// route_kernel's and to the oracle's.  TT adapts to T so small batches still
+// spread over many SMs.
+template <int TT, typename WT>
+__global__ void __launch_bounds__(ROUTE_WARPS * 32) route_fast_kernel(const RouteArgs p) {
+  griddep_launch_dependents();
+  griddep_wait();
+  constexpr int EE = 32 / TT;
+  extern __shared__ __align__(16) unsigned char rsh[];
+  uint16_t* xs = reinterpret_cast<uint16_t*>(rsh);                       // [TT][H]
+  float* s_score = reinterpret_cast<float*>(rsh + (size_t)TT * p.H * 2);  // [TT][E]
+  float* s_choice = s_score + TT * p.E;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.x * TT;
+  const int ntok = min(TT, p.T - t0);
+  const int H = p.H, E = p.E;
+  const int vec_per_row = H / 8;
+
+  // stage the token rows (16-byte vectors); rows past T are zero
+  for (int i = threadIdx.x; i < TT * vec_per_row; i += blockDim.x) {
+    const int t = i / vec_per_row, c = i - t * vec_per_row;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (t < ntok)
+      v = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.x) + (long long)(t0 + t) * p.ldx + c * 8);
+    reinterpret_cast<uint4*>(xs)[i] = v;
+  }
+  __syncthreads();
+
+  const int nchunks = vec_per_row;
+  for (int e0 = warp * EE; e0 < E; e0 += ROUTE_WARPS * EE) {
+    float v[32];
+#pragma unroll
+    for (int q = 0; q < 32; ++q) v[q] = 0.0f;
+    // weight chunks are prefetched one iteration ahead (raw 16-byte vectors)
+    constexpr int WV = sizeof(WT) == 4 ? 2 : 1;        // uint4 per 8-element chunk
+    uint4 wraw[EE][WV], wnext[EE][WV];
+    auto load_w = [&](int c, uint4 (&dst)[EE][WV]) {
+#pragma unroll
+      for (int j = 0; j < EE; ++j) {
+        const int e = e0 + j;
+#pragma unroll
+        for (int q = 0; q < WV; ++q) {
+          if (e < E && c < nchunks)
+            dst[j][q] = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(p.w) +
+                                                        ((long long)e * p.ldw + c * 8) * sizeof(WT) + q * 16);
+          else
+            dst[j][q] = make_uint4(0, 0, 0, 0);
+        }
+      }
+    };
+    load_w(lane, wraw);
+    for (int c = lane; c < nchunks; c += 32) {
+      load_w(c + 32, wnext);
+      float wv[EE][8];
+#pragma unroll
+      for (int j = 0; j < EE; ++j) {
+        if constexpr (sizeof(WT) == 4) {
+          wv[j][0] = __uint_as_float(wraw[j][0].x); wv[j][1] = __uint_as_float(wraw[j][0].y);
+          wv[j][2] = __uint_as_float(wraw[j][0].z); wv[j][3] = __uint_as_float(wraw[j][0].w);
+          wv[j][4] = __uint_as_float(wraw[j][1].x); wv[j][5] = __uint_as_float(wraw[j][1].y);
+          wv[j][6] = __uint_as_float(wraw[j][1].z); wv[j][7] = __uint_as_float(wraw[j][1].w);
+        } else {
+          const uint32_t w4[4] = {wraw[j][0].x, wraw[j][0].y, wraw[j][0].z, wraw[j][0].w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            if (p.w_dtype == 0) {
+              wv[j][2 * i] = __uint_as_float(w4[i] << 16);
+              wv[j][2 * i + 1] = __uint_as_float(w4[i] & 0xffff0000u);
+            } else {
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[i]));
+              wv[j][2 * i] = f.x;
+              wv[j][2 * i + 1] = f.y;
+            }
+          }
+        }
       }
 #pragma unroll
-      for (int m = 16; m > 0; m >>= 1) {
-        const float ob = __shfl_xor_sync(0xffffffffu, bb, m);
-        const int oe = __shfl_xor_sync(0xffffffffu, be, m);
-        const bool take = (be < 0) || (oe >= 0 && (ob > bb || (ob == bb && oe < be)));
-        if (take) { bb = ob; be = oe; }
+      for (int t = 0; t < TT; ++t) {
+        const uint4 u = reinterpret_cast<const uint4*>(xs)[t * vec_per_row + c];
+        const uint32_t x4[4] = {u.x, u.y, u.z, u.w};
+        float xv[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if (p.x_dtype == 0) {
+            xv[2 * i] = __uint_as_float(x4[i] << 16);
+            xv[2 * i + 1] = __uint_as_float(x4[i] & 0xffff0000u);
+          } else {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&x4[i]));
+            xv[2 * i] = f.x;
+            xv[2 * i + 1] = f.y;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < EE; ++j) v[t * EE + j] = __fmaf_rn(xv[i], wv[j][i], v[t * EE + j]);
       }
-      if (be >= 0 && (be & 31) == lane) taken |= 1u << (be >> 5);
-      isel[j] = be;
-      wsel[j] = (be >= 0) ? s_score[t * p.E + be] : 0.0f;
+#pragma unroll
+      for (int j = 0; j < EE; ++j)
+#pragma unroll
+        for (int q = 0; q < WV; ++q) wraw[j][q] = wnext[j][q];
     }
-    if (lane == 0) {
-      const bool norm = p.renorm && p.k > 1;
-      float denom = 1.0f;
-      if (norm) {
-        float sum = wsel[0];
-        for (int j = 1; j < p.k; ++j) sum = __fadd_rn(sum, wsel[j]);
-        denom = __fadd_rn(sum, 1e-20f);
-      }
-      for (int j = 0; j < p.k; ++j) {
-        float wj = wsel[j];
-        if (norm) wj = __fdiv_rn(wj, denom);
-        wj = __fmul_rn(wj, p.scale);
-        p.topk_ids[(long long)(t0 + t) * p.k + j] = isel[j];
-        p.topk_weight[(long long)(t0 + t) * p.k + j] = wj;
+    // reduce-scatter: after the step with offset m, a lane keeps the half of
+    // its values whose index bit log2(m) equals its own lane bit
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) {
+      const bool upper = (lane & m) != 0;
+#pragma unroll
+      for (int i = 0; i < m; ++i) {
+        const float send = upper ? v[i] : v[i + m];
+        const float keep = upper ? v[i + m] : v[i];
+        const float recv = __shfl_xor_sync(0xffffffffu, send, m);
+        v[i] = __fadd_rn(keep, recv);
       }
     }
-    __syncwarp();
+    const int t = lane / EE, e = e0 + (lane % EE);
+    if (t < ntok && e < E) {
+      const float lg = v[0];
+      if (p.logits) p.logits[(long long)(t0 + t) * E + e] = lg;
+      const float sc = sigmoid_fixed(lg);
+      s_score[t * E + e] = sc;
+      s_choice[t * E + e] = p.bias ? __fadd_rn(sc, p.bias[e]) : sc;
+    }
   }
+  __syncthreads();
+  route_topk(p, s_score, s_choice, t0, ntok);
 }
 
 // ------------------------------------------------------------------ align
@@ -234,6 +373,7 @@ struct AlignArgs {
   int* tile_expert;       // reference layout [num_tiles] or nullptr
   int* err;
   int S, E, block_m, num_tiles;
+  int ids_in_smem;        // 1: the launch reserved S ints of shared memory for the ids
 };
 
 constexpr int ALIGN_THREADS = 1024;
@@ -251,10 +391,19 @@ __global__ void __launch_bounds__(ALIGN_THREADS, 1) align_kernel(const AlignArgs
   const int L = (S + 31) / 32;
   const int lo = warp * L, hi = min(S, lo + L);
 
+  // the ids are read twice below; keep an int32 copy in shared memory when it fits
+  int* s_ids = s_pad + E + 1;
+  const bool cache_ids = p.ids_in_smem != 0;
   for (int i = tid; i < 32 * E; i += ALIGN_THREADS) hist[i] = 0;
+  if (cache_ids)
+    for (int i = tid; i < S; i += ALIGN_THREADS) {
+      const long long e = p.ids[i];
+      s_ids[i] = (e >= 0 && e < E) ? (int)e : -1;
+    }
   __syncthreads();
+  auto id_at = [&](int s) -> long long { return cache_ids ? (long long)s_ids[s] : p.ids[s]; };
   for (int s = lo + lane; s < hi; s += 32) {
-    const long long e = p.ids[s];
+    const long long e = id_at(s);
     if (e >= 0 && e < E) atomicAdd(&hist[warp * E + (int)e], 1);
   }
   __syncthreads();
@@ -305,7 +454,7 @@ __global__ void __launch_bounds__(ALIGN_THREADS, 1) align_kernel(const AlignArgs
     int e = -2;
     bool valid = false;
     if (s < hi) {
-      const long long ev = p.ids[s];
+      const long long ev = id_at(s);
       if (ev >= 0 && ev < E) { e = (int)ev; valid = true; }
       else { e = -1; }
     }
@@ -411,6 +560,80 @@ __global__ void combine_kernel(const void* ys, long long ldys, const int* slot_t
       acc = __fadd_rn(r, load_f(add, (long long)t * ld_add + h, dtype));
     }
     store_f(out, (long long)t * ld_out + h, acc, dtype);
+  }
+}
+
+// combine_kernel for 16-bit outputs with H % 8 == 0: a thread owns 8 adjacent
+// columns (16-byte loads and stores); same arithmetic, same order.
+__device__ __forceinline__ void unpack8(uint4 u, int dtype, float (&v)[8]) {
+  const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (dtype == 0) {
+      v[2 * i] = __uint_as_float(w4[i] << 16);
+      v[2 * i + 1] = __uint_as_float(w4[i] & 0xffff0000u);
+    } else {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[i]));
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+}
+
+__device__ __forceinline__ float round_to_dtype(float v, int dtype) {
+  return dtype == 0 ? __bfloat162float(__float2bfloat16_rn(v)) : __half2float(__float2half_rn(v));
+}
+
+__global__ void combine_vec_kernel(const void* ys, long long ldys, const int* slot_to_row, const float* w, void* out,
+                                   long long ld_out, const void* add, long long ld_add, int T, int k, int H,
+                                   int dtype) {
+  griddep_launch_dependents();
+  griddep_wait();
+  __shared__ int s_row[32];
+  __shared__ float s_w[32];
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  if (threadIdx.x < k) {
+    s_row[threadIdx.x] = slot_to_row[(long long)t * k + threadIdx.x];
+    s_w[threadIdx.x] = w[(long long)t * k + threadIdx.x];
+  }
+  __syncthreads();
+  const uint16_t* yb = reinterpret_cast<const uint16_t*>(ys);
+  for (int h8 = threadIdx.x; h8 < H / 8; h8 += blockDim.x) {
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+    for (int j = 0; j < k; ++j) {
+      const int row = s_row[j];
+      if (row < 0) continue;
+      float y[8];
+      unpack8(*reinterpret_cast<const uint4*>(yb + (long long)row * ldys + h8 * 8), dtype, y);
+      const float wj = s_w[j];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], __fmul_rn(y[i], wj));
+    }
+    if (add) {
+      float a[8];
+      unpack8(*reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(add) + (long long)t * ld_add + h8 * 8),
+              dtype, a);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(round_to_dtype(acc[i], dtype), a[i]);
+    }
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (dtype == 0) {
+        const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(acc[2 * i]));
+        const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(acc[2 * i + 1]));
+        o[i] = lo | (hi << 16);
+      } else {
+        const uint32_t lo = __half_as_ushort(__float2half_rn(acc[2 * i]));
+        const uint32_t hi = __half_as_ushort(__float2half_rn(acc[2 * i + 1]));
+        o[i] = lo | (hi << 16);
+      }
+    }
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + (long long)t * ld_out + h8 * 8) =
+        make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 

@@ -483,11 +483,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
   if (p.trace && tid == 0) p.trace[blockIdx.x * 8 + 7] = globaltimer_ns();
 }
 
-// Deterministic split-K reduction for tc_gemm_kernel: block (tile, chunk) sums
-// the fp32 partial slots of one split tile in K order for 16 activation rows
-// and applies the epilogue (bias, or SiLU*mul across the gate/up halves).
-// Whole tiles were already written by the GEMM.  The grid is sized for the
-// largest possible tile count; blocks past the actual count return at once.
+// Deterministic split-K reduction for tc_gemm_kernel.  A tile is split exactly
+// where a CTA boundary falls strictly inside it, so block (b, chunk) looks at
+// boundary b+1: if it is the first boundary inside its tile, the block sums that
+// tile's partial slots in K order for 16 activation rows and applies the
+// epilogue (bias, or SiLU*mul across the gate/up halves).  The grid is therefore
+// (gemm grid - 1) x (BMAX / 16) whatever the tile count, and whole tiles (written
+// by the GEMM itself) cost nothing here.
 struct TcFixupArgs {
   const float* partials;
   void* out;
@@ -502,27 +504,38 @@ template <int BMAX>
 __global__ void __launch_bounds__(128) tc_fixup_kernel(const TcFixupArgs p) {
   griddep_launch_dependents();
   griddep_wait();
-  __shared__ int s_total;
+  __shared__ int s_tab[2 * (TC_MAX_GROUPS + 1)];
   const int row = threadIdx.x;
-  const long long tile = blockIdx.x;
   const int ch = blockIdx.y;
-  const int* row_prefix = p.tables;
-  const int* chunk_prefix = p.tables ? p.tables + TC_MAX_GROUPS + 1 : nullptr;
+  const int* row_prefix = s_tab;
+  const int* chunk_prefix = s_tab + TC_MAX_GROUPS + 1;
   long long total_tiles;
   if (p.group_counts != nullptr) {
-    if (row == 0) s_total = chunk_prefix[p.num_groups];
+    // the GEMM's prefix tables, copied once into shared memory for the tile search
+    for (int g = row; g <= p.num_groups; g += 128) {
+      s_tab[g] = p.tables[g];
+      s_tab[TC_MAX_GROUPS + 1 + g] = p.tables[TC_MAX_GROUPS + 1 + g];
+    }
     __syncthreads();
-    total_tiles = (long long)s_total * p.row_tiles;
+    total_tiles = (long long)chunk_prefix[p.num_groups] * p.row_tiles;
   } else {
     total_tiles = (long long)((p.single_rows + BMAX - 1) / BMAX) * p.row_tiles;
   }
-  if (tile >= total_tiles) return;
   const long long kb = p.kb;
   const long long iters = total_tiles * kb;
+  if (iters == 0) return;
   const long long G = min((long long)p.grid, iters);
+  const long long cb = (long long)blockIdx.x + 1;      // CTA boundary: start of CTA cb
+  if (cb >= G) return;
+  const long long ib = sk_start(cb, iters, G);
+  if (ib % kb == 0) return;                            // on a tile edge: splits nothing
+  const long long tile = ib / kb;
+  if (cb > 1) {
+    const long long ip = sk_start(cb - 1, iters, G);
+    if (ip / kb == tile && ip % kb != 0) return;       // an earlier boundary owns this tile
+  }
   const long long c_first = sk_owner(tile * kb, iters, G);
   const long long c_last = sk_owner(tile * kb + kb - 1, iters, G);
-  if (c_first == c_last) return;                       // whole tile: written by the GEMM
   TcGemmArgs ta;                                       // decode_tile reads only these fields
   ta.group_counts = p.group_counts;
   ta.row_tiles = p.row_tiles;

@@ -17,6 +17,12 @@ Writes (inputs and the reference's outputs, bf16 as uint16 bit patterns):
                      (scaled down) and the magnitude / zero / bias cases of :74-109
   router.npz         the router restatement sigmoid(x.float() @ Wr.float().T), top-k of
                      score + bias, gathered scores renormalised (+1e-20) x scale, in torch
+  sdar_verify.npz    a tiny fp32 SDARForCausalLM (sdar/modeling_sdar.py, imported with the
+                     shims transformers 5.x needs) with patch_stock_rms_norm, its logits on a
+                     K=2 verify sequence from speculative_decoding/verify.py:350-418
+                     build_verify_sequence_multi, the mask of
+                     sdar/new_attn_multi_block.py:22-186, and mrs.py:111-145
+                     greedy_match_verify results
   manifest.json      provenance of every case
 """
 from __future__ import annotations
@@ -44,6 +50,55 @@ def bits(t: torch.Tensor) -> np.ndarray:
     if t.dtype == torch.bfloat16:
         return t.contiguous().view(torch.int16).numpy().view(np.uint16)
     return t.contiguous().numpy()
+
+
+def load_reference_sdar():
+    """Import the reference's sdar/modeling_sdar.py under transformers 5.x.
+
+    The file targets transformers 4.52 and a configuration module that is not in
+    the checkout, so five names are supplied before it is executed: a
+    SDARConfig (Qwen3Config subclass), SlidingWindowCache, LossKwargs, the
+    'default' RoPE init and a stand-in for flash-attn's Triton RMSNorm (the
+    runners replace RMSNorm.forward with patch_stock_rms_norm anyway).
+    """
+    import importlib.util
+    import types
+    from typing import TypedDict
+
+    import transformers.cache_utils as cu
+    import transformers.utils as tu
+    from transformers import Qwen3Config
+    from transformers.modeling_rope_utils import ROPE_INIT_FUNCTIONS
+    if not hasattr(cu, "SlidingWindowCache"):
+        cu.SlidingWindowCache = type("SlidingWindowCache", (), {})
+    if not hasattr(tu, "LossKwargs"):
+        tu.LossKwargs = TypedDict("LossKwargs", {}, total=False)
+    if "default" not in ROPE_INIT_FUNCTIONS:
+        def _default(config, device=None, **kw):
+            rp = getattr(config, "rope_parameters", None) or {}
+            base = rp.get("rope_theta", getattr(config, "rope_theta", 10000.0))
+            dim = getattr(config, "head_dim", config.hidden_size // config.num_attention_heads)
+            inv = 1.0 / (base ** (torch.arange(0, dim, 2, dtype=torch.int64).to(device=device, dtype=torch.float) / dim))
+            return inv, 1.0
+        ROPE_INIT_FUNCTIONS["default"] = _default
+    ln = types.ModuleType("flash_attn.ops.triton.layer_norm")
+    ln.rms_norm_fn = lambda *a, **k: None
+    for name in ("flash_attn.ops", "flash_attn.ops.triton"):
+        sys.modules.setdefault(name, types.ModuleType(name))
+    sys.modules["flash_attn.ops.triton.layer_norm"] = ln
+    pkg = types.ModuleType("sdar_ref")
+    pkg.__path__ = [str(REF / "sdar")]
+    sys.modules["sdar_ref"] = pkg
+    cfgmod = types.ModuleType("sdar_ref.configuration_sdar")
+    SDARConfig = type("SDARConfig", (Qwen3Config,), {"model_type": "sdar"})
+    cfgmod.SDARConfig = SDARConfig
+    sys.modules["sdar_ref.configuration_sdar"] = cfgmod
+    spec = importlib.util.spec_from_file_location("sdar_ref.modeling_sdar", REF / "sdar" / "modeling_sdar.py")
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["sdar_ref.modeling_sdar"] = mod
+    spec.loader.exec_module(mod)
+    mod.liger_kernel_is_available = False
+    return mod, SDARConfig
 
 
 def main():
@@ -166,6 +221,54 @@ def main():
         manifest["cases"][f"router/{name}"] = {"T": T, "H": H, "E": E, "k": k, "bias_std": bias_std,
                                                "src": "torch restatement of the sigmoid+bias top-k router"}
     np.savez_compressed(OUT / "router.npz", **arrs)
+
+    # ---------------------------------------------------------------- SDAR verify (tiny)
+    arrs = {}
+    mod, SDARConfig = load_reference_sdar()
+    from sdar.run_native_tp2 import patch_stock_rms_norm
+    from sdar.new_attn_multi_block import create_multi_block_causal_mask
+    from speculative_decoding.mrs import greedy_match_verify
+    from speculative_decoding.verify import build_verify_sequence_multi
+    cfg = SDARConfig(vocab_size=256, hidden_size=64, intermediate_size=128, num_hidden_layers=2,
+                     num_attention_heads=4, num_key_value_heads=2, head_dim=16, rope_theta=1e6,
+                     rms_norm_eps=1e-6, max_position_embeddings=512, attention_bias=False,
+                     tie_word_embeddings=False)
+    cfg._attn_implementation = "sdpa"
+    cfg.fuse_cross_entropy = False
+    m = mod.SDARForCausalLM(cfg).eval()
+    patch_stock_rms_norm(m)
+    torch.manual_seed(0)
+    with torch.no_grad():
+        for n, p in m.named_parameters():
+            if "norm" in n:
+                p.fill_(1.0)
+            else:
+                p.normal_(0, 0.02)
+    prompt = list(range(10, 30))
+    accepted = [[40, 41, 42, 43]]
+    drafts = [[5, 6, 7, 8], [9, 10, 11, 12]]
+    smaps = [[0, 2, 1, 3], [3, 1, 0, 2]]
+    ids, labels, blocks, _, pos = build_verify_sequence_multi(prompt, accepted, drafts, smaps, 4, 4,
+                                                             mask_token_id=255)
+    mask = create_multi_block_causal_mask(torch.tensor([labels]), torch.tensor([blocks]), 4,
+                                          block_causal_prompt=True)
+    with torch.no_grad():
+        logits = m(input_ids=torch.tensor([ids]), attention_mask=mask, position_ids=torch.tensor([pos]),
+                   use_cache=False).logits[0]
+    for k, v in m.state_dict().items():
+        arrs[f"w.{k.replace('model.', '', 1)}"] = v.numpy()
+    arrs.update({"ids": np.array(ids), "labels": np.array(labels), "blocks": np.array(blocks),
+                 "pos": np.array(pos), "mask": mask[0, 0].numpy(), "logits": logits.numpy()})
+    probs = torch.softmax(logits[-4:], -1)            # the last draft block's mask window
+    for name, d in (("hit", probs.argmax(-1).tolist()), ("miss2", probs.argmax(-1).tolist()[:2] + [0, 0])):
+        acc, n, bonus = greedy_match_verify(d, probs, probs, [0, 1, 2, 3])
+        arrs[f"greedy.{name}.draft"] = np.array(d)
+        arrs[f"greedy.{name}.accepted"] = np.array(acc)
+        arrs[f"greedy.{name}.n"] = np.array(n)
+        arrs[f"greedy.{name}.bonus"] = np.array(-1 if bonus is None else bonus)
+    np.savez_compressed(OUT / "sdar_verify.npz", **arrs)
+    manifest["cases"]["sdar_verify/tiny"] = {"layers": 2, "hidden": 64, "heads": "4/2", "head_dim": 16,
+                                             "src": "sdar/modeling_sdar.py SDARForCausalLM + patch_stock_rms_norm"}
 
     (OUT / "manifest.json").write_text(json.dumps(manifest, indent=1) + "\n")
     for p in sorted(OUT.glob("*.npz")):

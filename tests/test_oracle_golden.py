@@ -156,3 +156,29 @@ def test_silu_mul_oracle_is_fp32_product():
     acc, _ = O.thin_linear_silu_mul(x, wg, wu)
     g, u = x.astype(np.float64) @ wg.T, x.astype(np.float64) @ wu.T
     np.testing.assert_allclose(acc, g / (1 + np.exp(-g)) * u, rtol=1e-5, atol=1e-6)
+
+
+def test_torch_eager_restatement_matches_reference_moe():
+    """The CPU baseline's stock-path restatement (oracle/torch_eager.py) against the
+    reference's reference_moe_dispatch outputs."""
+    import torch
+    from oracle import torch_eager as TE
+    z = _load("moe_dispatch")
+    for c in _cases(z):
+        dt = str(z[f"{c}.dtype"])
+        tdt = {"torch.bfloat16": torch.bfloat16, "torch.float16": torch.float16,
+               "torch.float32": torch.float32}[dt]
+
+        def t(a):
+            if tdt == torch.bfloat16:
+                return torch.from_numpy(a.view(np.int16).copy()).view(torch.bfloat16)
+            if tdt == torch.float16:
+                return torch.from_numpy(a.view(np.float16).copy())
+            return torch.from_numpy(a.copy())
+        x, wg, wu, wd, ref = (t(z[f"{c}.{k}"]) for k in ("x", "wg", "wu", "wd", "ref"))
+        ids = torch.from_numpy(z[f"{c}.ids"])
+        w = torch.from_numpy(z[f"{c}.w"])
+        with torch.inference_mode():
+            got = TE.moe_infer(x, ids, w, wg, wu, wd)
+        err = float((got.float() - ref.float()).abs().max())
+        assert err <= _moe_tol(ref.float().numpy(), dt), c
