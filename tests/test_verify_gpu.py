@@ -107,6 +107,7 @@ def test_bf16_flips_only_at_near_ties_and_graph_replay():
         fused_toggle.apply_to_model(h.model, False)
         # fp32 truth for the same weights
         h32 = VerifyHarness(h.model.float(), h.prompt, sets[0], h.smaps, BL)
+        h32.smaps = h.smaps
         truths = [_logits(h32, d) for d in sets]
         rows = torch.cat([torch.arange(h.mask_rows(k).start, h.mask_rows(k).stop) for k in range(K)])
         noise = max(float((r - t)[rows].abs().max()) for r, t in zip(ref, truths))
