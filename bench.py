@@ -618,6 +618,24 @@ def profile_case(args):
     print(f"profile case {name} M={M}: {args.profile_launches + 1} launches, out {tuple(y.shape)}")
 
 
+def profile_sweep(args):
+    """One warm step, then --profile-launches steps of the whole SDAR-8B sweep
+    (20 linears, launched as the bench launches them), for ncu launch lists and
+    DRAM-traffic captures."""
+    from kernels import _lib
+    dev = torch.device("cuda", 0)
+    _lib.set_pdl(not args.no_pdl)
+    pool = make_weights(0, 1, dev)
+    xs = make_inputs(dev)
+    with torch.inference_mode():
+        run_step(pool[0], xs, 1, None)
+        torch.cuda.synchronize()
+        for i in range(args.profile_launches):
+            run_step(pool[(i + 1) % POOL], xs, 1, None)
+        torch.cuda.synchronize()
+    print(f"profile sweep: 1 + {args.profile_launches} steps of {len(MS) * len(SHAPES)} linears")
+
+
 def profile_moe(args):
     """A few MoE layers at T = --profile-moe (for ncu captures on a small case)."""
     from kernels.moe_dispatch_fused import moe_layer
@@ -661,6 +679,7 @@ def main():
     ap.add_argument("--profile-verify", default=None, choices=["ours", "cublas"])
     ap.add_argument("--profile-moe", type=int, default=0)
     ap.add_argument("--profile-case", default=None, choices=[s[0] for s in SHAPES])
+    ap.add_argument("--profile-sweep", action="store_true")
     ap.add_argument("--profile-m", type=int, default=16)
     ap.add_argument("--profile-launches", type=int, default=3)
     ap.add_argument("--gpus", type=int, default=1)
@@ -677,6 +696,8 @@ def main():
         args.warmup = 3
     if args.profile_case:
         profile_case(args)
+    elif args.profile_sweep:
+        profile_sweep(args)
     elif args.profile_moe:
         profile_moe(args)
     elif args.profile_verify:
