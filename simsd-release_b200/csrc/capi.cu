@@ -188,19 +188,41 @@ int launch_tc(int bmax, const TcGemmArgs& a, int grid, cudaStream_t s, int dev) 
 }
 
 // Fixup launch: one block per CTA boundary of the GEMM (grid - 1) and 16-row chunk.
+// Small kernels that run between tensor-core GEMMs ask for the largest
+// shared-memory carve-out: an SM changes its L1/shared split only when idle, so a
+// block configured otherwise would keep the next GEMM's CTA (about 200 KB of
+// shared memory) off its SM until the block exits.
+template <typename F>
+int prefer_shared(F* kern, int dev, int idx) {
+  static bool done[kMaxDev][16];
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!done[dev][idx]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared) !=
+        cudaSuccess)
+      return SIMSD_ERR_LAUNCH;
+    done[dev][idx] = true;
+  }
+  return SIMSD_OK;
+}
+
 template <int BMAX>
-int launch_fixup_b(const TcFixupArgs& f, cudaStream_t s) {
+int launch_fixup_b(const TcFixupArgs& f, cudaStream_t s, int dev) {
   if (f.grid <= 1) return SIMSD_OK;
-  return launch(tc_fixup_kernel<BMAX>, dim3((unsigned)(f.grid - 1), BMAX / 16), dim3(128), 0, s, f);
+  constexpr int idx = BMAX == 16 ? 0 : BMAX == 32 ? 1 : BMAX == 64 ? 2 : BMAX == 128 ? 3 : 4;
+  if (prefer_shared(tc_fixup_kernel<BMAX>, dev, idx) != SIMSD_OK) return SIMSD_ERR_LAUNCH;
+  const size_t smem = f.group_counts ? (size_t)2 * (f.num_groups + 1) * sizeof(int) : 0;
+  return launch(tc_fixup_kernel<BMAX>, dim3((unsigned)(f.grid - 1), BMAX / 16), dim3(128), smem, s, f);
 }
 
 int launch_fixup(int bmax, const TcFixupArgs& f, cudaStream_t s) {
+  const int dev = current_device();
+  if (dev < 0) return SIMSD_ERR_DEVICE;
   switch (bmax) {
-    case 16: return launch_fixup_b<16>(f, s);
-    case 32: return launch_fixup_b<32>(f, s);
-    case 64: return launch_fixup_b<64>(f, s);
-    case 128: return launch_fixup_b<128>(f, s);
-    case 256: return launch_fixup_b<256>(f, s);
+    case 16: return launch_fixup_b<16>(f, s, dev);
+    case 32: return launch_fixup_b<32>(f, s, dev);
+    case 64: return launch_fixup_b<64>(f, s, dev);
+    case 128: return launch_fixup_b<128>(f, s, dev);
+    case 256: return launch_fixup_b<256>(f, s, dev);
   }
   return SIMSD_ERR_UNSUPPORTED;
 }
@@ -226,11 +248,10 @@ TcFixupArgs fixup_args(const TcGemmArgs& a, int grid) {
 
 // Does the stream-K split of (tiles x kb) over `grid` CTAs cut any tile?
 bool any_split_tile(long long tiles, long long kb, long long grid) {
-  const long long iters = tiles * kb;
-  const long long G = std::min(grid, iters);
-  auto owner = [&](long long i) { return ((i + 1) * G + iters - 1) / iters - 1; };
-  for (long long t = 0; t < tiles; ++t)
-    if (owner(t * kb) != owner(t * kb + kb - 1)) return true;
+  const int iters = (int)(tiles * kb);
+  const SkSplit sk(iters, (int)std::min<long long>(grid, iters));
+  for (int t = 0; t < (int)tiles; ++t)
+    if (sk.owner(t * (int)kb) != sk.owner(t * (int)kb + (int)kb - 1)) return true;
   return false;
 }
 
@@ -265,6 +286,8 @@ int thin_tc_possible(const void* x, long long ldx_m, long long ldx_k, const void
   if (!al(x) || !al(w) || (w_up && !al(w_up))) return 0;
   if (M > 1 && (ldx_m < K || ((ldx_m * 2) & 15) != 0)) return 0;
   if (N > 1 && (ldw_n < K || ((ldw_n * 2) & 15) != 0)) return 0;
+  // the tensor-core kernel indexes (tile, k-block) iterations with 32-bit ints
+  if (cdiv(M, pick_bmax_rows(M)) * cdiv(N, 64) * cdiv(K, 64) >= (1LL << 31)) return 0;
   return 1;
 }
 
@@ -702,6 +725,11 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
   bool tc = dtype != SIMSD_F32 && H >= 64 && I >= 64 && (H % 8) == 0 && (I % 8) == 0 && al(w_gate) && al(w_up) &&
             al(w_down) && (ldg_e % 8) == 0 && (ldg_i % 8) == 0 && (ldd_e % 8) == 0 && (ldd_h % 8) == 0 &&
             ldg_i >= H && ldd_h >= I;
+  {
+    // the grouped GEMMs index (tile, k-block) iterations with 32-bit ints
+    const long long chunks = std::min<long long>(E, S) + S / 16 + 1;
+    if (chunks * std::max(cdiv(I, 64) * cdiv(H, 64), cdiv(H, 128) * cdiv(I, 64)) >= (1LL << 31)) tc = false;
+  }
   const MoePlan plan = plan_moe(T, k, E, H, I, dtype, sm_count_of(dev), tc);
   if (workspace_bytes < plan.total) return SIMSD_ERR_WORKSPACE;
 
@@ -717,6 +745,7 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
 
   int rc = launch_align(topk_ids, (int)S, E, counts, offsets, sorted, s2r, 16, 0, nullptr, nullptr, err, s, dev);
   if (rc != SIMSD_OK) return rc;
+  if (prefer_shared(gather_rows_kernel, dev, 5) != SIMSD_OK) return SIMSD_ERR_LAUNCH;
   rc = launch(gather_rows_kernel, dim3((unsigned)S), dim3(256), 0, s, x, (long long)ldx, (const int*)sorted, xs,
               (long long)H, (int)S, k, H, es);
   if (rc != SIMSD_OK) return rc;
@@ -822,9 +851,12 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
     if (rc != SIMSD_OK) return rc;
   }
   const bool vec = dtype != SIMSD_F32 && H % 8 == 0 && ld_out % 8 == 0 && al(out) && (add == nullptr || (al(add) && ld_add % 8 == 0)) && k <= 32;
-  if (vec)
+  if (vec) {
+    if (prefer_shared(combine_vec_kernel, dev, 6) != SIMSD_OK) return SIMSD_ERR_LAUNCH;
     return launch(combine_vec_kernel, dim3((unsigned)T), dim3(128), 0, s, (const void*)ys, (long long)H, (const int*)s2r,
                   topk_weight, out, (long long)ld_out, add, (long long)ld_add, T, k, H, dtype);
+  }
+  if (prefer_shared(combine_kernel, dev, 7) != SIMSD_OK) return SIMSD_ERR_LAUNCH;
   return launch(combine_kernel, dim3((unsigned)T), dim3(256), 0, s, (const void*)ys, (long long)H, (const int*)s2r,
                 topk_weight, out, (long long)ld_out, add, (long long)ld_add, T, k, H, dtype);
 }

@@ -100,11 +100,11 @@ struct TileInfo {
 // ordered (group, row chunk, column tile) so a CTA's consecutive tiles reuse
 // the same activation rows.
 template <int BMAX>
-__device__ __forceinline__ TileInfo decode_tile(long long j, const TcGemmArgs& p,
+__device__ __forceinline__ TileInfo decode_tile(int j, const TcGemmArgs& p,
                                                 const int* row_prefix, const int* chunk_prefix) {
   TileInfo ti;
-  const int chunk = (int)(j / p.row_tiles);
-  ti.rtile = (int)(j - (long long)chunk * p.row_tiles);
+  const int chunk = j / p.row_tiles;
+  ti.rtile = j - chunk * p.row_tiles;
   if (p.group_counts == nullptr) {
     ti.group = 0;
     ti.row0 = chunk * BMAX;
@@ -124,13 +124,20 @@ __device__ __forceinline__ TileInfo decode_tile(long long j, const TcGemmArgs& p
   return ti;
 }
 
-__device__ __forceinline__ long long sk_start(long long c, long long iters, long long G) {
-  return (c * iters) / G;
-}
-// CTA whose range holds iteration i.
-__device__ __forceinline__ long long sk_owner(long long i, long long iters, long long G) {
-  return ((i + 1) * G + iters - 1) / iters - 1;
-}
+// Stream-K partition of `iters` (tile, k-block) iterations over G CTAs: the
+// first r = iters % G CTAs take q + 1 = iters / G + 1 iterations, the others q.
+// 32-bit throughout (the host keeps iters below 2^31): these run on every CTA's
+// start-up path, where 64-bit divisions cost close to a microsecond.
+struct SkSplit {
+  int q, r;
+  __host__ __device__ __forceinline__ SkSplit(int iters, int G) : q(iters / G), r(iters - (iters / G) * G) {}
+  __host__ __device__ __forceinline__ int start(int c) const { return c * q + (c < r ? c : r); }
+  // CTA whose range holds iteration i
+  __host__ __device__ __forceinline__ int owner(int i) const {
+    const int t = r * (q + 1);
+    return i < t ? i / (q + 1) : r + (i - t) / q;
+  }
+};
 
 template <int BMAX, int KS, int RING_KB>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcGemmArgs p) {
@@ -236,12 +243,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
   // Partition over G = min(gridDim.x, iters) CTAs so that every partition is
   // non-empty (the tile count is data-dependent in grouped mode); CTAs beyond
   // G have no work.
-  const long long kb = p.kb;
-  const long long iters = total_tiles * kb;
-  const long long G = min((long long)gridDim.x, iters);
-  const long long c = blockIdx.x;
-  const long long it_begin = (c < G) ? sk_start(c, iters, G) : 0;
-  const long long it_end = (c < G) ? sk_start(c + 1, iters, G) : 0;
+  const int kb = p.kb;
+  const int iters = (int)total_tiles * kb;
+  const int G = min((int)gridDim.x, iters);
+  const int c = blockIdx.x;
+  int it_begin = 0, it_end = 0;
+  if (c < G) {
+    const SkSplit sk(iters, G);
+    it_begin = sk.start(c);
+    it_end = sk.start(c + 1);
+  }
 
   if (warp == 4) {
     // ================= TMA producer
@@ -273,10 +284,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                           pend_k0[q] + at * 64, pend_row0[q] + b * TC_BOX_ROWS, pol_x);
         npend = 0;
       };
-      for (long long it = it_begin; ok && it < it_end;) {
-        const long long tile = it / kb;
-        const int kb0 = (int)(it - tile * kb);
-        const int kb1 = (int)min(kb, it_end - tile * kb);
+      for (int it = it_begin; ok && it < it_end;) {
+        const int tile = it / kb;
+        const int kb0 = it - tile * kb;
+        const int kb1 = min(kb, it_end - tile * kb);
         const TileInfo ti = decode_tile<BMAX>(tile, p, row_prefix, chunk_prefix);
         const int nb = (ti.nrows + TC_BOX_ROWS - 1) / TC_BOX_ROWS;
         for (int k = kb0; k < kb1; k += KS) {
@@ -344,10 +355,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
       int acc_iter = 0;
       bool ok = true;
       bool issued_any = false;
-      for (long long it = it_begin; ok && it < it_end;) {
-        const long long tile = it / kb;
-        const int kb0 = (int)(it - tile * kb);
-        const int kb1 = (int)min(kb, it_end - tile * kb);
+      for (int it = it_begin; ok && it < it_end;) {
+        const int tile = it / kb;
+        const int kb0 = it - tile * kb;
+        const int kb1 = min(kb, it_end - tile * kb);
         const TileInfo ti = decode_tile<BMAX>(tile, p, row_prefix, chunk_prefix);
         const int nb = (ti.nrows + TC_BOX_ROWS - 1) / TC_BOX_ROWS;
         const uint32_t idesc = make_idesc_f16(p.is_bf16, 128, nb * TC_BOX_ROWS);
@@ -388,10 +399,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     // ================= epilogue warps 0-3: TMEM lanes 32*warp .. 32*warp+31
     const int row = tid;  // 0..127 == TMEM lane == tile row
     int acc_iter = 0;
-    for (long long it = it_begin; it < it_end;) {
-      const long long tile = it / kb;
-      const int kb0 = (int)(it - tile * kb);
-      const int kb1 = (int)min(kb, it_end - tile * kb);
+    for (int it = it_begin; it < it_end;) {
+      const int tile = it / kb;
+      const int kb0 = it - tile * kb;
+      const int kb1 = min(kb, it_end - tile * kb);
       const TileInfo ti = decode_tile<BMAX>(tile, p, row_prefix, chunk_prefix);
       const int nb = (ti.nrows + TC_BOX_ROWS - 1) / TC_BOX_ROWS;
       const int a = acc_iter & 1;
@@ -451,8 +462,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         // partial K range of this tile: park the fp32 partial in this CTA's slot,
         // laid out [weight row][activation row]; tc_fixup_kernel sums the slots
         // of every split tile in K order right after this kernel.
-        const long long first_tile_of_cta = it_begin / kb;
-        const long long slot = 2 * c + (tile == first_tile_of_cta ? 0 : 1);
+        const int first_tile_of_cta = it_begin / kb;
+        const long long slot = 2LL * c + (tile == first_tile_of_cta ? 0 : 1);
         float* P = p.partials + slot * (long long)(BMAX * 128) + (long long)row * BMAX;
         for (int ch = 0; ch < nb; ++ch) {
           float v[16];
@@ -504,38 +515,41 @@ template <int BMAX>
 __global__ void __launch_bounds__(128) tc_fixup_kernel(const TcFixupArgs p) {
   griddep_launch_dependents();
   griddep_wait();
-  __shared__ int s_tab[2 * (TC_MAX_GROUPS + 1)];
+  // grouped mode only: the GEMM's prefix tables, 2 x (num_groups + 1) ints of
+  // dynamic shared memory (none in single mode, so that these blocks never
+  // keep the next GEMM's CTAs off an SM)
+  extern __shared__ int s_tab[];
   const int row = threadIdx.x;
   const int ch = blockIdx.y;
   const int* row_prefix = s_tab;
-  const int* chunk_prefix = s_tab + TC_MAX_GROUPS + 1;
-  long long total_tiles;
+  const int* chunk_prefix = s_tab + p.num_groups + 1;
+  int total_tiles;
   if (p.group_counts != nullptr) {
-    // the GEMM's prefix tables, copied once into shared memory for the tile search
     for (int g = row; g <= p.num_groups; g += 128) {
       s_tab[g] = p.tables[g];
-      s_tab[TC_MAX_GROUPS + 1 + g] = p.tables[TC_MAX_GROUPS + 1 + g];
+      s_tab[p.num_groups + 1 + g] = p.tables[TC_MAX_GROUPS + 1 + g];
     }
     __syncthreads();
-    total_tiles = (long long)chunk_prefix[p.num_groups] * p.row_tiles;
+    total_tiles = chunk_prefix[p.num_groups] * p.row_tiles;
   } else {
-    total_tiles = (long long)((p.single_rows + BMAX - 1) / BMAX) * p.row_tiles;
+    total_tiles = ((p.single_rows + BMAX - 1) / BMAX) * p.row_tiles;
   }
-  const long long kb = p.kb;
-  const long long iters = total_tiles * kb;
+  const int kb = p.kb;
+  const int iters = total_tiles * kb;
   if (iters == 0) return;
-  const long long G = min((long long)p.grid, iters);
-  const long long cb = (long long)blockIdx.x + 1;      // CTA boundary: start of CTA cb
+  const int G = min(p.grid, iters);
+  const int cb = blockIdx.x + 1;                       // CTA boundary: start of CTA cb
   if (cb >= G) return;
-  const long long ib = sk_start(cb, iters, G);
+  const SkSplit sk(iters, G);
+  const int ib = sk.start(cb);
   if (ib % kb == 0) return;                            // on a tile edge: splits nothing
-  const long long tile = ib / kb;
+  const int tile = ib / kb;
   if (cb > 1) {
-    const long long ip = sk_start(cb - 1, iters, G);
+    const int ip = sk.start(cb - 1);
     if (ip / kb == tile && ip % kb != 0) return;       // an earlier boundary owns this tile
   }
-  const long long c_first = sk_owner(tile * kb, iters, G);
-  const long long c_last = sk_owner(tile * kb + kb - 1, iters, G);
+  const int c_first = sk.owner(tile * kb);
+  const int c_last = sk.owner(tile * kb + kb - 1);
   TcGemmArgs ta;                                       // decode_tile reads only these fields
   ta.group_counts = p.group_counts;
   ta.row_tiles = p.row_tiles;
@@ -543,12 +557,12 @@ __global__ void __launch_bounds__(128) tc_fixup_kernel(const TcFixupArgs p) {
   ta.num_groups = p.num_groups;
   const TileInfo ti = decode_tile<BMAX>(tile, ta, row_prefix, chunk_prefix);
   if (ch * 16 >= ti.nrows) return;
-  const int nseg = (int)(c_last - c_first + 1);
+  const int nseg = c_last - c_first + 1;
   const int odt = p.is_bf16 ? 0 : 1;
   char* outp = reinterpret_cast<char*>(p.out);
   auto slot_of = [&](int i) -> long long {
-    const long long cc = c_first + i;
-    return 2 * cc + ((tile == sk_start(cc, iters, G) / kb) ? 0 : 1);
+    const int cc = c_first + i;
+    return 2LL * cc + ((tile == sk.start(cc) / kb) ? 0 : 1);
   };
   if (!p.silu) {
     const int col = ti.rtile * 128 + row;
