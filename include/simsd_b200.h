@@ -56,6 +56,7 @@ extern "C" {
 
 /* ---- launch flags (process-wide) */
 #define SIMSD_LAUNCH_PDL 1   /* programmatic dependent launch, see simsd_set_launch_flags */
+#define SIMSD_LAUNCH_INKERNEL_REDUCE 2  /* split-K tiles summed inside the GEMM, see below */
 
 /* Library version string. */
 const char* simsd_version(void);
@@ -73,6 +74,10 @@ const char* simsd_status_string(int status);
  * it when the weights passed to simsd_thin_linear are not written by the kernel
  * launched just before it on the same stream (true for inference with fixed
  * weights).
+ * SIMSD_LAUNCH_INKERNEL_REDUCE: a tile whose K range is split over several CTAs
+ * is summed by the last of them to finish (counted per tile in the workspace
+ * header) instead of by a separate reduction kernel launched after the GEMM.
+ * Same summation order, so the two give identical bits.
  */
 int simsd_set_launch_flags(int flags);
 

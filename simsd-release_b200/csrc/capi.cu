@@ -130,6 +130,19 @@ int ring_kb() {
   return v;
 }
 
+// Weight stages a programmatic dependent launch fetches before waiting for the
+// previous kernel: SIMSD_TC_PREFETCH overrides the default.  The activation
+// boxes of those stages queue behind them, so a deep prefetch delays the first
+// MMA once the previous kernel is done.
+int prefetch_stages() {
+  static const int v = env_choice("SIMSD_TC_PREFETCH", {1, 2, 3, 4, 6, 10}, 10);
+  return v;
+}
+
+inline bool use_counters() {
+  return (g_launch_flags.load(std::memory_order_relaxed) & SIMSD_LAUNCH_INKERNEL_REDUCE) != 0;
+}
+
 int ks_for(int bmax) {
   static const int req = env_choice("SIMSD_TC_KS", {1, 2, 4}, 2);
   if (ring_kb() == 96) return std::min(req, bmax <= 32 ? 2 : 1);
@@ -154,6 +167,7 @@ int launch_tc_b(const TcGemmArgs& a, int grid, cudaStream_t s, int dev) {
   }
   TcGemmArgs args = a;
   args.pdl = pdl_on() ? 1 : 0;
+  args.prefetch = prefetch_stages();
   args.trace = (g_trace && g_trace_bytes >= (size_t)grid * 64) ? g_trace : nullptr;
   return launch(tc_gemm_kernel<BMAX, KS, RING>, dim3(grid), dim3(TC_THREADS), smem, s, args);
 }
@@ -294,11 +308,14 @@ int thin_tc_possible(const void* x, long long ldx_m, long long ldx_k, const void
 // ---------------------------------------------------------------- static scratch
 // Scratch of simsd_thin_linear_noalloc: a fixed device array that exists on every
 // GPU that loads this library, from module load until the process exits, so that
-// entry point never allocates.  Bytes [0, 256) hold its error word; the rest holds
-// the split-K partial slots.  Its name is only a host-side handle: the device
+// entry point never allocates.  Its first 64 KiB hold the error word (offset 0)
+// and the per-tile arrival counters (from offset 256; zero from module load, and
+// every launch leaves them zero); the rest holds the split-K partial slots.  Its name is only a host-side handle: the device
 // address comes from cudaGetSymbolAddress, once per device.
 constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;   // 8 MiB
-constexpr size_t kNoAllocHeader = 256;
+constexpr size_t kNoAllocHeader = size_t(64) << 10;
+constexpr size_t kNoAllocCounterOffset = 256;
+constexpr long long kNoAllocCounters = (long long)((kNoAllocHeader - kNoAllocCounterOffset) / 4);
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 void* g_noalloc_ptr[kMaxDev];
 
@@ -338,7 +355,7 @@ const char* simsd_status_string(int s) {
 }
 
 int simsd_set_launch_flags(int flags) {
-  return g_launch_flags.exchange(flags & SIMSD_LAUNCH_PDL);
+  return g_launch_flags.exchange(flags & (SIMSD_LAUNCH_PDL | SIMSD_LAUNCH_INKERNEL_REDUCE));
 }
 
 int simsd_get_launch_flags(void) { return g_launch_flags.load(); }
@@ -427,6 +444,7 @@ int simsd_thin_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w
     a.bias = bias;
     a.partials = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + WS_COUNTER_BYTES);
     a.tables = nullptr;
+    a.counters = use_counters() && pl.tiles <= WS_MAX_COUNTERS ? reinterpret_cast<int*>(workspace) : nullptr;
     a.err = err;
     a.group_counts = nullptr;
     a.num_groups = 1;
@@ -438,7 +456,7 @@ int simsd_thin_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w
     a.three_d = 0;
     a.is_bf16 = dtype == SIMSD_BF16 ? 1 : 0;
     int rc2 = launch_tc(pl.bmax, a, pl.grid, s, dev);
-    if (rc2 != SIMSD_OK || !any_split_tile(pl.tiles, pl.kb, pl.grid)) return rc2;
+    if (rc2 != SIMSD_OK || a.counters != nullptr || !any_split_tile(pl.tiles, pl.kb, pl.grid)) return rc2;
     return launch_fixup(pl.bmax, fixup_args(a, pl.grid), s);
   }
 
@@ -508,6 +526,9 @@ int simsd_thin_linear_noalloc(const void* x, int64_t ldx_m, int64_t ldx_k, const
     a.bias = bias;
     a.partials = reinterpret_cast<float*>(scratch + kNoAllocHeader);
     a.tables = nullptr;
+    a.counters = use_counters() && pl.tiles <= kNoAllocCounters
+                     ? reinterpret_cast<int*>(scratch + kNoAllocCounterOffset)
+                     : nullptr;
     a.err = err;
     a.group_counts = nullptr;
     a.num_groups = 1;
@@ -519,7 +540,7 @@ int simsd_thin_linear_noalloc(const void* x, int64_t ldx_m, int64_t ldx_k, const
     a.three_d = 0;
     a.is_bf16 = dtype == SIMSD_BF16 ? 1 : 0;
     rc = launch_tc(pl.bmax, a, pl.grid, s, dev);
-    if (rc != SIMSD_OK || !any_split_tile(pl.tiles, pl.kb, pl.grid)) return rc;
+    if (rc != SIMSD_OK || a.counters != nullptr || !any_split_tile(pl.tiles, pl.kb, pl.grid)) return rc;
     return launch_fixup(pl.bmax, fixup_args(a, pl.grid), s);
   }
   // layouts the tensor-core kernel cannot read need no scratch beyond the error word
@@ -769,6 +790,7 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
     a.ld_out = I;
     a.partials = reinterpret_cast<float*>(ws + plan.off_part);
     a.tables = reinterpret_cast<int*>(ws + plan.off_tables);
+    a.counters = use_counters() && plan.max_chunks * cdiv(I, 64) <= WS_MAX_COUNTERS ? reinterpret_cast<int*>(ws) : nullptr;
     a.err = err;
     a.group_counts = counts;
     a.num_groups = E;
@@ -779,7 +801,7 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
     a.three_d = 1;
     a.is_bf16 = dtype == SIMSD_BF16 ? 1 : 0;
     rc = launch_tc(plan.bmax, a, plan.grid, s, dev);
-    if (rc == SIMSD_OK) rc = launch_fixup(plan.bmax, fixup_args(a, plan.grid), s);
+    if (rc == SIMSD_OK && a.counters == nullptr) rc = launch_fixup(plan.bmax, fixup_args(a, plan.grid), s);
     if (rc != SIMSD_OK) return rc;
     // down: ys[row, h] = hbuf[row] . w_down[e, h]
     TcGemmArgs d;
@@ -797,6 +819,7 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
     d.ld_out = H;
     d.partials = a.partials;
     d.tables = a.tables;
+    d.counters = use_counters() && plan.max_chunks * cdiv(H, 128) <= WS_MAX_COUNTERS ? reinterpret_cast<int*>(ws) : nullptr;
     d.err = err;
     d.group_counts = counts;
     d.num_groups = E;
@@ -807,7 +830,7 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
     d.three_d = 1;
     d.is_bf16 = a.is_bf16;
     rc = launch_tc(plan.bmax, d, plan.grid, s, dev);
-    if (rc == SIMSD_OK) rc = launch_fixup(plan.bmax, fixup_args(d, plan.grid), s);
+    if (rc == SIMSD_OK && d.counters == nullptr) rc = launch_fixup(plan.bmax, fixup_args(d, plan.grid), s);
     if (rc != SIMSD_OK) return rc;
   } else {
     const long long max_chunks = std::min<long long>(E, S) + S / SIMT_ROWS + 1;

@@ -44,6 +44,7 @@ constexpr int TC_MAX_GROUPS = 1024;
 constexpr int TC_MAX_GRID = 1024;          // CTAs per launch (segments per tile <= this)
 constexpr int WS_COUNTER_BYTES = 256 * 1024;          // head of every workspace (reserved)
 constexpr int WS_ERR_OFFSET = WS_COUNTER_BYTES - 64;  // device error word
+constexpr int WS_MAX_COUNTERS = (WS_COUNTER_BYTES - 256) / 4;  // per-tile arrival counters from offset 0
 constexpr int TC_TABLE_INTS = 2 * (TC_MAX_GROUPS + 1);
 
 struct alignas(64) TcGemmArgs {
@@ -54,6 +55,8 @@ struct alignas(64) TcGemmArgs {
   const void* bias;          // [rows_out] or nullptr (single mode only)
   float* partials;           // [2 * gridDim.x][128 weight rows][BMAX activation rows] fp32
   int* tables;               // grouped mode: row and chunk prefixes for tc_fixup_kernel
+  int* counters;             // per-tile arrival counters (zero on entry and exit); nullptr =
+                             // split tiles are left to tc_fixup_kernel
   int* err;                  // device error word
   const int* group_counts;   // grouped mode: rows per group; nullptr = single mode
   long long ld_out;
@@ -66,6 +69,7 @@ struct alignas(64) TcGemmArgs {
   int three_d;
   int is_bf16;
   int pdl;                   // launched as a programmatic dependent (see griddep_wait)
+  int prefetch;              // ring stages of weights fetched before griddep_wait (single mode, pdl)
   unsigned long long* trace; // optional: 8 %globaltimer stamps per CTA (diagnostics)
 };
 
@@ -139,6 +143,102 @@ struct SkSplit {
   }
 };
 
+// Sum the nseg partial slots of split tile `tile` (contributors c_first ..
+// c_first + nseg - 1, in K order) for activation rows ch*16 .. ch*16+15 and
+// apply the epilogue: bias, or SiLU(gate) * up across the two 64-row halves
+// (threads 0-63 then take rows 0-7 of the chunk and threads 64-127 rows 8-15).
+// Called by 128 threads, `row` = thread index; used by the GEMM's last
+// contributor and by tc_fixup_kernel, so both produce the same bits.
+template <int BMAX>
+__device__ __forceinline__ void reduce_split_chunk(const float* partials, const SkSplit& sk, int kb, int tile,
+                                                   int c_first, int nseg, const TileInfo& ti, int ch, int row,
+                                                   char* outp, long long ld_out, const void* bias, int rows_out,
+                                                   int silu, int odt) {
+  auto slot_of = [&](int i) -> long long {
+    const int cc = c_first + i;
+    return 2LL * cc + ((tile == sk.start(cc) / kb) ? 0 : 1);
+  };
+  if (!silu) {
+    const int col = ti.rtile * 128 + row;
+    float acc[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
+    for (int i0 = 0; i0 < nseg; i0 += 8) {
+      float4 buf[8][4];
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (i0 + q < nseg) {
+          const float4* src = reinterpret_cast<const float4*>(
+              partials + slot_of(i0 + q) * (BMAX * 128) + (long long)row * BMAX + ch * 16);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) buf[q][u] = __ldcg(src + u);
+        }
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (i0 + q < nseg) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            acc[4 * u] = __fadd_rn(acc[4 * u], buf[q][u].x);
+            acc[4 * u + 1] = __fadd_rn(acc[4 * u + 1], buf[q][u].y);
+            acc[4 * u + 2] = __fadd_rn(acc[4 * u + 2], buf[q][u].z);
+            acc[4 * u + 3] = __fadd_rn(acc[4 * u + 3], buf[q][u].w);
+          }
+        }
+    }
+    if (col < rows_out) {
+      const float bv = bias ? load_f(bias, col, odt) : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int t = ch * 16 + j;
+        if (t < ti.nrows) store_f(outp, (long long)(ti.row0 + t) * ld_out + col, __fadd_rn(acc[j], bv), odt);
+      }
+    }
+  } else {
+    // 64 gate rows and their 64 up rows; threads 0-63 take activation rows
+    // 0-7 of the chunk, threads 64-127 rows 8-15
+    const int i = row & 63;
+    const int half = row >> 6;
+    const int col = ti.rtile * 64 + i;
+    float ag[8], au[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { ag[j] = 0.0f; au[j] = 0.0f; }
+    for (int i0 = 0; i0 < nseg; i0 += 4) {
+      float4 bg[4][2], bu[4][2];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (i0 + q < nseg) {
+          const float* base = partials + slot_of(i0 + q) * (BMAX * 128) + ch * 16 + half * 8;
+          const float4* sg = reinterpret_cast<const float4*>(base + (long long)i * BMAX);
+          const float4* su = reinterpret_cast<const float4*>(base + (long long)(64 + i) * BMAX);
+#pragma unroll
+          for (int u = 0; u < 2; ++u) { bg[q][u] = __ldcg(sg + u); bu[q][u] = __ldcg(su + u); }
+        }
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (i0 + q < nseg) {
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            ag[4 * u] = __fadd_rn(ag[4 * u], bg[q][u].x);
+            ag[4 * u + 1] = __fadd_rn(ag[4 * u + 1], bg[q][u].y);
+            ag[4 * u + 2] = __fadd_rn(ag[4 * u + 2], bg[q][u].z);
+            ag[4 * u + 3] = __fadd_rn(ag[4 * u + 3], bg[q][u].w);
+            au[4 * u] = __fadd_rn(au[4 * u], bu[q][u].x);
+            au[4 * u + 1] = __fadd_rn(au[4 * u + 1], bu[q][u].y);
+            au[4 * u + 2] = __fadd_rn(au[4 * u + 2], bu[q][u].z);
+            au[4 * u + 3] = __fadd_rn(au[4 * u + 3], bu[q][u].w);
+          }
+        }
+    }
+    if (col < rows_out) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int t = ch * 16 + half * 8 + j;
+        if (t < ti.nrows) store_f(outp, (long long)(ti.row0 + t) * ld_out + col, silu_mul(ag[j], au[j]), odt);
+      }
+    }
+  }
+}
+
 template <int BMAX, int KS, int RING_KB>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcGemmArgs p) {
   using Cfg = TcConfig<BMAX, KS, RING_KB>;
@@ -157,6 +257,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc);
   volatile int* abort_flag = misc + 1;
   int* sh_total_chunks = misc + 3;
+  volatile int* sh_last = misc + 4;         // epilogue: this CTA reduces the tile it just left
   int* row_prefix = misc + 16;                       // [num_groups + 1]
   int* chunk_prefix = row_prefix + (TC_MAX_GROUPS + 1);
   float* xbuf = reinterpret_cast<float*>(chunk_prefix + (TC_MAX_GROUPS + 1) + 4);  // [16][64]
@@ -247,9 +348,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
   const int iters = (int)total_tiles * kb;
   const int G = min((int)gridDim.x, iters);
   const int c = blockIdx.x;
+  const SkSplit sk(iters, G > 0 ? G : 1);
   int it_begin = 0, it_end = 0;
   if (c < G) {
-    const SkSplit sk(iters, G);
     it_begin = sk.start(c);
     it_end = sk.start(c + 1);
   }
@@ -292,7 +393,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         const int nb = (ti.nrows + TC_BOX_ROWS - 1) / TC_BOX_ROWS;
         for (int k = kb0; k < kb1; k += KS) {
           const int na = min(KS, kb1 - k);
-          if (!dep_ready && npend == STAGES) flush_pending();
+          if (!dep_ready && npend >= min(STAGES, p.prefetch)) flush_pending();
           if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, abort_flag, p.err)) { ok = false; break; }
           const uint32_t fb = smem_u32(&full_bar[stage]);
           mbar_arrive_expect_tx(fb, na * (TC_A_BYTES + nb * TC_BOX_BYTES));
@@ -460,8 +561,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         }
       } else {
         // partial K range of this tile: park the fp32 partial in this CTA's slot,
-        // laid out [weight row][activation row]; tc_fixup_kernel sums the slots
-        // of every split tile in K order right after this kernel.
+        // laid out [weight row][activation row].  The tile's last contributor
+        // to arrive (counted per tile) sums all its slots in K order and writes
+        // the output, so no CTA waits for another; without counters
+        // tc_fixup_kernel does the same right after this kernel.
         const int first_tile_of_cta = it_begin / kb;
         const long long slot = 2LL * c + (tile == first_tile_of_cta ? 0 : 1);
         float* P = p.partials + slot * (long long)(BMAX * 128) + (long long)row * BMAX;
@@ -475,6 +578,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         }
         tc_fence_before();
         mbar_arrive(smem_u32(&acce_bar[a]));
+        if (p.counters != nullptr) {
+          __threadfence();                       // this CTA's partial before its arrival
+          named_bar_sync(1, 128);
+          const int c_first = sk.owner(tile * kb);
+          const int nseg = sk.owner(tile * kb + kb - 1) - c_first + 1;
+          if (row == 0) {
+            const int prev = atomicAdd(&p.counters[tile], 1);
+            const bool last = prev == nseg - 1;
+            if (last) atomicExch(&p.counters[tile], 0);   // ready for the next launch
+            *sh_last = last ? 1 : 0;
+          }
+          named_bar_sync(1, 128);
+          if (*sh_last) {
+            __threadfence();                     // the other contributors' partials
+            for (int ch = 0; ch < nb; ++ch)
+              reduce_split_chunk<BMAX>(p.partials, sk, kb, tile, c_first, nseg, ti, ch, row, outp, p.ld_out,
+                                       p.bias, p.rows_out, p.silu, p.is_bf16 ? 0 : 1);
+          }
+        }
       }
       ++acc_iter;
       it = tile * kb + kb1;
@@ -560,89 +682,8 @@ __global__ void __launch_bounds__(128) tc_fixup_kernel(const TcFixupArgs p) {
   const int nseg = c_last - c_first + 1;
   const int odt = p.is_bf16 ? 0 : 1;
   char* outp = reinterpret_cast<char*>(p.out);
-  auto slot_of = [&](int i) -> long long {
-    const int cc = c_first + i;
-    return 2LL * cc + ((tile == sk.start(cc) / kb) ? 0 : 1);
-  };
-  if (!p.silu) {
-    const int col = ti.rtile * 128 + row;
-    float acc[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
-    for (int i0 = 0; i0 < nseg; i0 += 8) {
-      float4 buf[8][4];
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        if (i0 + q < nseg) {
-          const float4* src = reinterpret_cast<const float4*>(
-              p.partials + slot_of(i0 + q) * (BMAX * 128) + (long long)row * BMAX + ch * 16);
-#pragma unroll
-          for (int u = 0; u < 4; ++u) buf[q][u] = __ldcg(src + u);
-        }
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        if (i0 + q < nseg) {
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            acc[4 * u] = __fadd_rn(acc[4 * u], buf[q][u].x);
-            acc[4 * u + 1] = __fadd_rn(acc[4 * u + 1], buf[q][u].y);
-            acc[4 * u + 2] = __fadd_rn(acc[4 * u + 2], buf[q][u].z);
-            acc[4 * u + 3] = __fadd_rn(acc[4 * u + 3], buf[q][u].w);
-          }
-        }
-    }
-    if (col < p.rows_out) {
-      const float bv = p.bias ? load_f(p.bias, col, odt) : 0.0f;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int t = ch * 16 + j;
-        if (t < ti.nrows) store_f(outp, (long long)(ti.row0 + t) * p.ld_out + col, __fadd_rn(acc[j], bv), odt);
-      }
-    }
-  } else {
-    // 64 gate rows and their 64 up rows; threads 0-63 take activation rows
-    // 0-7 of the chunk, threads 64-127 rows 8-15
-    const int i = row & 63;
-    const int half = row >> 6;
-    const int col = ti.rtile * 64 + i;
-    float ag[8], au[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) { ag[j] = 0.0f; au[j] = 0.0f; }
-    for (int i0 = 0; i0 < nseg; i0 += 4) {
-      float4 bg[4][2], bu[4][2];
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        if (i0 + q < nseg) {
-          const float* base = p.partials + slot_of(i0 + q) * (BMAX * 128) + ch * 16 + half * 8;
-          const float4* sg = reinterpret_cast<const float4*>(base + (long long)i * BMAX);
-          const float4* su = reinterpret_cast<const float4*>(base + (long long)(64 + i) * BMAX);
-#pragma unroll
-          for (int u = 0; u < 2; ++u) { bg[q][u] = __ldcg(sg + u); bu[q][u] = __ldcg(su + u); }
-        }
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        if (i0 + q < nseg) {
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            ag[4 * u] = __fadd_rn(ag[4 * u], bg[q][u].x);
-            ag[4 * u + 1] = __fadd_rn(ag[4 * u + 1], bg[q][u].y);
-            ag[4 * u + 2] = __fadd_rn(ag[4 * u + 2], bg[q][u].z);
-            ag[4 * u + 3] = __fadd_rn(ag[4 * u + 3], bg[q][u].w);
-            au[4 * u] = __fadd_rn(au[4 * u], bu[q][u].x);
-            au[4 * u + 1] = __fadd_rn(au[4 * u + 1], bu[q][u].y);
-            au[4 * u + 2] = __fadd_rn(au[4 * u + 2], bu[q][u].z);
-            au[4 * u + 3] = __fadd_rn(au[4 * u + 3], bu[q][u].w);
-          }
-        }
-    }
-    if (col < p.rows_out) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int t = ch * 16 + half * 8 + j;
-        if (t < ti.nrows) store_f(outp, (long long)(ti.row0 + t) * p.ld_out + col, silu_mul(ag[j], au[j]), odt);
-      }
-    }
-  }
+  reduce_split_chunk<BMAX>(p.partials, sk, kb, tile, c_first, nseg, ti, ch, row, outp, p.ld_out, p.bias,
+                           p.rows_out, p.silu, odt);
 }
 
 }  // namespace simsd

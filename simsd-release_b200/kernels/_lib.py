@@ -30,6 +30,7 @@ EPI_NONE, EPI_SILU_MUL = 0, 1
 PATH_AUTO, PATH_TC, PATH_SIMT = 0, 1, 2
 
 LAUNCH_PDL = 1
+LAUNCH_INKERNEL_REDUCE = 2
 
 DEV_ERR_TIMEOUT = 1
 DEV_ERR_BAD_INDEX = 2
@@ -163,10 +164,23 @@ def clear_device_error(dev: torch.device | None = None) -> None:
               "simsd_workspace_init")
 
 
+def _set_flag(bit: int, enable: bool) -> bool:
+    L = lib()
+    old = L.simsd_get_launch_flags()
+    L.simsd_set_launch_flags((old | bit) if enable else (old & ~bit))
+    return bool(old & bit)
+
+
 def set_pdl(enable: bool) -> bool:
     """Launch kernels as programmatic dependents (weights must not be written by the
     kernel right before each call on the same stream).  Returns the previous setting."""
-    return bool(lib().simsd_set_launch_flags(LAUNCH_PDL if enable else 0) & LAUNCH_PDL)
+    return _set_flag(LAUNCH_PDL, enable)
+
+
+def set_inkernel_reduce(enable: bool) -> bool:
+    """Sum split-K tiles inside the GEMM (last contributor) instead of in a separate
+    reduction kernel; the bits are the same either way.  Returns the previous setting."""
+    return _set_flag(LAUNCH_INKERNEL_REDUCE, enable)
 
 
 class weights_static:

@@ -425,5 +425,25 @@ def test_programmatic_dependent_launch_in_graph():
     assert torch.equal(out, ref)
 
 
+@pytest.mark.parametrize("M,K,N,silu", [(4, 4096, 4096, False), (16, 4096, 6144, False), (32, 12288, 4096, False),
+                                         (64, 4096, 4096, False), (16, 4096, 12288, True), (64, 4096, 3072, True),
+                                         (200, 2048, 512, False), (3, 100, 300, False)])
+def test_inkernel_reduction_matches_fixup_kernel_bitwise(M, K, N, silu):
+    """Split tiles summed by their last contributor inside the GEMM give the same
+    bits as the separate reduction kernel (same slots, same order)."""
+    x = rnd(M, K, seed=M + 7)
+    ws = [rnd(N, K, scale=0.02, seed=N + K + i) for i in range(2 if silu else 1)]
+    f = (lambda: thin_linear_silu_mul(x, *ws)) if silu else (lambda: thin_linear(x, ws[0]))
+    with torch.inference_mode():
+        ref = f()
+        prev = _lib.set_inkernel_reduce(True)
+        try:
+            got = [f() for _ in range(2)]
+        finally:
+            _lib.set_inkernel_reduce(prev)
+        torch.cuda.synchronize()
+    assert all(torch.equal(g, ref) for g in got)
+
+
 def test_no_device_errors_recorded():
     assert _lib.device_error(torch.device(DEV, torch.cuda.current_device())) == 0
