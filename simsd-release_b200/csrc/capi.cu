@@ -13,6 +13,7 @@
 #include "moe.cuh"
 #include "simsd_b200.h"
 #include "simt_gemm.cuh"
+#include "tc_cluster.cuh"
 #include "tc_gemm.cuh"
 
 using namespace simsd;
@@ -292,6 +293,139 @@ ThinPlan plan_thin(int M, int N, int K, int epilogue, int split, int sms) {
   return p;
 }
 
+// ---------------------------------------------------------------- cluster path
+// K atoms per ring stage of tc_cluster_kernel (its ring shares shared memory
+// with the cluster receive buffer, so 64-row tiles use single-atom stages).
+constexpr int cluster_ks(int bmax) { return bmax <= 32 ? 2 : 1; }
+
+template <int BMAX>
+int cluster_prepare(int dev) {
+  constexpr int KS = cluster_ks(BMAX);
+  constexpr int smem = TcClusterConfig<BMAX, KS>::SMEM_BYTES;
+  static bool done[kMaxDev];
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!done[dev]) {
+    if (cudaFuncSetAttribute(tc_cluster_kernel<BMAX, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return SIMSD_ERR_LAUNCH;
+    done[dev] = true;
+  }
+  return SIMSD_OK;
+}
+
+// Clusters of S CTAs of tc_cluster_kernel<BMAX> that fit on the device at once
+// (the occupancy calculator knows how clusters pack into GPCs); 0 if none.
+template <int BMAX>
+int max_clusters_b(int S, int dev) {
+  constexpr int KS = cluster_ks(BMAX);
+  static int cache[kMaxDev][TC_CL_MAX + 1];
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (cache[dev][S] != 0) return cache[dev][S] > 0 ? cache[dev][S] : 0;
+  }
+  if (cluster_prepare<BMAX>(dev) != SIMSD_OK) return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)S);
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = TcClusterConfig<BMAX, KS>::SMEM_BYTES;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = (unsigned)S;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, tc_cluster_kernel<BMAX, KS>, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    n = 0;
+  }
+  std::lock_guard<std::mutex> lk(g_mu);
+  cache[dev][S] = n > 0 ? n : -1;
+  return n > 0 ? n : 0;
+}
+
+int max_clusters(int bmax, int S, int dev) {
+  switch (bmax) {
+    case 16: return max_clusters_b<16>(S, dev);
+    case 32: return max_clusters_b<32>(S, dev);
+    case 64: return max_clusters_b<64>(S, dev);
+  }
+  return 0;
+}
+
+template <int BMAX>
+int launch_cluster_b(const TcClusterArgs& a, int S, int C, cudaStream_t s, int dev) {
+  constexpr int KS = cluster_ks(BMAX);
+  if (cluster_prepare<BMAX>(dev) != SIMSD_OK) return SIMSD_ERR_LAUNCH;
+  TcClusterArgs args = a;
+  args.pdl = pdl_on() ? 1 : 0;
+  args.prefetch = prefetch_stages();
+  args.trace = (g_trace && g_trace_bytes >= (size_t)C * S * 64) ? g_trace : nullptr;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(C * S));
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = TcClusterConfig<BMAX, KS>::SMEM_BYTES;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeClusterDimension;
+  attr[n].val.clusterDim.x = (unsigned)S;
+  attr[n].val.clusterDim.y = 1;
+  attr[n].val.clusterDim.z = 1;
+  ++n;
+  if (pdl_on()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  if (cudaLaunchKernelEx(&cfg, tc_cluster_kernel<BMAX, KS>, args) != cudaSuccess) return SIMSD_ERR_LAUNCH;
+  return cudaGetLastError() == cudaSuccess ? SIMSD_OK : SIMSD_ERR_LAUNCH;
+}
+
+int launch_cluster(int bmax, const TcClusterArgs& a, int S, int C, cudaStream_t s, int dev) {
+  switch (bmax) {
+    case 16: return launch_cluster_b<16>(a, S, C, s, dev);
+    case 32: return launch_cluster_b<32>(a, S, C, s, dev);
+    case 64: return launch_cluster_b<64>(a, S, C, s, dev);
+  }
+  return SIMSD_ERR_UNSUPPORTED;
+}
+
+// Cluster size S and cluster count C for `tiles` output tiles of kb K blocks:
+// the fewest K blocks on any CTA (tiles per cluster x K blocks per rank), then
+// more CTAs, then the smaller cluster.  S = 0: no cluster plan (use stream-K).
+struct ClusterPlan {
+  int S = 0, C = 0;
+};
+ClusterPlan plan_cluster(int bmax, long long tiles, int kb, int dev) {
+  ClusterPlan best;
+  long long best_cost = -1, best_ctas = 0;
+  for (int S = 1; S <= TC_CL_MAX && S <= kb; ++S) {
+    const long long cmax = max_clusters(bmax, S, dev);
+    if (cmax <= 0) continue;
+    const long long c0 = std::min(cmax, tiles);
+    const long long w = cdiv(tiles, c0);
+    const long long C = cdiv(tiles, w);
+    const long long cost = w * cdiv(kb, S);
+    const long long ctas = C * S;
+    if (best_cost < 0 || cost < best_cost || (cost == best_cost && ctas > best_ctas)) {
+      best_cost = cost;
+      best_ctas = ctas;
+      best.S = S;
+      best.C = (int)C;
+    }
+  }
+  return best;
+}
+
+bool cluster_enabled() {
+  static const bool v = env_choice("SIMSD_TC_CLUSTER", {0, 1}, 1) == 1;
+  return v;
+}
+
 int thin_tc_possible(const void* x, long long ldx_m, long long ldx_k, const void* w, long long ldw_n,
                      long long ldw_k, const void* w_up, int M, int N, int K, int dtype) {
   if (dtype != SIMSD_BF16 && dtype != SIMSD_F16) return 0;
@@ -423,6 +557,38 @@ int simsd_thin_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w
     use_tc = false;
   } else {
     use_tc = tc_ok && K >= 64;
+  }
+
+  if (use_tc && M <= 64 && split == 0 && cluster_enabled()) {
+    // M <= 64: split-K tiles reduced inside thread-block clusters
+    const int bmax = pick_bmax_rows(M);
+    const long long row_tiles = silu ? cdiv(N, 64) : cdiv(N, 128);
+    const int kb = (int)cdiv(K, 64);
+    const ClusterPlan cp = plan_cluster(bmax, row_tiles, kb, dev);
+    if (cp.S > 0) {
+      if (ensure_encode() != SIMSD_OK) return SIMSD_ERR_DEVICE;
+      TcClusterArgs a;
+      memset(&a, 0, sizeof(a));
+      const long long lx = (M > 1) ? ldx_m : ((K * 2 + 15) / 16) * 8;
+      const long long lw = (N > 1) ? ldw_n : ((K * 2 + 15) / 16) * 8;
+      const uint64_t xd[2] = {(uint64_t)K, (uint64_t)M}, xs[1] = {(uint64_t)lx * 2};
+      const uint64_t wd[2] = {(uint64_t)K, (uint64_t)N}, wsb[1] = {(uint64_t)lw * 2};
+      int rc = encode_map(&a.tmB, x, dtype, 2, xd, xs, TC_BOX_ROWS);
+      if (rc == SIMSD_OK) rc = encode_map(&a.tmA0, w, dtype, 2, wd, wsb, silu ? 64 : 128);
+      if (rc == SIMSD_OK && silu) rc = encode_map(&a.tmA1, w_up, dtype, 2, wd, wsb, 64);
+      if (rc != SIMSD_OK) return rc;
+      a.out = y;
+      a.bias = bias;
+      a.err = err;
+      a.ld_out = ldy_m;
+      a.rows = M;
+      a.kb = kb;
+      a.rows_out = N;
+      a.row_tiles = (int)row_tiles;
+      a.silu = silu ? 1 : 0;
+      a.is_bf16 = dtype == SIMSD_BF16 ? 1 : 0;
+      return launch_cluster(bmax, a, cp.S, cp.C, s, dev);
+    }
   }
 
   if (use_tc) {

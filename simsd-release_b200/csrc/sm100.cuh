@@ -199,6 +199,91 @@ __host__ __device__ __forceinline__ uint32_t make_idesc_f16(int is_bf16, int M, 
   return d;
 }
 
+// ---------------------------------------------------------------- clusters / DSMEM
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// Every thread of every CTA in the cluster: makes barrier initialisation (and
+// other shared-memory writes before it) visible cluster-wide.  Used once, right
+// after set-up, when no CTA can be held up by another's work.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address in CTA `rank`'s shared memory of the variable at local address `a`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t a, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(rank));
+  return d;
+}
+// 16-byte store into another CTA's shared memory that completes `bytes` of the
+// transaction count of the mbarrier at `remote_bar` (same CTA as the data).
+__device__ __forceinline__ void st_async_v4(uint32_t remote_addr, float a, float b, float c, float d,
+                                            uint32_t remote_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+          remote_addr),
+      "r"(__float_as_uint(a)), "r"(__float_as_uint(b)), "r"(__float_as_uint(c)), "r"(__float_as_uint(d)),
+      "r"(remote_bar)
+      : "memory");
+}
+// Arrive on an mbarrier in another CTA of the cluster, releasing this thread's
+// prior memory accesses (and, through a preceding CTA barrier, its CTA's) at
+// cluster scope.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait (as mbar_wait) for a phase completed by other CTAs of the
+// cluster, acquiring their writes at cluster scope.
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                                  int* err_word) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > SIMSD_WAIT_LIMIT_NS) {
+      *abort_flag = 1;
+      if (err_word) atomicOr(err_word, SIMSD_DEV_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ bool mbar_wait_cluster_drain(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait_cluster(bar, parity)) {
+    if (globaltimer_ns() - t0 > limit_ns) return false;
+  }
+  return true;
+}
+
 // ---------------------------------------------------------------- PDL
 // Programmatic dependent launch: a kernel launched with programmatic stream
 // serialization may start before the previous kernel on its stream finishes;

@@ -1,0 +1,450 @@
+// Thin-M GEMM with the split-K reduction done inside a thread-block cluster.
+//
+// y[m, n] = sum_k x[m, k] w[n, k] (+ bias[n]) or, with the SiLU*mul epilogue,
+// y[m, i] = silu(x . w_gate[i]) * (x . w_up[i]), for M <= 64 activation rows.
+// Same tensor-core pipeline as tc_gemm_kernel (TMA ring of 128 weight rows x
+// 64 K and the activation box, tcgen05 MMA with the weights as the M = 128
+// operand and the activation rows as N, fp32 accumulators in TMEM), but the
+// work is split differently:
+//
+// * the grid is C clusters of S CTAs (S = 1..8); cluster c takes output tiles
+//   c, c + C, c + 2C, ... and CTA rank q of a cluster takes K blocks
+//   [q kb / S, (q + 1) kb / S) of each (the balanced split of SkSplit);
+// * after a tile's K slice, each CTA keeps the accumulator rows it owns (an
+//   S-th of the tile's 128 weight rows; for SiLU*mul the gate row i and up row
+//   64 + i always share an owner) and stores every other row straight into its
+//   owner's shared memory (st.async, completing bytes on the owner's
+//   mbarrier);
+// * each owner sums the S slices of its rows in rank (= K) order and writes
+//   them to y with the epilogue.
+//
+// So a split tile costs one trip over the cluster's shared-memory network — no
+// fp32 partials in global memory and no second kernel — and every output is
+// summed in a fixed order, bit-identical across calls and graph replays.
+//
+// All waits are bounded (sm100.cuh).  Before a CTA leaves it waits until its
+// peers have finished every access to its shared memory: its own receive
+// barrier covers the data sent to it, its free barrier the owners' releases
+// of the last data it sent.
+#pragma once
+#include "sm100.cuh"
+#include "tc_gemm.cuh"
+
+namespace simsd {
+
+constexpr int TC_CL_MAX = 8;          // largest cluster (portable)
+constexpr int TC_CL_RED_ROWS = 144;   // >= S * rows one owner holds, for every S <= 8
+
+struct TcClusterArgs {
+  CUtensorMap tmA0;          // weights (gate rows when silu): 2-D {K, N}
+  CUtensorMap tmA1;          // up rows (silu only)
+  CUtensorMap tmB;           // activations: 2-D {K, M}
+  void* out;                 // y, row stride ld_out elements
+  const void* bias;          // [rows_out] or nullptr
+  int* err;                  // device error word
+  long long ld_out;
+  int rows;                  // M (<= BMAX)
+  int kb;                    // K blocks of 64 (>= cluster size)
+  int rows_out;              // output columns (N, or N of the gate weight with silu)
+  int row_tiles;             // output tiles (128 weight rows, or 64 gate + 64 up rows)
+  int silu, is_bf16, pdl, prefetch;
+  unsigned long long* trace; // optional: 8 %globaltimer stamps per CTA (diagnostics)
+};
+
+template <int BMAX, int KS>
+struct TcClusterConfig {
+  static constexpr int A_ATOM = TC_A_BYTES;
+  static constexpr int B_ATOM = BMAX * 128;
+  static constexpr int A_STAGE = KS * A_ATOM;
+  static constexpr int B_STAGE = KS * B_ATOM;
+  static constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
+  static constexpr int RED_BYTES = TC_CL_RED_ROWS * BMAX * 4;
+  static constexpr int TAIL_BYTES = 2 * 10 * 8 + 8 * 8 + 64 + 64 * 16 * 4;
+  static constexpr int STAGES_RAW = (227 * 1024 - 1024 - RED_BYTES - TAIL_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 10 ? 10 : STAGES_RAW;
+  static constexpr int TMEM_COLS = (2 * BMAX) < 32 ? 32 : 2 * BMAX;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + RED_BYTES + TAIL_BYTES;
+  static_assert(STAGES >= 2, "ring needs two stages");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+  static_assert(BMAX <= 64, "cluster reduction holds at most 64 activation rows");
+};
+
+// Owner (cluster rank) of accumulator row r and the row's index in the owner's
+// receive slot, for cluster size S.  Plain tiles: rows cut into S runs of
+// ceil(128 / S).  SiLU*mul tiles: the pair (i, 64 + i) cut into S runs of
+// ceil(64 / S) pairs; an owner holds its gate rows first, then its up rows.
+struct RowOwner {
+  int S, silu, per;  // per = rows (plain) or pairs (silu) per owner
+  __host__ __device__ __forceinline__ RowOwner(int S_, int silu_)
+      : S(S_), silu(silu_), per(silu_ ? (64 + S_ - 1) / S_ : (128 + S_ - 1) / S_) {}
+  __host__ __device__ __forceinline__ int owner(int r) const { return silu ? (r & 63) / per : r / per; }
+  __host__ __device__ __forceinline__ int local(int r) const {
+    return silu ? (r & 63) - owner(r) * per + (r >= 64 ? per : 0) : r - owner(r) * per;
+  }
+  // rows of one sender's slot in an owner's receive buffer
+  __host__ __device__ __forceinline__ int slot_rows() const { return silu ? 2 * per : per; }
+  // rows owner o holds
+  __host__ __device__ __forceinline__ int rows_of(int o) const {
+    const int total = silu ? 64 : 128;
+    const int n = total - o * per;
+    const int k = n < per ? (n > 0 ? n : 0) : per;
+    return silu ? 2 * k : k;
+  }
+};
+
+template <int BMAX, int KS>
+__global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_constant__ TcClusterArgs p) {
+  using Cfg = TcClusterConfig<BMAX, KS>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * Cfg::A_STAGE;
+  float* red = reinterpret_cast<float*>(sB + STAGES * Cfg::B_STAGE);   // [S][slot rows][BMAX]
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(red) + Cfg::RED_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* accf_bar = empty_bar + STAGES;  // [2]
+  uint64_t* acce_bar = accf_bar + 2;        // [2]
+  uint64_t* drain_bar = acce_bar + 2;       // [1]
+  uint64_t* red_full = drain_bar + 1;       // [1] peers' rows for this CTA have landed
+  uint64_t* red_free = red_full + 1;        // [1] every owner has consumed this CTA's rows
+  int* misc = reinterpret_cast<int*>(red_free + 1);  // 16 ints
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc);
+  volatile int* abort_flag = misc + 1;
+  float* xbuf = reinterpret_cast<float*>(misc + 16);  // [16][64]
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int S = (int)cluster_nctarank();
+  const int q = (int)cluster_ctarank();
+  const int cid = (int)cluster_id_x();
+  const int C = (int)cluster_count_x();
+  if (p.trace && tid == 0) p.trace[blockIdx.x * 8 + 0] = globaltimer_ns();
+
+  // ---- set-up
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&accf_bar[a]), 1);
+      mbar_init(smem_u32(&acce_bar[a]), 128);
+    }
+    mbar_init(smem_u32(drain_bar), 1);
+    mbar_init(smem_u32(red_full), 1);
+    mbar_init(smem_u32(red_free), S > 1 ? S - 1 : 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 4 && lane == 0) {
+    prefetch_tmap(&p.tmA0);
+    if (p.silu) prefetch_tmap(&p.tmA1);
+    prefetch_tmap(&p.tmB);
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (tid == 0) griddep_launch_dependents();
+  tc_fence_before();
+  // barrier initialisation visible to the whole cluster before any remote use
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  if (p.trace && tid == 0) p.trace[blockIdx.x * 8 + 1] = globaltimer_ns();
+
+  const int kb = p.kb;
+  const int tiles = ((p.rows + BMAX - 1) / BMAX) * p.row_tiles;
+  const SkSplit ksplit(kb, S);
+  const int k_lo = ksplit.start(q), k_hi = ksplit.start(q + 1);
+  const int n_tiles = cid < tiles ? (tiles - 1 - cid) / C + 1 : 0;
+  auto tile_of = [&](int i) { return cid + i * C; };
+  const int nrows_all = p.rows < BMAX ? p.rows : BMAX;   // rows <= BMAX: one row block
+  const int nb = (nrows_all + TC_BOX_ROWS - 1) / TC_BOX_ROWS;
+
+  if (warp == 4) {
+    // ================= TMA producer
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_x = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0;
+      uint32_t last_parity = 0;
+      bool ok = true;
+      // Programmatic dependent launch: the first `prefetch` stages of weights
+      // are requested before griddep_wait(); their activation boxes follow it.
+      bool dep_ready = !p.pdl;
+      int npend = 0;
+      bool traced_first = false;
+      uint32_t pend_dst[STAGES], pend_bar[STAGES];
+      int pend_k0[STAGES], pend_na[STAGES];
+      auto flush_pending = [&]() {
+        griddep_wait();
+        dep_ready = true;
+        for (int s2 = 0; s2 < npend; ++s2)
+          for (int at = 0; at < pend_na[s2]; ++at)
+            for (int b = 0; b < nb; ++b)
+              tma_load_2d(pend_dst[s2] + at * Cfg::B_ATOM + b * TC_BOX_BYTES, &p.tmB, pend_bar[s2],
+                          pend_k0[s2] + at * 64, b * TC_BOX_ROWS, pol_x);
+        npend = 0;
+      };
+      for (int i = 0; ok && i < n_tiles; ++i) {
+        const int rtile = tile_of(i);   // one row block: tile index == output tile
+        for (int k = k_lo; k < k_hi; k += KS) {
+          const int na = min(KS, k_hi - k);
+          if (!dep_ready && npend >= min(STAGES, p.prefetch)) flush_pending();
+          if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, abort_flag, p.err)) { ok = false; break; }
+          const uint32_t fb = smem_u32(&full_bar[stage]);
+          mbar_arrive_expect_tx(fb, na * (TC_A_BYTES + nb * TC_BOX_BYTES));
+          issued_mask |= 1u << stage;
+          last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+          const uint32_t b_dst = smem_u32(sB + stage * Cfg::B_STAGE);
+          for (int at = 0; at < na; ++at) {
+            const uint32_t a_dst = smem_u32(sA + stage * Cfg::A_STAGE + at * Cfg::A_ATOM);
+            const int k0 = (k + at) * 64;
+            if (p.silu) {
+              tma_load_2d(a_dst, &p.tmA0, fb, k0, rtile * 64, pol_w);
+              tma_load_2d(a_dst + 8192, &p.tmA1, fb, k0, rtile * 64, pol_w);
+            } else {
+              tma_load_2d(a_dst, &p.tmA0, fb, k0, rtile * 128, pol_w);
+            }
+            if (dep_ready)
+              for (int b = 0; b < nb; ++b)
+                tma_load_2d(b_dst + at * Cfg::B_ATOM + b * TC_BOX_BYTES, &p.tmB, fb, k0, b * TC_BOX_ROWS, pol_x);
+          }
+          if (p.trace && !traced_first) { p.trace[blockIdx.x * 8 + 2] = globaltimer_ns(); traced_first = true; }
+          if (!dep_ready) {
+            pend_dst[npend] = b_dst;
+            pend_bar[npend] = fb;
+            pend_k0[npend] = k * 64;
+            pend_na[npend] = na;
+            ++npend;
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!dep_ready) flush_pending();
+      if (p.trace) p.trace[blockIdx.x * 8 + 4] = globaltimer_ns();
+      if (!ok) {
+        for (int s2 = 0; s2 < STAGES; ++s2)
+          if (issued_mask & (1u << s2))
+            mbar_wait_drain(smem_u32(&full_bar[s2]), (last_parity >> s2) & 1u, 100000000ull);
+      }
+    }
+  } else if (warp == 5) {
+    // ================= MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      bool issued_any = false;
+      const uint32_t idesc = make_idesc_f16(p.is_bf16, 128, nb * TC_BOX_ROWS);
+      for (int i = 0; ok && i < n_tiles; ++i) {
+        const int a = i & 1;
+        const uint32_t aphase = (i >> 1) & 1;
+        if (!mbar_wait(smem_u32(&acce_bar[a]), aphase ^ 1, abort_flag, p.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + a * BMAX;
+        for (int k = k_lo; k < k_hi; k += KS) {
+          const int na = min(KS, k_hi - k);
+          if (!mbar_wait(smem_u32(&full_bar[stage]), phase, abort_flag, p.err)) { ok = false; break; }
+          tc_fence_after();
+          if (p.trace && !issued_any) p.trace[blockIdx.x * 8 + 3] = globaltimer_ns();
+          for (int at = 0; at < na; ++at) {
+            const uint64_t adesc = make_sw128_desc(smem_u32(sA + stage * Cfg::A_STAGE + at * Cfg::A_ATOM));
+            const uint64_t bdesc = make_sw128_desc(smem_u32(sB + stage * Cfg::B_STAGE + at * Cfg::B_ATOM));
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              tc_mma_f16(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (k > k_lo || at > 0 || kk > 0) ? 1u : 0u);
+          }
+          issued_any = true;
+          tc_commit(smem_u32(&empty_bar[stage]));
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(smem_u32(&accf_bar[a]));
+      }
+      if (p.trace) p.trace[blockIdx.x * 8 + 5] = globaltimer_ns();
+      if (!ok && issued_any) {
+        tc_commit(smem_u32(drain_bar));
+        mbar_wait_drain(smem_u32(drain_bar), 0, 100000000ull);
+      }
+    }
+  } else {
+    // ================= epilogue warps 0-3: TMEM lanes 32*warp .. 32*warp+31
+    const int row = tid;   // 0..127 == TMEM lane == accumulator (weight) row
+    const RowOwner ro(S, p.silu);
+    const int own = ro.owner(row);
+    const int lr = ro.local(row);
+    const int slot_rows = ro.slot_rows();
+    const int odt = p.is_bf16 ? 0 : 1;
+    char* outp = reinterpret_cast<char*>(p.out);
+    const uint32_t red_u32 = smem_u32(red);
+    const uint32_t red_full_u32 = smem_u32(red_full);
+    const uint32_t red_free_u32 = smem_u32(red_free);
+    int done = 0;
+    for (int i = 0; i < n_tiles; ++i) {
+      const int rtile = tile_of(i);
+      const int a = i & 1;
+      const uint32_t aphase = (i >> 1) & 1;
+      if (!named_bar_and(1, 128, mbar_wait(smem_u32(&accf_bar[a]), aphase, abort_flag, p.err))) break;
+      tc_fence_after();
+      const uint32_t t_base = tmem_base + ((uint32_t)(warp * 32) << 16) + a * BMAX;
+      const int out_col0 = p.silu ? rtile * 64 : rtile * 128;
+
+      if (S == 1) {
+        // whole K range here: straight to y (as tc_gemm_kernel's whole tiles)
+        for (int ch = 0; ch < nb; ++ch) {
+          float v[16];
+          tmem_ld16(t_base + ch * 16, v);
+          tmem_wait_ld();
+          if (ch == nb - 1) {
+            tc_fence_before();
+            mbar_arrive(smem_u32(&acce_bar[a]));
+          }
+          if (!p.silu) {
+            const int col = out_col0 + row;
+            if (col < p.rows_out) {
+              const float bv = p.bias ? load_f(p.bias, col, odt) : 0.0f;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const int t = ch * 16 + j;
+                if (t < nrows_all) store_f(outp, (long long)t * p.ld_out + col, __fadd_rn(v[j], bv), odt);
+              }
+            }
+          } else {
+            if (row >= 64) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) xbuf[j * 64 + (row - 64)] = v[j];
+            }
+            named_bar_sync(1, 128);
+            if (row < 64) {
+              const int col = out_col0 + row;
+              if (col < p.rows_out) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const int t = ch * 16 + j;
+                  if (t < nrows_all)
+                    store_f(outp, (long long)t * p.ld_out + col, silu_mul(v[j], xbuf[j * 64 + row]), odt);
+                }
+              }
+            }
+            named_bar_sync(1, 128);
+          }
+        }
+        ++done;
+        continue;
+      }
+
+      // -- 1. the owners have consumed this CTA's rows of the previous tile
+      if (i > 0 && !named_bar_and(1, 128, mbar_wait_cluster(red_free_u32, (i - 1) & 1, abort_flag, p.err))) break;
+      // -- 2. bytes this CTA receives for the tile: its rows from every peer
+      if (row == 0) mbar_arrive_expect_tx(red_full_u32, (uint32_t)((S - 1) * ro.rows_of(q) * nb * 64));
+      // -- 3. drain the accumulator: keep own rows, send the others to their owners
+      float mine[BMAX];
+      const uint32_t dst_row = mapa_shared(red_u32 + (uint32_t)(((q * slot_rows) + lr) * BMAX * 4), (uint32_t)own);
+      const uint32_t dst_bar = mapa_shared(red_full_u32, (uint32_t)own);
+#pragma unroll
+      for (int ch = 0; ch < BMAX / 16; ++ch) {
+        if (ch < nb) {
+          float v[16];
+          tmem_ld16(t_base + ch * 16, v);
+          tmem_wait_ld();
+          if (own == q) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) mine[ch * 16 + j] = v[j];
+          } else {
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              st_async_v4(dst_row + (uint32_t)((ch * 16 + 4 * u) * 4), v[4 * u], v[4 * u + 1], v[4 * u + 2],
+                          v[4 * u + 3], dst_bar);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&acce_bar[a]));
+      // -- 4. every peer's rows for this CTA have landed
+      if (!named_bar_and(1, 128, mbar_wait_cluster(red_full_u32, i & 1, abort_flag, p.err))) break;
+      // -- 5. sum the owned rows in rank (= K) order and write them
+#pragma unroll
+      for (int ch = 0; ch < BMAX / 16; ++ch) {
+        if (ch >= nb) break;
+        float acc[16];
+        if (own == q) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
+          for (int r = 0; r < S; ++r) {
+            if (r == q) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) acc[j] = __fadd_rn(acc[j], mine[ch * 16 + j]);
+            } else {
+              const float4* src = reinterpret_cast<const float4*>(red + ((r * slot_rows) + lr) * BMAX + ch * 16);
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const float4 f = src[u];
+                acc[4 * u] = __fadd_rn(acc[4 * u], f.x);
+                acc[4 * u + 1] = __fadd_rn(acc[4 * u + 1], f.y);
+                acc[4 * u + 2] = __fadd_rn(acc[4 * u + 2], f.z);
+                acc[4 * u + 3] = __fadd_rn(acc[4 * u + 3], f.w);
+              }
+            }
+          }
+        }
+        if (!p.silu) {
+          const int col = out_col0 + row;
+          if (own == q && col < p.rows_out) {
+            const float bv = p.bias ? load_f(p.bias, col, odt) : 0.0f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int t = ch * 16 + j;
+              if (t < nrows_all) store_f(outp, (long long)t * p.ld_out + col, __fadd_rn(acc[j], bv), odt);
+            }
+          }
+        } else {
+          if (own == q && row >= 64) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) xbuf[j * 64 + (row - 64)] = acc[j];
+          }
+          named_bar_sync(1, 128);
+          if (own == q && row < 64) {
+            const int col = out_col0 + row;
+            if (col < p.rows_out) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const int t = ch * 16 + j;
+                if (t < nrows_all) store_f(outp, (long long)t * p.ld_out + col, silu_mul(acc[j], xbuf[j * 64 + row]), odt);
+              }
+            }
+          }
+          named_bar_sync(1, 128);
+        }
+      }
+      // -- 6. this CTA's receive buffer is free again: tell every sender
+      named_bar_sync(1, 128);
+      if (row == 0)
+        for (int r = 0; r < S; ++r)
+          if (r != q) mbar_arrive_remote(mapa_shared(red_free_u32, (uint32_t)r));
+      ++done;
+    }
+    // Before leaving: the owners' releases of this CTA's last rows have arrived
+    // (the last access a peer makes to this CTA's shared memory).  Bounded.
+    if (S > 1 && done > 0 && row == 0) mbar_wait_cluster_drain(red_free_u32, (done - 1) & 1, 200000000ull);
+  }
+
+  if (p.trace && tid == 0) {
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    p.trace[blockIdx.x * 8 + 6] = smid;
+  }
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+  if (p.trace && tid == 0) p.trace[blockIdx.x * 8 + 7] = globaltimer_ns();
+}
+
+}  // namespace simsd
