@@ -22,10 +22,10 @@
 // fp32 partials in global memory and no second kernel — and every output is
 // summed in a fixed order, bit-identical across calls and graph replays.
 //
-// All waits are bounded (sm100.cuh).  Before a CTA leaves it waits until its
-// peers have finished every access to its shared memory: its own receive
-// barrier covers the data sent to it, its free barrier the owners' releases
-// of the last data it sent.
+// All waits are bounded (sm100.cuh).  A CTA leaves only after every peer's
+// access to its shared memory is over: the rows sent to it are counted by its
+// receive barrier, and after a cluster's last tile no CTA sends anything more
+// (nor releases a buffer), so the receive wait of that tile is the last one.
 #pragma once
 #include "sm100.cuh"
 #include "tc_gemm.cuh"
@@ -285,6 +285,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
     const uint32_t red_u32 = smem_u32(red);
     const uint32_t red_full_u32 = smem_u32(red_full);
     const uint32_t red_free_u32 = smem_u32(red_free);
+    auto swz = [](int lr, int j) { return BMAX >= 32 ? (j ^ (lr & 7)) : (j ^ ((lr >> 1) & 3)); };
     int done = 0;
     for (int i = 0; i < n_tiles; ++i) {
       const int rtile = tile_of(i);
@@ -346,6 +347,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
       // -- 3. drain the accumulator: keep own rows, send the others to their owners
       float mine[BMAX];
       const uint32_t dst_row = mapa_shared(red_u32 + (uint32_t)(((q * slot_rows) + lr) * BMAX * 4), (uint32_t)own);
+      // 16-byte column group j of a received row sits at group swz(j): the XOR
+      // spreads the rows that one quarter-warp touches over all 32 banks
       const uint32_t dst_bar = mapa_shared(red_full_u32, (uint32_t)own);
 #pragma unroll
       for (int ch = 0; ch < BMAX / 16; ++ch) {
@@ -359,7 +362,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
           } else {
 #pragma unroll
             for (int u = 0; u < 4; ++u)
-              st_async_v4(dst_row + (uint32_t)((ch * 16 + 4 * u) * 4), v[4 * u], v[4 * u + 1], v[4 * u + 2],
+              st_async_v4(dst_row + (uint32_t)(swz(lr, ch * 4 + u) * 16), v[4 * u], v[4 * u + 1], v[4 * u + 2],
                           v[4 * u + 3], dst_bar);
           }
         }
@@ -368,70 +371,64 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
       mbar_arrive(smem_u32(&acce_bar[a]));
       // -- 4. every peer's rows for this CTA have landed
       if (!named_bar_and(1, 128, mbar_wait_cluster(red_full_u32, i & 1, abort_flag, p.err))) break;
-      // -- 5. sum the owned rows in rank (= K) order and write them
+      // -- 5. park this CTA's own rows in its (otherwise unused) slot, then all
+      // 128 threads share the owned outputs: each sums one (row, activation
+      // row) over the S slots in rank (= K) order and writes it to y
+      if (own == q) {
+        float4* dst = reinterpret_cast<float4*>(red + ((q * slot_rows) + lr) * BMAX);
 #pragma unroll
-      for (int ch = 0; ch < BMAX / 16; ++ch) {
-        if (ch >= nb) break;
-        float acc[16];
-        if (own == q) {
+        for (int ch = 0; ch < BMAX / 16; ++ch) {
+          if (ch >= nb) break;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
-          for (int r = 0; r < S; ++r) {
-            if (r == q) {
-#pragma unroll
-              for (int j = 0; j < 16; ++j) acc[j] = __fadd_rn(acc[j], mine[ch * 16 + j]);
-            } else {
-              const float4* src = reinterpret_cast<const float4*>(red + ((r * slot_rows) + lr) * BMAX + ch * 16);
-#pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const float4 f = src[u];
-                acc[4 * u] = __fadd_rn(acc[4 * u], f.x);
-                acc[4 * u + 1] = __fadd_rn(acc[4 * u + 1], f.y);
-                acc[4 * u + 2] = __fadd_rn(acc[4 * u + 2], f.z);
-                acc[4 * u + 3] = __fadd_rn(acc[4 * u + 3], f.w);
-              }
-            }
-          }
-        }
-        if (!p.silu) {
-          const int col = out_col0 + row;
-          if (own == q && col < p.rows_out) {
-            const float bv = p.bias ? load_f(p.bias, col, odt) : 0.0f;
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int t = ch * 16 + j;
-              if (t < nrows_all) store_f(outp, (long long)t * p.ld_out + col, __fadd_rn(acc[j], bv), odt);
-            }
-          }
-        } else {
-          if (own == q && row >= 64) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) xbuf[j * 64 + (row - 64)] = acc[j];
-          }
-          named_bar_sync(1, 128);
-          if (own == q && row < 64) {
-            const int col = out_col0 + row;
-            if (col < p.rows_out) {
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const int t = ch * 16 + j;
-                if (t < nrows_all) store_f(outp, (long long)t * p.ld_out + col, silu_mul(acc[j], xbuf[j * 64 + row]), odt);
-              }
-            }
-          }
-          named_bar_sync(1, 128);
+          for (int u = 0; u < 4; ++u)
+            dst[swz(lr, ch * 4 + u)] = make_float4(mine[ch * 16 + 4 * u], mine[ch * 16 + 4 * u + 1],
+                                                   mine[ch * 16 + 4 * u + 2], mine[ch * 16 + 4 * u + 3]);
         }
       }
-      // -- 6. this CTA's receive buffer is free again: tell every sender
       named_bar_sync(1, 128);
-      if (row == 0)
-        for (int r = 0; r < S; ++r)
-          if (r != q) mbar_arrive_remote(mapa_shared(red_free_u32, (uint32_t)r));
+      {
+        // owned rows (plain) or pairs (silu), in the slot's local order
+        const int units = p.silu ? ro.rows_of(q) / 2 : ro.rows_of(q);
+        const int first = q * ro.per;   // first owned row (plain) or pair (silu)
+        auto slot_val = [&](int r, int l, int t) -> float {
+          return red[((r * slot_rows) + l) * BMAX + swz(l, t >> 2) * 4 + (t & 3)];
+        };
+        for (int e = row; e < units * nrows_all; e += 128) {
+          const int t = e / units;          // activation row
+          const int l = e - t * units;      // owned unit; consecutive threads -> consecutive columns
+          const int col = (p.silu ? rtile * 64 : rtile * 128) + first + l;
+          if (col >= p.rows_out) continue;
+          if (!p.silu) {
+            float acc = 0.0f;
+            for (int r = 0; r < S; ++r) acc = __fadd_rn(acc, slot_val(r, l, t));
+            const float bv = p.bias ? load_f(p.bias, col, odt) : 0.0f;
+            store_f(outp, (long long)t * p.ld_out + col, __fadd_rn(acc, bv), odt);
+          } else {
+            float g = 0.0f, u = 0.0f;
+            for (int r = 0; r < S; ++r) {
+              g = __fadd_rn(g, slot_val(r, l, t));
+              u = __fadd_rn(u, slot_val(r, ro.per + l, t));
+            }
+            store_f(outp, (long long)t * p.ld_out + col, silu_mul(g, u), odt);
+          }
+        }
+      }
+      // -- 6. this CTA's receive buffer is free again: tell every sender.  Not
+      // after the last tile: nothing is sent after it, so once its rows have
+      // landed here (step 4) no peer touches this CTA's shared memory again and
+      // every CTA may leave as soon as its own rows are written.
+      if (i + 1 < n_tiles) {
+        named_bar_sync(1, 128);
+        if (row == 0)
+          for (int r = 0; r < S; ++r)
+            if (r != q) mbar_arrive_remote(mapa_shared(red_free_u32, (uint32_t)r));
+      }
       ++done;
     }
-    // Before leaving: the owners' releases of this CTA's last rows have arrived
-    // (the last access a peer makes to this CTA's shared memory).  Bounded.
-    if (S > 1 && done > 0 && row == 0) mbar_wait_cluster_drain(red_free_u32, (done - 1) & 1, 200000000ull);
+    if (S > 1 && done < n_tiles && row == 0) {
+      // aborting: give peers that may still be sending to this CTA time to land
+      mbar_wait_cluster_drain(red_full_u32, done & 1, 100000000ull);
+    }
   }
 
   if (p.trace && tid == 0) {
