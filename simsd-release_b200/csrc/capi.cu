@@ -136,12 +136,19 @@ int ring_kb() {
 // boxes of those stages queue behind them, so a deep prefetch delays the first
 // MMA once the previous kernel is done.
 int prefetch_stages() {
-  static const int v = env_choice("SIMSD_TC_PREFETCH", {1, 2, 3, 4, 6, 10}, 10);
+  static const int v = env_choice("SIMSD_TC_PREFETCH", {1, 2, 3, 4, 6, 10}, 2);
   return v;
 }
 
 inline bool use_counters() {
   return (g_launch_flags.load(std::memory_order_relaxed) & SIMSD_LAUNCH_INKERNEL_REDUCE) != 0;
+}
+
+// Weight stages the cluster GEMM requests into L2 ahead of its shared-memory
+// ring: SIMSD_TC_L2_AHEAD overrides the default.
+int l2_ahead_stages() {
+  static const int v = env_choice("SIMSD_TC_L2_AHEAD", {0, 2, 4, 8, 12, 16, 24}, 0);
+  return v;
 }
 
 int ks_for(int bmax) {
@@ -361,6 +368,7 @@ int launch_cluster_b(const TcClusterArgs& a, int S, int C, cudaStream_t s, int d
   TcClusterArgs args = a;
   args.pdl = pdl_on() ? 1 : 0;
   args.prefetch = prefetch_stages();
+  args.l2_ahead = l2_ahead_stages();
   args.trace = (g_trace && g_trace_bytes >= (size_t)C * S * 64) ? g_trace : nullptr;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(C * S));

@@ -120,6 +120,17 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
+// Fetch a 2-D box of a tensor into L2 only (no shared memory, no barrier): lets
+// a weight stream keep more DRAM requests in flight than its shared-memory ring
+// holds.  Same coordinate rules as tma_load_2d.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int c0, int c1, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.prefetch.tensor.2d.L2.global.tile.L2::cache_hint [%0, {%1, %2}], %3;" ::"l"(
+          reinterpret_cast<uint64_t>(tmap)),
+      "r"(c0), "r"(c1), "l"(policy)
+      : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),

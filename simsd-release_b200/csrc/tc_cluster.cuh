@@ -48,6 +48,7 @@ struct TcClusterArgs {
   int rows_out;              // output columns (N, or N of the gate weight with silu)
   int row_tiles;             // output tiles (128 weight rows, or 64 gate + 64 up rows)
   int silu, is_bf16, pdl, prefetch;
+  int l2_ahead;              // ring stages of weights requested into L2 ahead of the ring
   unsigned long long* trace; // optional: 8 %globaltimer stamps per CTA (diagnostics)
 };
 
@@ -191,10 +192,29 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
                           pend_k0[s2] + at * 64, b * TC_BOX_ROWS, pol_x);
         npend = 0;
       };
+      // L2 prefetch cursor over the (tile, stage) sequence: DRAM requests for the
+      // weights run l2_ahead stages ahead of the shared-memory ring
+      const int nsteps = (k_hi - k_lo + KS - 1) / KS;
+      const int total_steps = n_tiles * nsteps;
+      int pf = 0, step = 0;
       for (int i = 0; ok && i < n_tiles; ++i) {
         const int rtile = tile_of(i);   // one row block: tile index == output tile
-        for (int k = k_lo; k < k_hi; k += KS) {
+        for (int k = k_lo; k < k_hi; k += KS, ++step) {
           const int na = min(KS, k_hi - k);
+          if (pf <= step) pf = step + 1;
+          for (; pf < total_steps && pf <= step + p.l2_ahead; ++pf) {
+            const int pi = pf / nsteps;
+            const int pk = k_lo + (pf - pi * nsteps) * KS;
+            const int prt = tile_of(pi);
+            for (int at = 0; at < KS && pk + at < k_hi; ++at) {
+              if (p.silu) {
+                tma_prefetch_l2_2d(&p.tmA0, (pk + at) * 64, prt * 64, pol_w);
+                tma_prefetch_l2_2d(&p.tmA1, (pk + at) * 64, prt * 64, pol_w);
+              } else {
+                tma_prefetch_l2_2d(&p.tmA0, (pk + at) * 64, prt * 128, pol_w);
+              }
+            }
+          }
           if (!dep_ready && npend >= min(STAGES, p.prefetch)) flush_pending();
           if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, abort_flag, p.err)) { ok = false; break; }
           const uint32_t fb = smem_u32(&full_bar[stage]);
@@ -387,29 +407,44 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
       }
       named_bar_sync(1, 128);
       {
-        // owned rows (plain) or pairs (silu), in the slot's local order
+        // owned rows (plain) or pairs (silu), in the slot's local order; each
+        // thread takes one unit and 4 consecutive activation rows (one 16-byte
+        // group of every slot), consecutive threads consecutive columns
         const int units = p.silu ? ro.rows_of(q) / 2 : ro.rows_of(q);
         const int first = q * ro.per;   // first owned row (plain) or pair (silu)
-        auto slot_val = [&](int r, int l, int t) -> float {
-          return red[((r * slot_rows) + l) * BMAX + swz(l, t >> 2) * 4 + (t & 3)];
+        const int groups = (nrows_all + 3) >> 2;
+        auto slot4 = [&](int r, int l, int g) -> float4 {
+          return reinterpret_cast<const float4*>(red + ((r * slot_rows) + l) * BMAX)[swz(l, g)];
         };
-        for (int e = row; e < units * nrows_all; e += 128) {
-          const int t = e / units;          // activation row
-          const int l = e - t * units;      // owned unit; consecutive threads -> consecutive columns
+        for (int e = row; e < units * groups; e += 128) {
+          const int g = e / units;
+          const int l = e - g * units;
           const int col = (p.silu ? rtile * 64 : rtile * 128) + first + l;
           if (col >= p.rows_out) continue;
-          if (!p.silu) {
-            float acc = 0.0f;
-            for (int r = 0; r < S; ++r) acc = __fadd_rn(acc, slot_val(r, l, t));
-            const float bv = p.bias ? load_f(p.bias, col, odt) : 0.0f;
-            store_f(outp, (long long)t * p.ld_out + col, __fadd_rn(acc, bv), odt);
-          } else {
-            float g = 0.0f, u = 0.0f;
-            for (int r = 0; r < S; ++r) {
-              g = __fadd_rn(g, slot_val(r, l, t));
-              u = __fadd_rn(u, slot_val(r, ro.per + l, t));
+          float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f), b = a;
+          for (int r = 0; r < S; ++r) {
+            const float4 f = slot4(r, l, g);
+            a.x = __fadd_rn(a.x, f.x);
+            a.y = __fadd_rn(a.y, f.y);
+            a.z = __fadd_rn(a.z, f.z);
+            a.w = __fadd_rn(a.w, f.w);
+            if (p.silu) {
+              const float4 h = slot4(r, ro.per + l, g);
+              b.x = __fadd_rn(b.x, h.x);
+              b.y = __fadd_rn(b.y, h.y);
+              b.z = __fadd_rn(b.z, h.z);
+              b.w = __fadd_rn(b.w, h.w);
             }
-            store_f(outp, (long long)t * p.ld_out + col, silu_mul(g, u), odt);
+          }
+          const float va[4] = {a.x, a.y, a.z, a.w};
+          const float vb[4] = {b.x, b.y, b.z, b.w};
+          const float bv = (!p.silu && p.bias) ? load_f(p.bias, col, odt) : 0.0f;
+#pragma unroll
+          for (int k4 = 0; k4 < 4; ++k4) {
+            const int t = 4 * g + k4;
+            if (t < nrows_all)
+              store_f(outp, (long long)t * p.ld_out + col, p.silu ? silu_mul(va[k4], vb[k4]) : __fadd_rn(va[k4], bv),
+                      odt);
           }
         }
       }
