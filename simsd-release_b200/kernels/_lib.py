@@ -8,6 +8,7 @@ buffer (kernels/thin_linear_fused.py:173-190); `reset_workspace()` drops them
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 from pathlib import Path
 
@@ -100,6 +101,27 @@ def check(rc: int, what: str) -> None:
 
 def stream_ptr(dev: torch.device) -> int:
     return torch.cuda.current_stream(dev).cuda_stream
+
+
+def device_guard(dev: torch.device):
+    """`torch.cuda.device(dev)` when `dev` is not the current device (tensors of a
+    sharded model may live elsewhere); a no-op context otherwise, which keeps the
+    common call cheap."""
+    if dev.index is None or dev.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(dev)
+
+
+_WS_SIZES: dict[tuple, int] = {}
+
+
+def thin_workspace_size(dev_index: int, M: int, N: int, K: int, code: int, epilogue: int, split: int) -> int:
+    """simsd_thin_linear_workspace_size, memoised (pure arithmetic for a device)."""
+    key = (dev_index, M, N, K, code, epilogue, split)
+    v = _WS_SIZES.get(key)
+    if v is None:
+        v = _WS_SIZES[key] = lib().simsd_thin_linear_workspace_size(M, N, K, code, epilogue, split)
+    return v
 
 
 def require_cuda(*tensors: torch.Tensor) -> torch.device:

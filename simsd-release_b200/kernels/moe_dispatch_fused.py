@@ -66,7 +66,7 @@ def align(topk_ids: torch.Tensor, E: int, block_m: int = BLOCK_M, num_tiles: int
     if reference_layout:
         out["slots"] = torch.empty(num_tiles * block_m, **i32)
         out["tile_expert"] = torch.empty(num_tiles, **i32)
-    with torch.cuda.device(dev):
+    with _lib.device_guard(dev):
         rc = _lib.lib().simsd_moe_align(
             flat.data_ptr(), S, E, out["counts"].data_ptr(), out["offsets"].data_ptr(),
             out["sorted_slots"].data_ptr(), out["slot_to_row"].data_ptr(), block_m, num_tiles,
@@ -110,7 +110,7 @@ def moe_route(x: torch.Tensor, w_router: torch.Tensor, bias: torch.Tensor | None
     ids = torch.empty((T, k), dtype=torch.int64, device=dev)
     wts = torch.empty((T, k), dtype=torch.float32, device=dev)
     logits = torch.empty((T, E), dtype=torch.float32, device=dev) if return_logits else None
-    with torch.cuda.device(dev):
+    with _lib.device_guard(dev):
         rc = _lib.lib().simsd_moe_route(
             x.data_ptr(), x.stride(0), _lib.dtype_code(x.dtype),
             w_router.data_ptr(), w_router.stride(0), _lib.dtype_code(w_router.dtype),
@@ -165,7 +165,7 @@ def moe_dispatch(x, topk_ids, topk_weight, w_gate, w_up, w_down, add=None):
         if add.stride(1) != 1:
             add = add.contiguous()
     L = _lib.lib()
-    with torch.cuda.device(dev):
+    with _lib.device_guard(dev):
         nbytes = L.simsd_moe_workspace_size(T, k, E, H, I, code)
         ws = _lib.workspace(dev, nbytes)
         rc = L.simsd_moe_dispatch(

@@ -127,8 +127,8 @@ def thin_linear(x: torch.Tensor, w: torch.Tensor,
         if tuned is not None:
             split = int(tuned[3])
     L = _lib.lib()
-    with torch.cuda.device(dev):
-        nbytes = L.simsd_thin_linear_workspace_size(M, N, K, code, _lib.EPI_NONE, split)
+    with _lib.device_guard(dev):
+        nbytes = _lib.thin_workspace_size(torch.cuda.current_device(), M, N, K, code, _lib.EPI_NONE, split)
         ws = _lib.workspace(dev, nbytes)
         rc = L.simsd_thin_linear(
             x2.data_ptr(), x2.stride(0), x2.stride(1),
@@ -173,8 +173,8 @@ def thin_linear_silu_mul(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tens
         return y.zero_().view(out_shape)
     x2 = x.reshape(M, K)
     L = _lib.lib()
-    with torch.cuda.device(dev):
-        nbytes = L.simsd_thin_linear_workspace_size(M, I, K, code, _lib.EPI_SILU_MUL, split)
+    with _lib.device_guard(dev):
+        nbytes = _lib.thin_workspace_size(torch.cuda.current_device(), M, I, K, code, _lib.EPI_SILU_MUL, split)
         ws = _lib.workspace(dev, nbytes)
         rc = L.simsd_thin_linear(
             x2.data_ptr(), x2.stride(0), x2.stride(1),
