@@ -160,6 +160,7 @@ def make_inputs(dev, seed=7):
 
 
 def run_step(ws, xs, world, dist, outs=None):
+    from kernels.parallel import gather_columns
     from kernels.thin_linear_fused import thin_linear, thin_linear_silu_mul
     res = []
     for M in MS:
@@ -167,9 +168,7 @@ def run_step(ws, xs, world, dist, outs=None):
             x = xs[M][K]
             y = thin_linear_silu_mul(x, *ws[name]) if silu else thin_linear(x, ws[name])
             if world > 1:
-                gathered = torch.empty((world, *y.shape), dtype=y.dtype, device=y.device)
-                dist.all_gather_into_tensor(gathered, y)
-                y = gathered.permute(1, 0, 2).reshape(M, -1)
+                y = gather_columns(y)
             res.append(y)
     return res
 
