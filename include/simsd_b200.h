@@ -54,6 +54,11 @@ extern "C" {
 #define SIMSD_PATH_TC 1      /* force the tcgen05/TMA kernel (SIMSD_ERR_ALIGN if not possible) */
 #define SIMSD_PATH_SIMT 2    /* force the CUDA-core kernel                            */
 
+/* ---- device error bits (OR-ed into a device error word) */
+#define SIMSD_DEV_ERR_TIMEOUT   1   /* a bounded wait ran out (the kernel gave up cleanly) */
+#define SIMSD_DEV_ERR_BAD_INDEX 2   /* an expert id >= E */
+#define SIMSD_DEV_ERR_CAPACITY  4   /* an expert-parallel bucket overflowed */
+
 /* ---- launch flags (process-wide) */
 #define SIMSD_LAUNCH_PDL 1   /* programmatic dependent launch, see simsd_set_launch_flags */
 #define SIMSD_LAUNCH_INKERNEL_REDUCE 2  /* split-K tiles summed inside the GEMM, see below */
@@ -181,9 +186,13 @@ int simsd_moe_route(const void* x, int64_t ldx, int x_dtype, const void* wr, int
  * Expert align: per-expert counts, offsets and the stable slot permutation.
  * Replaces _align - kernels/moe_dispatch_fused.py:93-132 (bit-exact).
  *
- *   topk_ids [S] int64 (S = T*k, slot s = t*k + j), 0 <= id < E <= 1024
+ *   topk_ids [S] int64 (S = T*k, slot s = t*k + j), 0 <= id < E <= 1024; a
+ *   negative id is a slot without an expert (an empty expert-parallel bucket
+ *   entry): it is left out silently; an id >= E is left out and raises
+ *   SIMSD_DEV_ERR_BAD_INDEX.  (The reference has no such slots.)
  *   counts [E], offsets [E+1] (exclusive prefix of counts), sorted_slots [S]
- *   (= argsort(ids, stable=True)), slot_to_row [S] (its inverse; -1 for an invalid id)
+ *   (= argsort(ids, stable=True) over the kept slots, then -1), slot_to_row [S]
+ *   (its inverse; -1 for a slot left out)
  *   slots_padded [num_tiles*block_m] and tile_expert [num_tiles]: optional (both NULL
  *   or both set) copies in the reference's padded layout (`slots`, `tile_expert`).
  *   `err_word`: device int that receives SIMSD_DEV_ERR bits, or NULL.
@@ -209,6 +218,7 @@ size_t simsd_moe_workspace_size(int T, int k, int E, int H, int I, int dtype);
  *   w_down [E, H, I]:       element (e, h, i) at base + e*ldd_e + h*ldd_h + i
  *   out [T, H] (row stride ld_out), add [T, H] (row stride ld_add) or NULL.
  *   dtype: x, weights, out and add share it (SIMSD_BF16 | SIMSD_F16 | SIMSD_F32).
+ * Slots whose id is negative contribute nothing (see simsd_moe_align).
  */
 int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids,
                        const float* topk_weight, const void* w_gate, const void* w_up,
@@ -216,6 +226,42 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids,
                        int64_t ldd_h, void* out, int64_t ld_out, const void* add,
                        int64_t ld_add, int T, int k, int E, int H, int I, int dtype,
                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- expert parallelism (no counterpart in the reference, which runs the MoE
+ * layer on one GPU): experts split over `world` ranks in contiguous blocks of
+ * E / world, tokens routed on their owner rank, rows exchanged with all-to-all
+ * in fixed-capacity per-peer buckets (so the exchange is CUDA-graph capturable),
+ * each rank running simsd_moe_dispatch on the rows it receives (k = 1, weight 1,
+ * negative id = empty entry), and the owner combining the returned rows. */
+
+/*
+ * Bucket plan of this rank's slots: for slot s = t*k + j with expert e =
+ * topk_ids[s], peer = e / (E / world); in slot order each peer's slots take
+ * positions 0, 1, ... of its bucket: send_slot[peer*capacity + i] = s,
+ * send_expert[...] = e % (E / world), slot_pos[s] = peer*capacity + i.  Unused
+ * bucket entries are -1.  A slot past `capacity` (SIMSD_DEV_ERR_CAPACITY) or with
+ * an id outside [0, E) (SIMSD_DEV_ERR_BAD_INDEX for id >= E) gets slot_pos -1.
+ * counts[peer] = slots bound for the peer.  E % world == 0, world <= 64.
+ */
+int simsd_moe_ep_plan(const int64_t* topk_ids, int S, int E, int world, int capacity,
+                      int32_t* send_slot, int32_t* send_expert, int32_t* slot_pos,
+                      int32_t* counts, int* err_word, void* stream);
+
+/*
+ * out[r, :] = x[slots[r] / k, :] for r < R; rows with slots[r] < 0 are left as
+ * they are.  x [*, H] row stride ldx, out [R, H] row stride ld_out.
+ */
+int simsd_moe_gather_rows(const void* x, int64_t ldx, const int32_t* slots, int R, int k, int H,
+                          int dtype, void* out, int64_t ld_out, void* stream);
+
+/*
+ * out[t] = cast( sum_j fp32(ys[slot_row[t*k + j]]) * topk_weight[t, j] ) over
+ * j in order, rows -1 skipped; with `add`, out[t] = cast(cast(sum) + add[t]).
+ * The combine step of simsd_moe_dispatch on rows the caller supplies.
+ */
+int simsd_moe_combine(const void* ys, int64_t ldys, const int32_t* slot_row,
+                      const float* topk_weight, void* out, int64_t ld_out, const void* add,
+                      int64_t ld_add, int T, int k, int H, int dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -148,3 +148,33 @@ def moe_dispatch(x, ids, w, wg, wu, wd, add=None, mode: int = 0):
     lib().oracle_moe_dispatch(_p(x), _p(ids), _p(w), _p(wg), _p(wu), _p(wd), _p(a), T, k, E, H, I,
                               _dt(x), mode, _p(acc), _p(out))
     return acc, out
+
+
+def ep_plan(ids: np.ndarray, E: int, world: int, cap: int):
+    """Per-peer buckets of slots for the expert-parallel MoE layer (numpy).
+
+    The reference runs its MoE layer on one GPU and has no such step; this is
+    the contract of simsd_moe_ep_plan, restated for the checks: expert e lives
+    on rank e // (E // world) as local expert e % (E // world); each peer's
+    slots, in slot order (the stable order moe_infer's argsort gives within an
+    expert, kernels/workspace/moe_dispatch/build_oracle.py:34-67), fill its
+    bucket from position 0; slots past `cap` or with ids outside [0, E) are not
+    sent (slot_pos -1).
+    """
+    flat = np.asarray(ids, dtype=np.int64).reshape(-1)
+    epr = E // world
+    send_slot = np.full(world * cap, -1, np.int32)
+    send_expert = np.full(world * cap, -1, np.int32)
+    slot_pos = np.full(flat.size, -1, np.int32)
+    counts = np.zeros(world, np.int32)
+    for s, e in enumerate(flat):
+        if e < 0 or e >= E:
+            continue
+        peer = int(e) // epr
+        pos = counts[peer]
+        counts[peer] += 1
+        if pos < cap:
+            send_slot[peer * cap + pos] = s
+            send_expert[peer * cap + pos] = int(e) - peer * epr
+            slot_pos[s] = peer * cap + pos
+    return {"send_slot": send_slot, "send_expert": send_expert, "slot_pos": slot_pos, "counts": counts}

@@ -1058,4 +1058,63 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
                 topk_weight, out, (long long)ld_out, add, (long long)ld_add, T, k, H, dtype);
 }
 
+int simsd_moe_ep_plan(const int64_t* topk_ids, int S, int E, int world, int capacity, int32_t* send_slot,
+                      int32_t* send_expert, int32_t* slot_pos, int32_t* counts, int* err_word, void* stream) {
+  if (S < 0 || E < 1 || world < 1 || world > EP_MAX_WORLD || E % world != 0 || capacity < 0) return SIMSD_ERR_SHAPE;
+  if (S > 0 && (topk_ids == nullptr || slot_pos == nullptr)) return SIMSD_ERR_SHAPE;
+  if (capacity > 0 && (send_slot == nullptr || send_expert == nullptr)) return SIMSD_ERR_SHAPE;
+  if (counts == nullptr || err_word == nullptr) return SIMSD_ERR_SHAPE;
+  if ((long long)world * capacity >= (1LL << 31)) return SIMSD_ERR_UNSUPPORTED;
+  const int dev = current_device();
+  if (dev < 0) return SIMSD_ERR_DEVICE;
+  if (prefer_shared(ep_plan_kernel, dev, 8) != SIMSD_OK) return SIMSD_ERR_LAUNCH;
+  EpPlanArgs a;
+  a.ids = reinterpret_cast<const long long*>(topk_ids);
+  a.send_slot = send_slot;
+  a.send_expert = send_expert;
+  a.slot_pos = slot_pos;
+  a.counts = counts;
+  a.err = err_word;
+  a.S = S;
+  a.E = E;
+  a.world = world;
+  a.cap = capacity;
+  return launch(ep_plan_kernel, dim3(1), dim3(EP_THREADS), 0, (cudaStream_t)stream, a);
+}
+
+int simsd_moe_gather_rows(const void* x, int64_t ldx, const int32_t* slots, int R, int k, int H, int dtype,
+                          void* out, int64_t ld_out, void* stream) {
+  if (R < 0 || k < 1 || H < 1 || ldx < H || ld_out < H) return SIMSD_ERR_SHAPE;
+  if (dtype != SIMSD_BF16 && dtype != SIMSD_F16 && dtype != SIMSD_F32) return SIMSD_ERR_DTYPE;
+  if (R == 0) return SIMSD_OK;
+  if (x == nullptr || slots == nullptr || out == nullptr) return SIMSD_ERR_SHAPE;
+  const int dev = current_device();
+  if (dev < 0) return SIMSD_ERR_DEVICE;
+  if (prefer_shared(gather_rows_kernel, dev, 5) != SIMSD_OK) return SIMSD_ERR_LAUNCH;
+  return launch(gather_rows_kernel, dim3((unsigned)R), dim3(256), 0, (cudaStream_t)stream, x, (long long)ldx,
+                (const int*)slots, out, (long long)ld_out, R, k, H, esize(dtype));
+}
+
+int simsd_moe_combine(const void* ys, int64_t ldys, const int32_t* slot_row, const float* topk_weight, void* out,
+                      int64_t ld_out, const void* add, int64_t ld_add, int T, int k, int H, int dtype, void* stream) {
+  if (T < 0 || k < 1 || H < 1 || ldys < H || ld_out < H || (add && ld_add < H)) return SIMSD_ERR_SHAPE;
+  if (dtype != SIMSD_BF16 && dtype != SIMSD_F16 && dtype != SIMSD_F32) return SIMSD_ERR_DTYPE;
+  if (T == 0) return SIMSD_OK;
+  if (ys == nullptr || slot_row == nullptr || topk_weight == nullptr || out == nullptr) return SIMSD_ERR_SHAPE;
+  const int dev = current_device();
+  if (dev < 0) return SIMSD_ERR_DEVICE;
+  cudaStream_t s = (cudaStream_t)stream;
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const bool vec = dtype != SIMSD_F32 && H % 8 == 0 && ld_out % 8 == 0 && ldys % 8 == 0 && al(out) && al(ys) &&
+                   (add == nullptr || (al(add) && ld_add % 8 == 0)) && k <= 32;
+  if (vec) {
+    if (prefer_shared(combine_vec_kernel, dev, 6) != SIMSD_OK) return SIMSD_ERR_LAUNCH;
+    return launch(combine_vec_kernel, dim3((unsigned)T), dim3(128), 0, s, ys, (long long)ldys, (const int*)slot_row,
+                  topk_weight, out, (long long)ld_out, add, (long long)ld_add, T, k, H, dtype);
+  }
+  if (prefer_shared(combine_kernel, dev, 7) != SIMSD_OK) return SIMSD_ERR_LAUNCH;
+  return launch(combine_kernel, dim3((unsigned)T), dim3(256), 0, s, ys, (long long)ldys, (const int*)slot_row,
+                topk_weight, out, (long long)ld_out, add, (long long)ld_add, T, k, H, dtype);
+}
+
 }  // extern "C"

@@ -368,7 +368,7 @@ struct AlignArgs {
   int* counts;            // [E]
   int* offsets;           // [E+1]
   int* sorted_slots;      // [S]  row -> slot
-  int* slot_to_row;       // [S]  slot -> row, -1 for an invalid id
+  int* slot_to_row;       // [S]  slot -> row, -1 for an id outside [0, E)
   int* slots_padded;      // reference layout [num_tiles*block_m] or nullptr
   int* tile_expert;       // reference layout [num_tiles] or nullptr
   int* err;
@@ -398,7 +398,7 @@ __global__ void __launch_bounds__(ALIGN_THREADS, 1) align_kernel(const AlignArgs
   if (cache_ids)
     for (int i = tid; i < S; i += ALIGN_THREADS) {
       const long long e = p.ids[i];
-      s_ids[i] = (e >= 0 && e < E) ? (int)e : -1;
+      s_ids[i] = (e >= 0 && e < E) ? (int)e : (e < 0 ? -1 : E);   // E: out of range
     }
   __syncthreads();
   auto id_at = [&](int s) -> long long { return cache_ids ? (long long)s_ids[s] : p.ids[s]; };
@@ -467,7 +467,7 @@ __global__ void __launch_bounds__(ALIGN_THREADS, 1) align_kernel(const AlignArgs
     if (s < hi) {
       p.slot_to_row[s] = row;
       if (valid) p.sorted_slots[row] = s;
-      else atomicOr(p.err, SIMSD_DEV_ERR_BAD_INDEX);
+      else if (id_at(s) >= 0) atomicOr(p.err, SIMSD_DEV_ERR_BAD_INDEX);   // id >= E; negative = no expert
     }
   }
   // rows left over by invalid ids hold no slot
@@ -635,6 +635,90 @@ __global__ void combine_vec_kernel(const void* ys, long long ldys, const int* sl
     *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + (long long)t * ld_out + h8 * 8) =
         make_uint4(o[0], o[1], o[2], o[3]);
   }
+}
+
+
+// ------------------------------------------------------------------ expert-parallel buckets
+// Expert e lives on rank e / (E / world) as its local expert e % (E / world).
+// Slot s = t*k + j of this rank's tokens goes to bucket peer(ids[s]) at the
+// next free position, in slot order (stable): send_slot[peer*cap + i] = s,
+// send_expert[...] = local expert id, slot_pos[s] = peer*cap + i.  Unused
+// bucket entries hold -1; a slot beyond `cap` or with an id outside [0, E) gets
+// slot_pos -1 (BAD_INDEX / CAPACITY in the error word).  counts[peer] = slots
+// bound for the peer.  One CTA; stable ranks come from warp match masks and a
+// per-chunk scan over warps.
+struct EpPlanArgs {
+  const long long* ids;  // [S]
+  int* send_slot;        // [world * cap]
+  int* send_expert;      // [world * cap]
+  int* slot_pos;         // [S]
+  int* counts;           // [world]
+  int* err;
+  int S, E, world, cap;
+};
+
+constexpr int EP_THREADS = 1024;
+constexpr int EP_MAX_WORLD = 64;
+
+__global__ void __launch_bounds__(EP_THREADS, 1) ep_plan_kernel(const EpPlanArgs p) {
+  griddep_launch_dependents();
+  griddep_wait();
+  __shared__ int s_warp[32][EP_MAX_WORLD];
+  __shared__ int s_base[EP_MAX_WORLD];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int epr = p.E / p.world;
+  const long long nb = (long long)p.world * p.cap;
+  for (long long i = tid; i < nb; i += EP_THREADS) {
+    p.send_slot[i] = -1;
+    p.send_expert[i] = -1;
+  }
+  if (tid < p.world) s_base[tid] = 0;
+  const unsigned lt = (1u << lane) - 1u;
+  for (int base = 0; base < p.S; base += EP_THREADS) {
+    for (int i = tid; i < 32 * EP_MAX_WORLD; i += EP_THREADS) (&s_warp[0][0])[i] = 0;
+    __syncthreads();
+    const int s = base + tid;
+    int peer = -1, lid = -1;
+    if (s < p.S) {
+      const long long e = p.ids[s];
+      if (e >= 0 && e < p.E) {
+        peer = (int)(e / epr);
+        lid = (int)(e - (long long)peer * epr);
+      } else if (e >= p.E) {
+        atomicOr(p.err, SIMSD_DEV_ERR_BAD_INDEX);
+      }
+    }
+    const unsigned same = __match_any_sync(0xffffffffu, peer);
+    const int rank_in_warp = __popc(same & lt);
+    if (peer >= 0 && lane == __ffs(same) - 1) s_warp[warp][peer] = __popc(same);
+    __syncthreads();
+    if (tid < p.world) {
+      int run = s_base[tid];
+      for (int w = 0; w < 32; ++w) {
+        const int v = s_warp[w][tid];
+        s_warp[w][tid] = run;
+        run += v;
+      }
+      s_base[tid] = run;
+    }
+    __syncthreads();
+    if (s < p.S) {
+      int slot_pos = -1;
+      if (peer >= 0) {
+        const int pos = s_warp[warp][peer] + rank_in_warp;
+        if (pos < p.cap) {
+          slot_pos = peer * p.cap + pos;
+          p.send_slot[slot_pos] = s;
+          p.send_expert[slot_pos] = lid;
+        } else {
+          atomicOr(p.err, SIMSD_DEV_ERR_CAPACITY);
+        }
+      }
+      p.slot_pos[s] = slot_pos;
+    }
+    __syncthreads();
+  }
+  if (tid < p.world) p.counts[tid] = s_base[tid];
 }
 
 }  // namespace simsd

@@ -21,6 +21,7 @@
 // device error word bits (OR-ed into the caller's error word)
 #define SIMSD_DEV_ERR_TIMEOUT   1
 #define SIMSD_DEV_ERR_BAD_INDEX 2
+#define SIMSD_DEV_ERR_CAPACITY  4   // expert-parallel bucket overflow
 
 namespace simsd {
 

@@ -35,6 +35,7 @@ LAUNCH_INKERNEL_REDUCE = 2
 
 DEV_ERR_TIMEOUT = 1
 DEV_ERR_BAD_INDEX = 2
+DEV_ERR_CAPACITY = 4
 
 _DTYPE = {torch.bfloat16: SIMSD_BF16, torch.float16: SIMSD_F16, torch.float32: SIMSD_F32}
 
@@ -59,6 +60,9 @@ SIGNATURES: dict[str, tuple] = {
     "simsd_moe_workspace_size": (_S, [_I, _I, _I, _I, _I, _I]),
     "simsd_moe_dispatch": (_I, [_P, _L, _P, _P, _P, _P, _L, _L, _P, _L, _L, _P, _L, _P, _L, _I, _I,
                                 _I, _I, _I, _I, _P, _S, _P]),
+    "simsd_moe_ep_plan": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
+    "simsd_moe_gather_rows": (_I, [_P, _L, _P, _I, _I, _I, _I, _P, _L, _P]),
+    "simsd_moe_combine": (_I, [_P, _L, _P, _P, _P, _L, _P, _L, _I, _I, _I, _I, _P]),
 }
 
 _lib = None

@@ -17,6 +17,7 @@ for p in (str(REPO / "simsd-release_b200"), str(REPO)):
     if p not in sys.path:
         sys.path.insert(0, p)
 
+import numpy as np  # noqa: E402
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 import torch.nn.functional as F  # noqa: E402
@@ -48,7 +49,104 @@ def case_column():
     assert torch.equal(gu.w_gate.data, wg[lo:hi]) and torch.equal(gu.w_up.data, wu[lo:hi])
 
 
-CASES = {"column": case_column}
+class CpuEpOps:
+    """CPU stand-ins for the expert-parallel layer's compute steps (fp32, one
+    row at a time, so a row's result never depends on what it is batched with)."""
+
+    @staticmethod
+    def route(x, w_router, bias, k, renorm, scale):
+        from oracle.torch_eager import route
+        return route(x, w_router, bias, k, renorm=renorm, scale=scale)
+
+    @staticmethod
+    def plan(ids, E, world, cap):
+        from oracle import oracle as O
+        return {k: torch.from_numpy(v) for k, v in O.ep_plan(ids.numpy(), E, world, cap).items()}
+
+    @staticmethod
+    def gather(x, slots, k):
+        out = torch.zeros((slots.numel(), x.shape[1]), dtype=x.dtype)
+        for r, s in enumerate(slots.tolist()):
+            if s >= 0:
+                out[r] = x[s // k]
+        return out
+
+    @staticmethod
+    def expert_row(row, wg, wu, wd):
+        return F.linear(F.silu(F.linear(row, wg)) * F.linear(row, wu), wd)
+
+    @staticmethod
+    def experts(rows, expert_ids, w_gate, w_up, w_down):
+        out = torch.zeros_like(rows)
+        for r, e in enumerate(expert_ids.tolist()):
+            if e >= 0:
+                out[r] = CpuEpOps.expert_row(rows[r:r + 1], w_gate[e], w_up[e], w_down[e])[0]
+        return out
+
+    @staticmethod
+    def combine(ys, slot_pos, w, add):
+        T, k = w.shape
+        out = torch.zeros((T, ys.shape[1]), dtype=torch.float32)
+        for t in range(T):
+            for j in range(k):
+                p = int(slot_pos[t * k + j])
+                if p >= 0:
+                    out[t] += ys[p].float() * w[t, j]
+        if add is not None:
+            out = out + add
+        return out.to(ys.dtype)
+
+    @staticmethod
+    def shared(x, w_gate, w_up, w_down):
+        return F.linear(F.silu(F.linear(x, w_gate)) * F.linear(x, w_up), w_down)
+
+
+def case_ep_moe():
+    """Expert-parallel layer (2 ranks, CPU ops) == the same computation done
+    token by token on one process, for every rank's tokens; plus the bucket
+    plan's invariants."""
+    from kernels import moe_parallel as MP
+    from oracle import oracle as O
+    rank, world = dist.get_rank(), dist.get_world_size()
+    T, H, E, k, I = 6, 16, 8, 3, 8
+    g = torch.Generator().manual_seed(1)
+    wr = torch.randn(E, H, generator=g) * 0.3
+    bias = torch.randn(E, generator=g) * 0.5
+    wg, wu = torch.randn(E, I, H, generator=g) * 0.3, torch.randn(E, I, H, generator=g) * 0.3
+    wd = torch.randn(E, H, I, generator=g) * 0.3
+    sh = (torch.randn(I, H, generator=g) * 0.3, torch.randn(I, H, generator=g) * 0.3,
+          torch.randn(H, I, generator=g) * 0.3)
+    xs = [torch.randn(T, H, generator=g) for _ in range(world)]   # every rank's tokens
+    lo, hi = MP.expert_range(E, rank, world)
+    for capacity, shared in ((None, None), (None, sh), (T * k + 5, None)):
+        out = MP.ep_moe_layer(xs[rank], wr, bias, k, wg[lo:hi], wu[lo:hi], wd[lo:hi], E, capacity=capacity,
+                              shared=shared, ops=CpuEpOps)
+        ids, w = CpuEpOps.route(xs[rank], wr, bias, k, True, 1.0)
+        ref = torch.zeros(T, H)
+        for t in range(T):
+            for j in range(k):
+                e = int(ids[t, j])
+                ref[t] += CpuEpOps.expert_row(xs[rank][t:t + 1], wg[e], wu[e], wd[e])[0] * w[t, j]
+        if shared is not None:
+            ref = ref + CpuEpOps.shared(xs[rank], *shared)
+        assert torch.equal(out, ref), (rank, capacity, (out - ref).abs().max())
+    # plan invariants: every slot sent once, to the rank holding its expert, in slot order
+    ids = torch.randint(0, E, (T, k), generator=g)
+    p = O.ep_plan(ids.numpy(), E, world, T * k)
+    flat = ids.reshape(-1).numpy()
+    for s, pos in enumerate(p["slot_pos"]):
+        peer = pos // (T * k)
+        assert peer == flat[s] // (E // world) and p["send_slot"][pos] == s
+        assert p["send_expert"][pos] == flat[s] % (E // world)
+    for peer in range(world):
+        sent = [v for v in p["send_slot"][peer * T * k:(peer + 1) * T * k] if v >= 0]
+        assert sent == sorted(sent) and len(sent) == p["counts"][peer]
+    # a capacity below a bucket's load drops the slots past it
+    q = O.ep_plan(np.zeros(5, np.int64), E, world, 2)
+    assert list(q["slot_pos"]) == [0, 1, -1, -1, -1] and q["counts"][0] == 5
+
+
+CASES = {"column": case_column, "ep_moe": case_ep_moe}
 
 
 def main():

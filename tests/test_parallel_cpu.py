@@ -31,6 +31,10 @@ def test_column_parallel_matches_full_linear_gloo():
     run_dist("column")
 
 
+def test_expert_parallel_layer_matches_single_process_gloo():
+    run_dist("ep_moe")
+
+
 def test_column_range_rejects_uneven_split():
     sys.path.insert(0, str(REPO / "simsd-release_b200"))
     from kernels import parallel as P
@@ -39,3 +43,11 @@ def test_column_range_rejects_uneven_split():
         P.column_range(10, 0, 3)
     w = torch.arange(12.0).reshape(6, 2)
     assert torch.equal(P.column_shard(w, 2, 3), w[4:6])
+
+
+def test_expert_range():
+    sys.path.insert(0, str(REPO / "simsd-release_b200"))
+    from kernels import moe_parallel as MP
+    assert MP.expert_range(256, 3, 8) == (96, 128)
+    with pytest.raises(ValueError):
+        MP.expert_range(10, 0, 4)
