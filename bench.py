@@ -348,6 +348,8 @@ def gpu_arm(args):
     line["clocks"] = clk_summary
     if world == 1 and "verify" in args.workload:
         line["verify"] = verify_bench(dev, args.steps)
+    if "ep" in args.workload.split(","):
+        line["ep_moe"] = ep_moe_bench(dev, rank, world, dist, args.steps)
     if world == 1 and "moe" in args.workload:
         line["moe"] = moe_bench(dev, args.steps, None if args.no_cpu_baseline else min(5.0, args.cpu_seconds))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -369,6 +371,72 @@ def moe_bytes_flops(T: int, n_active: int) -> tuple[int, int]:
     b = n_active * 3 * H * I * 2 + 3 * H * I * 2 + E * H * 2 + 2 * T * H * 2 + T * k * 12
     f = 2 * T * (k + 1) * 3 * H * I + 2 * T * E * H
     return b, f
+
+
+# ------------------------------------------------------------------ EP MoE
+EP = dict(H=4096, E=256, k=8, I=1536, bias_std=0.5, Ts=(256, 1024, 4096))
+
+
+def ep_moe_bench(dev, rank: int, world: int, dist, steps: int) -> dict:
+    """Expert-parallel MoE layer: E/world experts per rank, T/world tokens per
+    rank, all-to-all exchange (NCCL); at world 1 the single-GPU layer."""
+    from kernels.moe_dispatch_fused import moe_layer, moe_route
+    from kernels.moe_parallel import ep_moe_layer, expert_range
+    H, E, k, I = EP["H"], EP["E"], EP["k"], EP["I"]
+    bf = torch.bfloat16
+    g0 = torch.Generator(device=dev).manual_seed(77)            # replicated: router
+    wr = (torch.randn(E, H, generator=g0, device=dev) * 0.02).to(bf)
+    bias = torch.randn(E, generator=g0, device=dev) * EP["bias_std"]
+    shared = tuple((torch.randn(*sh, generator=g0, device=dev) * 0.02).to(bf) for sh in ((I, H), (I, H), (H, I)))
+    lo, hi = expert_range(E, rank, world)
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)   # this rank's experts and tokens
+    wg, wu = [(torch.randn(hi - lo, I, H, generator=g, device=dev) * 0.02).to(bf) for _ in range(2)]
+    wd = (torch.randn(hi - lo, H, I, generator=g, device=dev) * 0.02).to(bf)
+    pk = peaks()
+    out = {}
+    with torch.inference_mode():
+        for T in EP["Ts"]:
+            Tr = T // world
+            x = torch.randn(Tr, H, generator=g, device=dev).to(bf)
+            ids, _ = moe_route(x, wr, bias, k=k)
+            active = torch.zeros(E, dtype=torch.int32, device=dev)
+            active[ids.reshape(-1)] = 1
+            if world > 1:
+                dist.all_reduce(active, op=dist.ReduceOp.MAX)
+            n_active = int(active.sum().item())
+
+            def layer():
+                if world == 1:
+                    return moe_layer(x, wr, bias, k, wg, wu, wd, shared=shared)
+                return ep_moe_layer(x, wr, bias, k, wg, wu, wd, E, shared=shared)
+
+            for _ in range(3):
+                layer()
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            n = max(5, min(steps, 50))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(n):
+                layer()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / n
+            if world > 1:
+                t = torch.tensor([ms], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ms = float(t.item())
+            b = n_active * 3 * H * I * 2 + world * (3 * H * I * 2 + E * H * 2) + 2 * T * H * 2 + T * k * 12
+            a2a = 2 * T * k * H * 2 * (world - 1) // world if world > 1 else 0
+            out[f"T{T}"] = {"ms": round(ms, 4), "gbs": round(b / ms / 1e6, 1), "n_active_experts": n_active,
+                            "frac_hbm_peak_per_gpu": round(b / ms / 1e6 / world / pk["hbm_gbs"], 4),
+                            "a2a_bytes_expected": a2a}
+    return {"workload": "EP MoE layer, BASELINE configs[4]: H=4096, E=256 (E/N per GPU), top-8 sigmoid+bias(N(0,0.5)), "
+                        "I=1536 SiLU*mul experts + 1 shared expert, bf16, T tokens split over N GPUs, "
+                        "all-to-all in fixed-capacity buckets (eager launches)",
+            "metric": "MoE layer HBM GB/s, all GPUs (algorithmic bytes: active experts + per-GPU shared/router + activations)",
+            "n_gpus": world, "per_T": out}
 
 
 def moe_bench(dev, steps: int, cpu_seconds: float | None) -> dict:
@@ -692,8 +760,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
-    ap.add_argument("--workload", default="thin,moe,verify",
-                    help="comma list of extra legs measured at N=1 besides the headline (moe, verify)")
+    ap.add_argument("--workload", default="thin,moe,verify,ep",
+                    help="comma list of legs: thin (headline), moe and verify (N=1), ep (expert-parallel MoE, any N)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -1,0 +1,78 @@
+"""Multi-GPU cases (one process per GPU, NCCL) run by test_multi_gpu.py.
+
+Each rank checks its own result against the single-GPU path on the same
+inputs; a failing rank exits non-zero.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+import sys
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parents[1]
+for p in (str(REPO / "simsd-release_b200"), str(REPO)):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+
+def _close(a, b, rel=1e-2):
+    return float((a.float() - b.float()).abs().max()) <= rel * float(b.float().abs().max())
+
+
+def case_column(dev):
+    from kernels.parallel import ColumnParallelGateUp, ColumnParallelThinLinear
+    from kernels.thin_linear_fused import thin_linear, thin_linear_silu_mul
+    g = torch.Generator(device=dev).manual_seed(0)       # same weights on every rank
+    bf = torch.bfloat16
+    x = torch.randn(32, 4096, generator=g, device=dev).to(bf)
+    w = (torch.randn(6144, 4096, generator=g, device=dev) * 0.02).to(bf)
+    wg, wu = [(torch.randn(3072, 4096, generator=g, device=dev) * 0.02).to(bf) for _ in range(2)]
+    with torch.inference_mode():
+        y = ColumnParallelThinLinear(w)(x)
+        h = ColumnParallelGateUp(wg, wu)(x)
+        assert _close(y, thin_linear(x, w)) and _close(h, thin_linear_silu_mul(x, wg, wu))
+
+
+def case_ep(dev):
+    from kernels.moe_dispatch_fused import moe_layer
+    from kernels.moe_parallel import ep_moe_layer, expert_range
+    rank, world = dist.get_rank(), dist.get_world_size()
+    T, k, E, H, I = 64, 8, 64, 1024, 512
+    bf = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(1)       # same model on every rank
+    wr = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(bf)
+    bias = torch.randn(E, generator=g, device=dev) * 0.5
+    wg, wu = [(torch.randn(E, I, H, generator=g, device=dev) * 0.02).to(bf) for _ in range(2)]
+    wd = (torch.randn(E, H, I, generator=g, device=dev) * 0.02).to(bf)
+    gx = torch.Generator(device=dev).manual_seed(10 + rank)
+    x = torch.randn(T, H, generator=gx, device=dev).to(bf)
+    lo, hi = expert_range(E, rank, world)
+    with torch.inference_mode():
+        got = ep_moe_layer(x, wr, bias, k, wg[lo:hi], wu[lo:hi], wd[lo:hi], E)
+        ref = moe_layer(x, wr, bias, k, wg, wu, wd)
+        torch.cuda.synchronize()
+    assert _close(got, ref), (rank, float((got.float() - ref.float()).abs().max()))
+
+
+CASES = {"column": case_column, "ep": case_ep}
+
+
+def main():
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        for name in sys.argv[1:]:
+            CASES[name](dev)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
