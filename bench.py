@@ -311,7 +311,13 @@ def gpu_arm(args):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_ms = float(t.item())
         del houts
+        # CUDA graphs that hold NCCL calls must be gone before the process
+        # group is destroyed, or destroy_process_group waits for good
         graphs.clear()
+        del gr
+        import gc
+        gc.collect()
+        torch.cuda.synchronize()
 
     total_bytes = step_bytes(1)
     value = total_bytes / (ms * 1e-3) / 1e9
