@@ -159,16 +159,22 @@ def make_inputs(dev, seed=7):
             for M in MS}
 
 
-def run_step(ws, xs, world, dist, outs=None):
+def run_step(ws, xs, world, dist, ag=None):
+    """One sweep step.  world > 1: each linear is column-parallel, its output
+    all-gathered by `ag` (FusedAllGather: fused into the GEMM over NVLink) or,
+    without it, by an NCCL all-gather after the local GEMM."""
     from kernels.parallel import gather_columns
     from kernels.thin_linear_fused import thin_linear, thin_linear_silu_mul
     res = []
     for M in MS:
         for name, K, N, silu in SHAPES:
             x = xs[M][K]
-            y = thin_linear_silu_mul(x, *ws[name]) if silu else thin_linear(x, ws[name])
-            if world > 1:
-                y = gather_columns(y)
+            if world > 1 and ag is not None:
+                y = ag.linear(x, *ws[name]) if silu else ag.linear(x, ws[name])
+            else:
+                y = thin_linear_silu_mul(x, *ws[name]) if silu else thin_linear(x, ws[name])
+                if world > 1:
+                    y = gather_columns(y)
             res.append(y)
     return res
 
@@ -234,16 +240,20 @@ def gpu_arm(args):
     # Inference weights are fixed, so every launch may stream its weights while
     # the previous kernel drains (programmatic dependent launch).
     _lib.set_pdl(not args.no_pdl)
+    ag = None
+    if world > 1 and not args.nccl_gather:
+        from kernels.parallel import FusedAllGather
+        ag = FusedAllGather()
 
     with torch.inference_mode():
         for _ in range(max(3, args.warmup)):
-            run_step(pool[0], xs, world, dist)
+            run_step(pool[0], xs, world, dist, ag)
         torch.cuda.synchronize()
         graphs = []
         for p in range(POOL):
             gr = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gr):
-                run_step(pool[p], xs, world, dist)
+                run_step(pool[p], xs, world, dist, ag)
             graphs.append(gr)
         for i in range(max(3, args.warmup)):
             graphs[i % POOL].replay()
@@ -287,7 +297,7 @@ def gpu_arm(args):
                 d2h += M * ((N // 2) if silu else N) * 2
         for _ in range(3):
             dxs = {M: {K: hx[M][K].to(dev, non_blocking=True) for K in (4096, 12288)} for M in MS}
-            res = run_step(pool[0], dxs, world, dist)
+            res = run_step(pool[0], dxs, world, dist, ag)
             if houts is None:
                 houts = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
             for h, r in zip(houts, res):
@@ -300,7 +310,7 @@ def gpu_arm(args):
         e2.record()
         for i in range(e2e_steps):
             dxs = {M: {K: hx[M][K].to(dev, non_blocking=True) for K in (4096, 12288)} for M in MS}
-            res = run_step(pool[i % POOL], dxs, world, dist)
+            res = run_step(pool[i % POOL], dxs, world, dist, ag)
             for h, r in zip(houts, res):
                 h.copy_(r, non_blocking=True)   # into pinned host buffers
         e3.record()
@@ -318,6 +328,10 @@ def gpu_arm(args):
         import gc
         gc.collect()
         torch.cuda.synchronize()
+        if ag is not None:
+            if dist:
+                dist.barrier()
+            ag.close()
 
     total_bytes = step_bytes(1)
     value = total_bytes / (ms * 1e-3) / 1e9
@@ -330,7 +344,9 @@ def gpu_arm(args):
         "config": {"workload": "SDAR-8B thin-M linear sweep (BASELINE configs[1])",
                    "shapes": {n: [K, N] for n, K, N, _ in SHAPES}, "M": MS,
                    "gate_up_epilogue": "SiLU(gate)*up -> [M,12288]",
-                   "parallelism": f"column-parallel x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                   "parallelism": f"column-parallel x{world}" + ((" + NCCL all-gather" if args.nccl_gather else
+                                                                  " + all-gather fused into the GEMM (NVLink peer stores)")
+                                                                 if world > 1 else ""),
                    "l2": "inputs larger than L2: 2 weight copies x 386 MB cycled per step",
                    "launch": "no PDL" if args.no_pdl else "programmatic dependent launch (weights static)",
                    "timing": "CUDA-graph replay, CUDA events, max over ranks"},
@@ -766,6 +782,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
+    ap.add_argument("--nccl-gather", action="store_true",
+                    help="N > 1: all-gather each linear's columns with NCCL instead of the fused kernel")
     ap.add_argument("--workload", default="thin,moe,verify,ep",
                     help="comma list of legs: thin (headline), moe and verify (N=1), ep (expert-parallel MoE, any N)")
     args = ap.parse_args()

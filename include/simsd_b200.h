@@ -227,6 +227,41 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids,
                        int64_t ld_add, int T, int k, int E, int H, int I, int dtype,
                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- column-parallel thin linear with the all-gather fused in (no counterpart in
+ * the reference).  Each rank of a node holds rows [rank*N, (rank+1)*N) of the
+ * full weight and writes its output columns straight into every rank's y
+ * (NVLink peer stores); the ranks' kernels then meet on counters in their
+ * signal blocks, so a launch completes when this rank's y is whole.  All ranks
+ * must make the same sequence of these calls with the same shapes. */
+
+#define SIMSD_IPC_HANDLE_BYTES 64
+#define SIMSD_SIGNAL_BYTES 256   /* one rank's signal block (zeroed by simsd_ipc_alloc) */
+
+/* Device memory other processes of the node can map: cudaMalloc'd, zeroed. */
+int simsd_ipc_alloc(size_t bytes, void** dev_ptr);
+int simsd_ipc_free(void* dev_ptr);
+/* Export a simsd_ipc_alloc block (SIMSD_IPC_HANDLE_BYTES bytes into `handle`). */
+int simsd_ipc_handle(const void* dev_ptr, void* handle);
+/* Map another process's exported block on the current device. */
+int simsd_ipc_open(const void* handle, void** dev_ptr);
+int simsd_ipc_close(void* dev_ptr);
+
+/*
+ * y_r[m, col_offset + n] = (x w^T)[m, n] (+ bias[n]) for every rank r, or the
+ * SiLU*mul epilogue with w_up; n < N (this rank's output columns).
+ *   peer_y [world]: every rank's y (same layout, row stride ldy), this rank's
+ *   own at peer_y[rank]; peer_signal [world]: every rank's signal block.
+ * 1 < world <= 8, M <= 64, bf16/fp16 with TMA-describable layouts; other
+ * requests return SIMSD_ERR_UNSUPPORTED (use simsd_thin_linear and a
+ * collective instead).
+ */
+int simsd_thin_linear_allgather(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w,
+                                int64_t ldw_n, int64_t ldw_k, const void* w_up, const void* bias,
+                                void* const* peer_y, int64_t ldy, int col_offset, int M, int N,
+                                int K, int dtype, int epilogue, int rank, int world,
+                                void* const* peer_signal, void* workspace, size_t workspace_bytes,
+                                void* stream);
+
 /* ---- expert parallelism (no counterpart in the reference, which runs the MoE
  * layer on one GPU): experts split over `world` ranks in contiguous blocks of
  * E / world, tokens routed on their owner rank, rows exchanged with all-to-all

@@ -434,6 +434,49 @@ bool cluster_enabled() {
   return v;
 }
 
+// One tc_cluster_kernel launch for a thin linear with M <= 64 (layouts already
+// checked by thin_tc_possible).  world > 1: the fused all-gather variant, with
+// peer outputs / signal blocks and this rank's column offset.  Returns
+// SIMSD_ERR_UNSUPPORTED when no cluster plan fits.
+int thin_cluster(const void* x, long long ldx_m, const void* w, long long ldw_n, const void* w_up, const void* bias,
+                 void* y, long long ldy, int M, int N, int K, int dtype, bool silu, int* err, void* const* peer_y,
+                 int col_offset, int world, int rank, void* const* peer_sig, cudaStream_t s, int dev) {
+  const int bmax = pick_bmax_rows(M);
+  const long long row_tiles = silu ? cdiv(N, 64) : cdiv(N, 128);
+  const int kb = (int)cdiv(K, 64);
+  const ClusterPlan cp = plan_cluster(bmax, row_tiles, kb, dev);
+  if (cp.S <= 0) return SIMSD_ERR_UNSUPPORTED;
+  if (ensure_encode() != SIMSD_OK) return SIMSD_ERR_DEVICE;
+  TcClusterArgs a;
+  memset(&a, 0, sizeof(a));
+  const long long lx = (M > 1) ? ldx_m : ((K * 2 + 15) / 16) * 8;
+  const long long lw = (N > 1) ? ldw_n : ((K * 2 + 15) / 16) * 8;
+  const uint64_t xd[2] = {(uint64_t)K, (uint64_t)M}, xs[1] = {(uint64_t)lx * 2};
+  const uint64_t wd[2] = {(uint64_t)K, (uint64_t)N}, wsb[1] = {(uint64_t)lw * 2};
+  int rc = encode_map(&a.tmB, x, dtype, 2, xd, xs, TC_BOX_ROWS);
+  if (rc == SIMSD_OK) rc = encode_map(&a.tmA0, w, dtype, 2, wd, wsb, silu ? 64 : 128);
+  if (rc == SIMSD_OK && silu) rc = encode_map(&a.tmA1, w_up, dtype, 2, wd, wsb, 64);
+  if (rc != SIMSD_OK) return rc;
+  a.out = y;
+  a.bias = bias;
+  a.err = err;
+  a.ld_out = ldy;
+  a.rows = M;
+  a.kb = kb;
+  a.rows_out = N;
+  a.row_tiles = (int)row_tiles;
+  a.silu = silu ? 1 : 0;
+  a.is_bf16 = dtype == SIMSD_BF16 ? 1 : 0;
+  a.world = world;
+  a.rank = rank;
+  a.col_offset = col_offset;
+  for (int r = 0; r < world && world > 1; ++r) {
+    a.peer_out[r] = peer_y[r];
+    a.peer_sig[r] = static_cast<int*>(peer_sig[r]);
+  }
+  return launch_cluster(bmax, a, cp.S, cp.C, s, dev);
+}
+
 int thin_tc_possible(const void* x, long long ldx_m, long long ldx_k, const void* w, long long ldw_n,
                      long long ldw_k, const void* w_up, int M, int N, int K, int dtype) {
   if (dtype != SIMSD_BF16 && dtype != SIMSD_F16) return 0;
@@ -569,34 +612,9 @@ int simsd_thin_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w
 
   if (use_tc && M <= 64 && split == 0 && cluster_enabled()) {
     // M <= 64: split-K tiles reduced inside thread-block clusters
-    const int bmax = pick_bmax_rows(M);
-    const long long row_tiles = silu ? cdiv(N, 64) : cdiv(N, 128);
-    const int kb = (int)cdiv(K, 64);
-    const ClusterPlan cp = plan_cluster(bmax, row_tiles, kb, dev);
-    if (cp.S > 0) {
-      if (ensure_encode() != SIMSD_OK) return SIMSD_ERR_DEVICE;
-      TcClusterArgs a;
-      memset(&a, 0, sizeof(a));
-      const long long lx = (M > 1) ? ldx_m : ((K * 2 + 15) / 16) * 8;
-      const long long lw = (N > 1) ? ldw_n : ((K * 2 + 15) / 16) * 8;
-      const uint64_t xd[2] = {(uint64_t)K, (uint64_t)M}, xs[1] = {(uint64_t)lx * 2};
-      const uint64_t wd[2] = {(uint64_t)K, (uint64_t)N}, wsb[1] = {(uint64_t)lw * 2};
-      int rc = encode_map(&a.tmB, x, dtype, 2, xd, xs, TC_BOX_ROWS);
-      if (rc == SIMSD_OK) rc = encode_map(&a.tmA0, w, dtype, 2, wd, wsb, silu ? 64 : 128);
-      if (rc == SIMSD_OK && silu) rc = encode_map(&a.tmA1, w_up, dtype, 2, wd, wsb, 64);
-      if (rc != SIMSD_OK) return rc;
-      a.out = y;
-      a.bias = bias;
-      a.err = err;
-      a.ld_out = ldy_m;
-      a.rows = M;
-      a.kb = kb;
-      a.rows_out = N;
-      a.row_tiles = (int)row_tiles;
-      a.silu = silu ? 1 : 0;
-      a.is_bf16 = dtype == SIMSD_BF16 ? 1 : 0;
-      return launch_cluster(bmax, a, cp.S, cp.C, s, dev);
-    }
+    const int rc = thin_cluster(x, ldx_m, w, ldw_n, w_up, bias, y, ldy_m, M, N, K, dtype, silu, err, nullptr, 0, 1,
+                                0, nullptr, s, dev);
+    if (rc != SIMSD_ERR_UNSUPPORTED) return rc;
   }
 
   if (use_tc) {
@@ -1115,6 +1133,69 @@ int simsd_moe_combine(const void* ys, int64_t ldys, const int32_t* slot_row, con
   if (prefer_shared(combine_kernel, dev, 7) != SIMSD_OK) return SIMSD_ERR_LAUNCH;
   return launch(combine_kernel, dim3((unsigned)T), dim3(256), 0, s, ys, (long long)ldys, (const int*)slot_row,
                 topk_weight, out, (long long)ld_out, add, (long long)ld_add, T, k, H, dtype);
+}
+
+int simsd_ipc_alloc(size_t bytes, void** dev_ptr) {
+  if (dev_ptr == nullptr || bytes == 0) return SIMSD_ERR_SHAPE;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return SIMSD_ERR_DEVICE;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess) {
+    cudaFree(p);
+    return SIMSD_ERR_DEVICE;
+  }
+  *dev_ptr = p;
+  return SIMSD_OK;
+}
+
+int simsd_ipc_free(void* dev_ptr) { return cudaFree(dev_ptr) == cudaSuccess ? SIMSD_OK : SIMSD_ERR_DEVICE; }
+
+int simsd_ipc_handle(const void* dev_ptr, void* handle) {
+  static_assert(sizeof(cudaIpcMemHandle_t) <= SIMSD_IPC_HANDLE_BYTES, "handle size");
+  if (dev_ptr == nullptr || handle == nullptr) return SIMSD_ERR_SHAPE;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr)) != cudaSuccess) return SIMSD_ERR_DEVICE;
+  memset(handle, 0, SIMSD_IPC_HANDLE_BYTES);
+  memcpy(handle, &h, sizeof(h));
+  return SIMSD_OK;
+}
+
+int simsd_ipc_open(const void* handle, void** dev_ptr) {
+  if (handle == nullptr || dev_ptr == nullptr) return SIMSD_ERR_SHAPE;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return SIMSD_ERR_DEVICE;
+  *dev_ptr = p;
+  return SIMSD_OK;
+}
+
+int simsd_ipc_close(void* dev_ptr) {
+  return cudaIpcCloseMemHandle(dev_ptr) == cudaSuccess ? SIMSD_OK : SIMSD_ERR_DEVICE;
+}
+
+int simsd_thin_linear_allgather(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w, int64_t ldw_n,
+                                int64_t ldw_k, const void* w_up, const void* bias, void* const* peer_y, int64_t ldy,
+                                int col_offset, int M, int N, int K, int dtype, int epilogue, int rank, int world,
+                                void* const* peer_signal, void* workspace, size_t workspace_bytes, void* stream) {
+  if (M < 1 || N < 1 || K < 1 || col_offset < 0) return SIMSD_ERR_SHAPE;
+  if (world < 2 || world > TC_AG_MAX_WORLD || rank < 0 || rank >= world) return SIMSD_ERR_UNSUPPORTED;
+  if (dtype != SIMSD_BF16 && dtype != SIMSD_F16) return SIMSD_ERR_UNSUPPORTED;
+  if (epilogue != SIMSD_EPI_NONE && epilogue != SIMSD_EPI_SILU_MUL) return SIMSD_ERR_UNSUPPORTED;
+  const bool silu = epilogue == SIMSD_EPI_SILU_MUL;
+  if (silu && (w_up == nullptr || bias != nullptr)) return SIMSD_ERR_UNSUPPORTED;
+  if (x == nullptr || w == nullptr || peer_y == nullptr || peer_signal == nullptr) return SIMSD_ERR_SHAPE;
+  for (int r = 0; r < world; ++r)
+    if (peer_y[r] == nullptr || peer_signal[r] == nullptr) return SIMSD_ERR_SHAPE;
+  if (ldy < (long long)col_offset + N) return SIMSD_ERR_SHAPE;
+  if (workspace == nullptr || workspace_bytes < (size_t)WS_COUNTER_BYTES) return SIMSD_ERR_WORKSPACE;
+  if (M > 64 || K < 64 || !cluster_enabled() ||
+      !thin_tc_possible(x, ldx_m, ldx_k, w, ldw_n, ldw_k, w_up, M, N, K, dtype))
+    return SIMSD_ERR_UNSUPPORTED;
+  const int dev = current_device();
+  if (dev < 0) return SIMSD_ERR_DEVICE;
+  int* err = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + WS_ERR_OFFSET);
+  return thin_cluster(x, ldx_m, w, ldw_n, w_up, bias, peer_y[rank], ldy, M, N, K, dtype, silu, err, peer_y,
+                      col_offset, world, rank, peer_signal, (cudaStream_t)stream, dev);
 }
 
 }  // extern "C"

@@ -296,6 +296,20 @@ __device__ __forceinline__ bool mbar_wait_cluster_drain(uint32_t bar, uint32_t p
   return true;
 }
 
+// ---------------------------------------------------------------- cross-GPU signals
+// Add to an int in another GPU's memory (an NVLink peer mapping) with release
+// semantics at system scope: every write this thread made before it (and,
+// through a preceding CTA barrier, its CTA's) is visible to a reader that
+// acquires the new value.
+__device__ __forceinline__ void red_add_release_sys(int* addr, int v) {
+  asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* addr) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
 // ---------------------------------------------------------------- PDL
 // Programmatic dependent launch: a kernel launched with programmatic stream
 // serialization may start before the previous kernel on its stream finishes;

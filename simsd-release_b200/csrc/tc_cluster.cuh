@@ -33,6 +33,8 @@
 namespace simsd {
 
 constexpr int TC_CL_MAX = 8;          // largest cluster (portable)
+constexpr int TC_AG_MAX_WORLD = 8;    // ranks of a fused column-parallel all-gather
+constexpr int TC_SIG_SLOTS = 32;      // signal counters per rank, used round robin
 constexpr int TC_CL_RED_ROWS = 144;   // >= S * rows one owner holds, for every S <= 8
 
 struct TcClusterArgs {
@@ -50,6 +52,12 @@ struct TcClusterArgs {
   int silu, is_bf16, pdl, prefetch;
   int l2_ahead;              // ring stages of weights requested into L2 ahead of the ring
   unsigned long long* trace; // optional: 8 %globaltimer stamps per CTA (diagnostics)
+  // column-parallel all-gather (world > 1): every output element is stored at
+  // column col_offset + col of each rank's y (peer_out[r], NVLink mappings),
+  // then the ranks' CTAs meet on counters in peer_sig (see the kernel's end)
+  int world, rank, col_offset;
+  void* peer_out[TC_AG_MAX_WORLD];
+  int* peer_sig[TC_AG_MAX_WORLD];  // each rank's signal block: TC_SIG_SLOTS counters, then its launch count
 };
 
 template <int BMAX, int KS>
@@ -306,6 +314,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
     const uint32_t red_full_u32 = smem_u32(red_full);
     const uint32_t red_free_u32 = smem_u32(red_free);
     auto swz = [](int lr, int j) { return BMAX >= 32 ? (j ^ (lr & 7)) : (j ^ ((lr >> 1) & 3)); };
+    // y[t, col] on this GPU, or on every rank's GPU for the fused all-gather
+    auto put = [&](long long t, int col, float v) {
+      if (p.world <= 1) {
+        store_f(outp, t * p.ld_out + col, v, odt);
+      } else {
+        for (int r = 0; r < p.world; ++r) store_f(p.peer_out[r], t * p.ld_out + p.col_offset + col, v, odt);
+      }
+    };
     int done = 0;
     for (int i = 0; i < n_tiles; ++i) {
       const int rtile = tile_of(i);
@@ -333,7 +349,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
                 const int t = ch * 16 + j;
-                if (t < nrows_all) store_f(outp, (long long)t * p.ld_out + col, __fadd_rn(v[j], bv), odt);
+                if (t < nrows_all) put(t, col, __fadd_rn(v[j], bv));
               }
             }
           } else {
@@ -349,7 +365,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
                 for (int j = 0; j < 16; ++j) {
                   const int t = ch * 16 + j;
                   if (t < nrows_all)
-                    store_f(outp, (long long)t * p.ld_out + col, silu_mul(v[j], xbuf[j * 64 + row]), odt);
+                    put(t, col, silu_mul(v[j], xbuf[j * 64 + row]));
                 }
               }
             }
@@ -443,8 +459,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
           for (int k4 = 0; k4 < 4; ++k4) {
             const int t = 4 * g + k4;
             if (t < nrows_all)
-              store_f(outp, (long long)t * p.ld_out + col, p.silu ? silu_mul(va[k4], vb[k4]) : __fadd_rn(va[k4], bv),
-                      odt);
+              put(t, col, p.silu ? silu_mul(va[k4], vb[k4]) : __fadd_rn(va[k4], bv));
           }
         }
       }
@@ -463,6 +478,37 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
     if (S > 1 && done < n_tiles && row == 0) {
       // aborting: give peers that may still be sending to this CTA time to land
       mbar_wait_cluster_drain(red_full_u32, done & 1, 100000000ull);
+    }
+    if (p.world > 1) {
+      // Fused all-gather: this CTA's stores to every rank are made visible
+      // (system-scope fence, then a release add on each rank's counter for
+      // this launch); CTA 0 of each rank then waits until all ranks' CTAs have
+      // added, so the launch completes only when this rank's y is whole.
+      // Counter slot = this rank's launch count mod TC_SIG_SLOTS, kept on the
+      // device (graph replays advance it); every rank launches the same
+      // sequence, so the slots agree.  The wait is bounded.
+      griddep_wait();   // the previous launch's count update is visible (no-op without PDL)
+      __threadfence_system();
+      named_bar_sync(1, 128);
+      if (row == 0) {
+        int* my_sig = p.peer_sig[p.rank];
+        const int seq = *reinterpret_cast<volatile int*>(my_sig + TC_SIG_SLOTS);
+        const int slot = seq & (TC_SIG_SLOTS - 1);
+        for (int r = 0; r < p.world; ++r) red_add_release_sys(p.peer_sig[r] + slot, 1);
+        if (blockIdx.x == 0) {
+          const int total = p.world * (int)gridDim.x;
+          const uint64_t t0 = globaltimer_ns();
+          while (ld_acquire_sys(my_sig + slot) < total) {
+            if (globaltimer_ns() - t0 > SIMSD_WAIT_LIMIT_NS) {
+              atomicOr(p.err, SIMSD_DEV_ERR_TIMEOUT);
+              break;
+            }
+          }
+          my_sig[slot] = 0;   // no rank adds to this slot again before this launch count comes round
+          __threadfence_system();
+          *reinterpret_cast<volatile int*>(my_sig + TC_SIG_SLOTS) = seq + 1;
+        }
+      }
     }
   }
 

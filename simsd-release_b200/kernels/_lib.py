@@ -32,6 +32,8 @@ PATH_AUTO, PATH_TC, PATH_SIMT = 0, 1, 2
 
 LAUNCH_PDL = 1
 LAUNCH_INKERNEL_REDUCE = 2
+IPC_HANDLE_BYTES = 64
+SIGNAL_BYTES = 256
 
 DEV_ERR_TIMEOUT = 1
 DEV_ERR_BAD_INDEX = 2
@@ -60,6 +62,13 @@ SIGNATURES: dict[str, tuple] = {
     "simsd_moe_workspace_size": (_S, [_I, _I, _I, _I, _I, _I]),
     "simsd_moe_dispatch": (_I, [_P, _L, _P, _P, _P, _P, _L, _L, _P, _L, _L, _P, _L, _P, _L, _I, _I,
                                 _I, _I, _I, _I, _P, _S, _P]),
+    "simsd_ipc_alloc": (_I, [_S, ctypes.POINTER(_P)]),
+    "simsd_ipc_free": (_I, [_P]),
+    "simsd_ipc_handle": (_I, [_P, _P]),
+    "simsd_ipc_open": (_I, [_P, ctypes.POINTER(_P)]),
+    "simsd_ipc_close": (_I, [_P]),
+    "simsd_thin_linear_allgather": (_I, [_P, _L, _L, _P, _L, _L, _P, _P, _P, _L, _I, _I, _I, _I, _I, _I, _I, _I,
+                                         _P, _P, _S, _P]),
     "simsd_moe_ep_plan": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
     "simsd_moe_gather_rows": (_I, [_P, _L, _P, _I, _I, _I, _I, _P, _L, _P]),
     "simsd_moe_combine": (_I, [_P, _L, _P, _P, _P, _L, _P, _L, _I, _I, _I, _I, _P]),

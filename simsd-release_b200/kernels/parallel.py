@@ -16,9 +16,12 @@ CUDA thin-M kernel.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from .thin_linear_fused import thin_linear, thin_linear_silu_mul
 
 
@@ -103,3 +106,112 @@ class ColumnParallelGateUp(torch.nn.Module):
         lead = x.shape[:-1]
         y = thin_linear_silu_mul(x.reshape(-1, x.shape[-1]), self.w_gate, self.w_up)
         return gather_columns(y, self.group).reshape(*lead, self.out_features)
+
+
+# ------------------------------------------------------------------ fused all-gather
+class _CudaArray:
+    """A raw device pointer seen by torch through __cuda_array_interface__."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3}
+
+
+class SymmetricBlock:
+    """One device block per rank, mapped into every rank of the group
+    (simsd_ipc_alloc / cudaIpc handles exchanged with all_gather_object).
+    Collective: every rank constructs it with the same size, in the same order."""
+
+    def __init__(self, nbytes: int, group=None):
+        L = _lib.lib()
+        self.rank, self.world = _group_info(group)
+        own = ctypes.c_void_p()
+        _lib.check(L.simsd_ipc_alloc(nbytes, ctypes.byref(own)), "ipc_alloc")
+        self.nbytes = nbytes
+        self.own = own.value
+        handle = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+        _lib.check(L.simsd_ipc_handle(self.own, handle), "ipc_handle")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self.ptrs: list[int] = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                self.ptrs.append(self.own)
+            else:
+                p = ctypes.c_void_p()
+                _lib.check(L.simsd_ipc_open(ctypes.create_string_buffer(h, len(h)), ctypes.byref(p)), "ipc_open")
+                self.ptrs.append(p.value)
+        self.tensor = torch.as_tensor(_CudaArray(self.own, nbytes), device=f"cuda:{torch.cuda.current_device()}")
+
+    def close(self) -> None:
+        if not self.ptrs:
+            return
+        L = _lib.lib()
+        for r, p in enumerate(self.ptrs):
+            if r != self.rank:
+                L.simsd_ipc_close(p)
+        self.ptrs = []
+        self.tensor = None
+        L.simsd_ipc_free(self.own)
+
+
+class FusedAllGather:
+    """Column-parallel thin linears whose all-gather is fused into the GEMM
+    (simsd_thin_linear_allgather): each rank stores its columns straight into
+    every rank's output over NVLink, then the ranks meet on device counters.
+
+    `linear(x, w_local, w_up_local=None, bias_local=None)` returns the full
+    [M, world * n] output.  It lives in buffers this object owns, two per
+    output shape used in turn, so a result stays valid until the second-next
+    call with the same shape.  Peers write into them, and every launch ends
+    with all ranks meeting, so a peer runs at most one fused launch ahead:
+    consume each result before issuing the next fused call (as a model's next
+    op does).  Calls are collective: every rank makes the same sequence of
+    calls with the same shapes.  Shapes the fused kernel does not take (M > 64,
+    fp32, odd layouts) fall back to thin_linear and gather_columns (NCCL).
+    """
+
+    def __init__(self, group=None):
+        self.group = group
+        self.rank, self.world = _group_info(group)
+        self.sig = SymmetricBlock(_lib.SIGNAL_BYTES, group)
+        self.outs: dict[tuple, SymmetricBlock] = {}
+        self._sig_arr = (ctypes.c_void_p * self.world)(*self.sig.ptrs)
+        self._out_arrs: dict[tuple, ctypes.Array] = {}
+        self._calls: dict[tuple, int] = {}
+
+    def _out(self, M: int, N: int, dtype: torch.dtype):
+        calls = self._calls.get((M, N, dtype), 0)
+        self._calls[(M, N, dtype)] = calls + 1
+        key = (M, N, dtype, calls & 1)
+        blk = self.outs.get(key)
+        if blk is None:
+            esz = torch.empty((), dtype=dtype).element_size()
+            blk = self.outs[key] = SymmetricBlock(M * N * esz, self.group)
+            self._out_arrs[key] = (ctypes.c_void_p * self.world)(*blk.ptrs)
+        return blk.tensor.view(dtype).view(M, N), self._out_arrs[key]
+
+    def linear(self, x: torch.Tensor, w: torch.Tensor, w_up: torch.Tensor | None = None,
+               bias: torch.Tensor | None = None) -> torch.Tensor:
+        M, K = x.shape
+        n = w.shape[0]
+        N = n * self.world
+        code = _lib.dtype_code(x.dtype)
+        y, peers = self._out(M, N, x.dtype)
+        dev = x.device
+        ws = _lib.workspace(dev, _lib.lib().simsd_workspace_header_bytes())
+        rc = _lib.lib().simsd_thin_linear_allgather(
+            x.data_ptr(), x.stride(0), x.stride(1), w.data_ptr(), w.stride(0), w.stride(1),
+            w_up.data_ptr() if w_up is not None else None, bias.data_ptr() if bias is not None else None,
+            peers, N, self.rank * n, M, n, K, code, _lib.EPI_SILU_MUL if w_up is not None else _lib.EPI_NONE,
+            self.rank, self.world, self._sig_arr, ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
+        if rc == _lib.SIMSD_ERR_UNSUPPORTED:
+            local = thin_linear_silu_mul(x, w, w_up) if w_up is not None else thin_linear(x, w, bias)
+            return gather_columns(local, self.group)
+        _lib.check(rc, "thin_linear_allgather")
+        return y
+
+    def close(self) -> None:
+        for blk in self.outs.values():
+            blk.close()
+        self.outs.clear()
+        self.sig.close()
