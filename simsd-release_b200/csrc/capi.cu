@@ -453,7 +453,7 @@ int thin_cluster(const void* x, long long ldx_m, const void* w, long long ldw_n,
   const long long lw = (N > 1) ? ldw_n : ((K * 2 + 15) / 16) * 8;
   const uint64_t xd[2] = {(uint64_t)K, (uint64_t)M}, xs[1] = {(uint64_t)lx * 2};
   const uint64_t wd[2] = {(uint64_t)K, (uint64_t)N}, wsb[1] = {(uint64_t)lw * 2};
-  int rc = encode_map(&a.tmB, x, dtype, 2, xd, xs, TC_BOX_ROWS);
+  int rc = encode_map(&a.tmB, x, dtype, 2, xd, xs, (uint32_t)bmax);
   if (rc == SIMSD_OK) rc = encode_map(&a.tmA0, w, dtype, 2, wd, wsb, silu ? 64 : 128);
   if (rc == SIMSD_OK && silu) rc = encode_map(&a.tmA1, w_up, dtype, 2, wd, wsb, 64);
   if (rc != SIMSD_OK) return rc;
@@ -627,7 +627,7 @@ int simsd_thin_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w
     const long long lw = (N > 1) ? ldw_n : ((K * 2 + 15) / 16) * 8;
     const uint64_t xd[2] = {(uint64_t)K, (uint64_t)M}, xs[1] = {(uint64_t)lx * 2};
     const uint64_t wd[2] = {(uint64_t)K, (uint64_t)N}, wsb[1] = {(uint64_t)lw * 2};
-    int rc = encode_map(&a.tmB, x, dtype, 2, xd, xs, TC_BOX_ROWS);
+    int rc = encode_map(&a.tmB, x, dtype, 2, xd, xs, (uint32_t)pl.bmax);
     if (rc == SIMSD_OK) rc = encode_map(&a.tmA0, w, dtype, 2, wd, wsb, silu ? 64 : 128);
     if (rc == SIMSD_OK && silu) rc = encode_map(&a.tmA1, w_up, dtype, 2, wd, wsb, 64);
     if (rc != SIMSD_OK) return rc;
@@ -709,7 +709,7 @@ int simsd_thin_linear_noalloc(const void* x, int64_t ldx_m, int64_t ldx_k, const
     const long long lw = (N > 1) ? ldw_n : ((K * 2 + 15) / 16) * 8;
     const uint64_t xd[2] = {(uint64_t)K, (uint64_t)M}, xs[1] = {(uint64_t)lx * 2};
     const uint64_t wd[2] = {(uint64_t)K, (uint64_t)N}, wsb[1] = {(uint64_t)lw * 2};
-    int rc = encode_map(&a.tmB, x, dtype, 2, xd, xs, TC_BOX_ROWS);
+    int rc = encode_map(&a.tmB, x, dtype, 2, xd, xs, (uint32_t)pl.bmax);
     if (rc == SIMSD_OK) rc = encode_map(&a.tmA0, w, dtype, 2, wd, wsb, silu ? 64 : 128);
     if (rc == SIMSD_OK && silu) rc = encode_map(&a.tmA1, w_up, dtype, 2, wd, wsb, 64);
     if (rc != SIMSD_OK) return rc;
@@ -975,7 +975,7 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
       const uint64_t bs[1] = {(uint64_t)H * es};
       rc = encode_map(&a.tmA0, w_gate, dtype, 3, gd, gs, 64);
       if (rc == SIMSD_OK) rc = encode_map(&a.tmA1, w_up, dtype, 3, gd, gs, 64);
-      if (rc == SIMSD_OK) rc = encode_map(&a.tmB, xs, dtype, 2, bd, bs, TC_BOX_ROWS);
+      if (rc == SIMSD_OK) rc = encode_map(&a.tmB, xs, dtype, 2, bd, bs, (uint32_t)plan.bmax);
       if (rc != SIMSD_OK) return rc;
     }
     a.out = hbuf;
@@ -992,8 +992,13 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
     a.silu = 1;
     a.three_d = 1;
     a.is_bf16 = dtype == SIMSD_BF16 ? 1 : 0;
+    // a grouped GEMM with at least two tiles per CTA splits no tile (tc_whole_tiles);
+    // there are at least ceil(S / bmax) row chunks, so often that is known here
+    const long long min_chunks = std::max<long long>(1, cdiv(S, plan.bmax));
     rc = launch_tc(plan.bmax, a, plan.grid, s, dev);
-    if (rc == SIMSD_OK && a.counters == nullptr) rc = launch_fixup(plan.bmax, fixup_args(a, plan.grid), s);
+    if (rc == SIMSD_OK && a.counters == nullptr &&
+        !tc_whole_tiles(true, (int)std::min<long long>(min_chunks * a.row_tiles, 1 << 30), plan.grid))
+      rc = launch_fixup(plan.bmax, fixup_args(a, plan.grid), s);
     if (rc != SIMSD_OK) return rc;
     // down: ys[row, h] = hbuf[row] . w_down[e, h]
     TcGemmArgs d;
@@ -1004,7 +1009,7 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
       const uint64_t bd[2] = {(uint64_t)I, (uint64_t)S};
       const uint64_t bs[1] = {(uint64_t)I * es};
       rc = encode_map(&d.tmA0, w_down, dtype, 3, dd, ds, 128);
-      if (rc == SIMSD_OK) rc = encode_map(&d.tmB, hbuf, dtype, 2, bd, bs, TC_BOX_ROWS);
+      if (rc == SIMSD_OK) rc = encode_map(&d.tmB, hbuf, dtype, 2, bd, bs, (uint32_t)plan.bmax);
       if (rc != SIMSD_OK) return rc;
     }
     d.out = ys;
@@ -1022,7 +1027,9 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
     d.three_d = 1;
     d.is_bf16 = a.is_bf16;
     rc = launch_tc(plan.bmax, d, plan.grid, s, dev);
-    if (rc == SIMSD_OK && d.counters == nullptr) rc = launch_fixup(plan.bmax, fixup_args(d, plan.grid), s);
+    if (rc == SIMSD_OK && d.counters == nullptr &&
+        !tc_whole_tiles(true, (int)std::min<long long>(min_chunks * d.row_tiles, 1 << 30), plan.grid))
+      rc = launch_fixup(plan.bmax, fixup_args(d, plan.grid), s);
     if (rc != SIMSD_OK) return rc;
   } else {
     const long long max_chunks = std::min<long long>(E, S) + S / SIMT_ROWS + 1;

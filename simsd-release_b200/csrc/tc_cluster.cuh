@@ -195,9 +195,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
         dep_ready = true;
         for (int s2 = 0; s2 < npend; ++s2)
           for (int at = 0; at < pend_na[s2]; ++at)
-            for (int b = 0; b < nb; ++b)
-              tma_load_2d(pend_dst[s2] + at * Cfg::B_ATOM + b * TC_BOX_BYTES, &p.tmB, pend_bar[s2],
-                          pend_k0[s2] + at * 64, b * TC_BOX_ROWS, pol_x);
+            tma_load_2d(pend_dst[s2] + at * Cfg::B_ATOM, &p.tmB, pend_bar[s2], pend_k0[s2] + at * 64, 0, pol_x);
         npend = 0;
       };
       // L2 prefetch cursor over the (tile, stage) sequence: DRAM requests for the
@@ -226,7 +224,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
           if (!dep_ready && npend >= min(STAGES, p.prefetch)) flush_pending();
           if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, abort_flag, p.err)) { ok = false; break; }
           const uint32_t fb = smem_u32(&full_bar[stage]);
-          mbar_arrive_expect_tx(fb, na * (TC_A_BYTES + nb * TC_BOX_BYTES));
+          mbar_arrive_expect_tx(fb, na * (TC_A_BYTES + Cfg::B_ATOM));
           issued_mask |= 1u << stage;
           last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
           const uint32_t b_dst = smem_u32(sB + stage * Cfg::B_STAGE);
@@ -239,9 +237,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
             } else {
               tma_load_2d(a_dst, &p.tmA0, fb, k0, rtile * 128, pol_w);
             }
-            if (dep_ready)
-              for (int b = 0; b < nb; ++b)
-                tma_load_2d(b_dst + at * Cfg::B_ATOM + b * TC_BOX_BYTES, &p.tmB, fb, k0, b * TC_BOX_ROWS, pol_x);
+            if (dep_ready) tma_load_2d(b_dst + at * Cfg::B_ATOM, &p.tmB, fb, k0, 0, pol_x);
           }
           if (p.trace && !traced_first) { p.trace[blockIdx.x * 8 + 2] = globaltimer_ns(); traced_first = true; }
           if (!dep_ready) {
@@ -481,16 +477,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
     }
     if (p.world > 1) {
       // Fused all-gather: this CTA's stores to every rank are made visible
-      // (system-scope fence, then a release add on each rank's counter for
-      // this launch); CTA 0 of each rank then waits until all ranks' CTAs have
+      // (a CTA barrier, then one thread's system-scope fence and a release add
+      // on each rank's counter for this launch; the barrier orders the other
+      // threads' stores before them); CTA 0 of each rank then waits until all ranks' CTAs have
       // added, so the launch completes only when this rank's y is whole.
       // Counter slot = this rank's launch count mod TC_SIG_SLOTS, kept on the
       // device (graph replays advance it); every rank launches the same
       // sequence, so the slots agree.  The wait is bounded.
       griddep_wait();   // the previous launch's count update is visible (no-op without PDL)
-      __threadfence_system();
-      named_bar_sync(1, 128);
+      named_bar_sync(1, 128);   // every epilogue thread's stores precede thread 0's release
       if (row == 0) {
+        __threadfence_system();
         int* my_sig = p.peer_sig[p.rank];
         const int seq = *reinterpret_cast<volatile int*>(my_sig + TC_SIG_SLOTS);
         const int slot = seq & (TC_SIG_SLOTS - 1);

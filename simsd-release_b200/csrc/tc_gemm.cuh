@@ -38,8 +38,10 @@ namespace simsd {
 
 constexpr int TC_THREADS = 192;            // warps 0-3 epilogue, 4 TMA, 5 MMA
 constexpr int TC_A_BYTES = 128 * 128;      // 128 weight rows x 64 bf16
-constexpr int TC_BOX_ROWS = 16;            // activation rows per TMA box
-constexpr int TC_BOX_BYTES = TC_BOX_ROWS * 128;
+constexpr int TC_BOX_ROWS = 16;            // activation rows per MMA N step (tcgen05 N granularity)
+// The activation tile of a stage atom is one TMA box of BMAX rows x 64 K
+// (128-byte rows, SW128); rows past the valid ones (beyond M, or the next
+// expert's rows in grouped mode) are loaded or zero-filled and never stored.
 constexpr int TC_MAX_GROUPS = 1024;
 constexpr int TC_MAX_GRID = 1024;          // CTAs per launch (segments per tile <= this)
 constexpr int WS_COUNTER_BYTES = 256 * 1024;          // head of every workspace (reserved)
@@ -126,6 +128,14 @@ __device__ __forceinline__ TileInfo decode_tile(int j, const TcGemmArgs& p,
     ti.nrows = min(BMAX, row_prefix[lo + 1] - ti.row0);
   }
   return ti;
+}
+
+// Work split of a grouped (MoE) GEMM with at least two tiles per CTA: whole
+// tiles, balanced by count (the experts' tiles are many and alike, so this
+// loses little balance and needs no split-K partials).  Otherwise, and always
+// in single mode, the stream-K split below.
+__host__ __device__ __forceinline__ bool tc_whole_tiles(bool grouped, int total_tiles, int grid) {
+  return grouped && total_tiles >= 2 * grid;
 }
 
 // Stream-K partition of `iters` (tile, k-block) iterations over G CTAs: the
@@ -350,7 +360,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
   const int c = blockIdx.x;
   const SkSplit sk(iters, G > 0 ? G : 1);
   int it_begin = 0, it_end = 0;
-  if (c < G) {
+  if (tc_whole_tiles(p.group_counts != nullptr, (int)total_tiles, (int)gridDim.x)) {
+    // grouped GEMM with at least two tiles per CTA: whole tiles, balanced by
+    // count — no split tile, so no partials and nothing for the fixup
+    const SkSplit ts((int)total_tiles, (int)gridDim.x);
+    it_begin = ts.start(c) * kb;
+    it_end = ts.start(c + 1) * kb;
+  } else if (c < G) {
     it_begin = sk.start(c);
     it_end = sk.start(c + 1);
   }
@@ -374,15 +390,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
       int npend = 0;
       bool traced_first = false;
       uint32_t pend_dst[Cfg::STAGES], pend_bar[Cfg::STAGES];
-      int pend_k0[Cfg::STAGES], pend_na[Cfg::STAGES], pend_row0[Cfg::STAGES], pend_nb[Cfg::STAGES];
+      int pend_k0[Cfg::STAGES], pend_na[Cfg::STAGES], pend_row0[Cfg::STAGES];
       auto flush_pending = [&]() {
         griddep_wait();
         dep_ready = true;
         for (int q = 0; q < npend; ++q)
           for (int at = 0; at < pend_na[q]; ++at)
-            for (int b = 0; b < pend_nb[q]; ++b)
-              tma_load_2d(pend_dst[q] + at * Cfg::B_ATOM + b * TC_BOX_BYTES, &p.tmB, pend_bar[q],
-                          pend_k0[q] + at * 64, pend_row0[q] + b * TC_BOX_ROWS, pol_x);
+            tma_load_2d(pend_dst[q] + at * Cfg::B_ATOM, &p.tmB, pend_bar[q], pend_k0[q] + at * 64, pend_row0[q], pol_x);
         npend = 0;
       };
       for (int it = it_begin; ok && it < it_end;) {
@@ -396,7 +410,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
           if (!dep_ready && npend >= min(STAGES, p.prefetch)) flush_pending();
           if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, abort_flag, p.err)) { ok = false; break; }
           const uint32_t fb = smem_u32(&full_bar[stage]);
-          mbar_arrive_expect_tx(fb, na * (TC_A_BYTES + nb * TC_BOX_BYTES));
+          mbar_arrive_expect_tx(fb, na * (TC_A_BYTES + Cfg::B_ATOM));
           issued_mask |= 1u << stage;
           last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
           const uint32_t b_dst = smem_u32(sB + stage * Cfg::B_STAGE);
@@ -417,11 +431,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
               if (p.three_d) tma_load_3d(a_dst, &p.tmA0, fb, k0, r0, ti.group, pol_w);
               else tma_load_2d(a_dst, &p.tmA0, fb, k0, r0, pol_w);
             }
-            if (dep_ready) {
-              for (int b = 0; b < nb; ++b)
-                tma_load_2d(b_dst + at * Cfg::B_ATOM + b * TC_BOX_BYTES, &p.tmB, fb, k0, ti.row0 + b * TC_BOX_ROWS,
-                            pol_x);
-            }
+            if (dep_ready) tma_load_2d(b_dst + at * Cfg::B_ATOM, &p.tmB, fb, k0, ti.row0, pol_x);
           }
           if (p.trace && !traced_first) { p.trace[blockIdx.x * 8 + 2] = globaltimer_ns(); traced_first = true; }
           if (!dep_ready) {
@@ -430,7 +440,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
             pend_k0[npend] = k * 64;
             pend_na[npend] = na;
             pend_row0[npend] = ti.row0;
-            pend_nb[npend] = nb;
             ++npend;
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -659,6 +668,7 @@ __global__ void __launch_bounds__(128) tc_fixup_kernel(const TcFixupArgs p) {
   const int kb = p.kb;
   const int iters = total_tiles * kb;
   if (iters == 0) return;
+  if (tc_whole_tiles(p.group_counts != nullptr, total_tiles, p.grid)) return;   // no split tiles
   const int G = min(p.grid, iters);
   const int cb = blockIdx.x + 1;                       // CTA boundary: start of CTA cb
   if (cb >= G) return;
