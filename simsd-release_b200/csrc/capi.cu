@@ -797,12 +797,23 @@ int simsd_moe_route(const void* x, int64_t ldx, int x_dtype, const void* wr, int
     while (tt > 4 && smem_for(tt) > 200 * 1024) tt >>= 1;
     if (smem_for(tt) <= 200 * 1024) {
       const size_t smem = smem_for(tt);
-      const dim3 grid((unsigned)cdiv(T, tt)), block(ROUTE_WARPS * 32);
+      // few token blocks: split the experts over blocks as well (logits to
+      // `logits`, then route_topk_kernel) so the router uses more SMs
+      const long long bx = cdiv(T, tt);
+      int ny = 1;
+      if (logits != nullptr && bx * 2 <= sms) ny = (int)std::min<long long>(16, sms / bx);
+      const dim3 grid((unsigned)bx, (unsigned)ny), block(ROUTE_WARPS * 32);
       cudaStream_t st = (cudaStream_t)stream;
       auto go = [&](auto kern) -> int {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess)
           return SIMSD_ERR_LAUNCH;
-        return launch(kern, grid, block, smem, st, a);
+        int rc = launch(kern, grid, block, smem, st, a);
+        if (rc != SIMSD_OK || ny == 1) return rc;
+        const size_t tsmem = (size_t)2 * ROUTE_WARPS * E * sizeof(float);
+        if (cudaFuncSetAttribute(route_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsmem) !=
+            cudaSuccess)
+          return SIMSD_ERR_LAUNCH;
+        return launch(route_topk_kernel, dim3((unsigned)cdiv(T, ROUTE_WARPS)), block, tsmem, st, a);
       };
       if (w_dtype == SIMSD_F32) {
         if (tt == 16) return go(route_fast_kernel<16, float>);

@@ -258,7 +258,11 @@ __global__ void __launch_bounds__(ROUTE_WARPS * 32) route_fast_kernel(const Rout
   __syncthreads();
 
   const int nchunks = vec_per_row;
-  for (int e0 = warp * EE; e0 < E; e0 += ROUTE_WARPS * EE) {
+  // experts of this block: all of them, or (grid.y > 1) a slice whose logits go
+  // to p.logits for route_topk_kernel
+  const int per = gridDim.y > 1 ? ((E + gridDim.y - 1) / gridDim.y + EE - 1) / EE * EE : E;
+  const int ebeg = blockIdx.y * per, eend = min(E, ebeg + per);
+  for (int e0 = ebeg + warp * EE; e0 < eend; e0 += ROUTE_WARPS * EE) {
     float v[32];
 #pragma unroll
     for (int q = 0; q < 32; ++q) v[q] = 0.0f;
@@ -271,7 +275,7 @@ __global__ void __launch_bounds__(ROUTE_WARPS * 32) route_fast_kernel(const Rout
         const int e = e0 + j;
 #pragma unroll
         for (int q = 0; q < WV; ++q) {
-          if (e < E && c < nchunks)
+          if (e < eend && c < nchunks)
             dst[j][q] = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(p.w) +
                                                         ((long long)e * p.ldw + c * 8) * sizeof(WT) + q * 16);
           else
@@ -345,13 +349,37 @@ __global__ void __launch_bounds__(ROUTE_WARPS * 32) route_fast_kernel(const Rout
       }
     }
     const int t = lane / EE, e = e0 + (lane % EE);
-    if (t < ntok && e < E) {
+    if (t < ntok && e < eend) {
       const float lg = v[0];
       if (p.logits) p.logits[(long long)(t0 + t) * E + e] = lg;
-      const float sc = sigmoid_fixed(lg);
-      s_score[t * E + e] = sc;
-      s_choice[t * E + e] = p.bias ? __fadd_rn(sc, p.bias[e]) : sc;
+      if (gridDim.y == 1) {
+        const float sc = sigmoid_fixed(lg);
+        s_score[t * E + e] = sc;
+        s_choice[t * E + e] = p.bias ? __fadd_rn(sc, p.bias[e]) : sc;
+      }
     }
+  }
+  if (gridDim.y > 1) return;   // route_topk_kernel selects from p.logits
+  __syncthreads();
+  route_topk(p, s_score, s_choice, t0, ntok);
+}
+
+// Top-k over logits that route_fast_kernel wrote with its experts split over
+// blocks (few tokens, so that the logits use many SMs): the same sigmoid, bias
+// and selection as its fused path, ROUTE_WARPS tokens per block.
+__global__ void __launch_bounds__(ROUTE_WARPS * 32) route_topk_kernel(const RouteArgs p) {
+  griddep_launch_dependents();
+  griddep_wait();
+  extern __shared__ float tsh[];
+  float* s_score = tsh;                        // [ROUTE_WARPS][E]
+  float* s_choice = tsh + ROUTE_WARPS * p.E;   // [ROUTE_WARPS][E]
+  const int t0 = blockIdx.x * ROUTE_WARPS;
+  const int ntok = min(ROUTE_WARPS, p.T - t0);
+  for (int i = threadIdx.x; i < ntok * p.E; i += blockDim.x) {
+    const int t = i / p.E, e = i - t * p.E;
+    const float sc = sigmoid_fixed(p.logits[(long long)(t0 + t) * p.E + e]);
+    s_score[i] = sc;
+    s_choice[i] = p.bias ? __fadd_rn(sc, p.bias[e]) : sc;
   }
   __syncthreads();
   route_topk(p, s_score, s_choice, t0, ntok);

@@ -109,14 +109,16 @@ def moe_route(x: torch.Tensor, w_router: torch.Tensor, bias: torch.Tensor | None
         w_router = w_router.contiguous()
     ids = torch.empty((T, k), dtype=torch.int64, device=dev)
     wts = torch.empty((T, k), dtype=torch.float32, device=dev)
-    logits = torch.empty((T, E), dtype=torch.float32, device=dev) if return_logits else None
+    # always handed to the library: with few tokens it splits the experts over
+    # blocks and passes the logits through this buffer to its top-k kernel
+    logits = torch.empty((T, E), dtype=torch.float32, device=dev)
     with _lib.device_guard(dev):
         rc = _lib.lib().simsd_moe_route(
             x.data_ptr(), x.stride(0), _lib.dtype_code(x.dtype),
             w_router.data_ptr(), w_router.stride(0), _lib.dtype_code(w_router.dtype),
             bias.data_ptr() if bias is not None else None, T, H, E, k, int(bool(renorm)),
             ctypes.c_float(scale), ids.data_ptr(), wts.data_ptr(),
-            logits.data_ptr() if logits is not None else None, _lib.stream_ptr(dev))
+            logits.data_ptr(), _lib.stream_ptr(dev))
     _lib.check(rc, "moe_route")
     return (ids, wts, logits) if return_logits else (ids, wts)
 
