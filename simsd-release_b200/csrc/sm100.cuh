@@ -304,6 +304,11 @@ __device__ __forceinline__ bool mbar_wait_cluster_drain(uint32_t bar, uint32_t p
 __device__ __forceinline__ void red_add_release_sys(int* addr, int v) {
   asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
 }
+__device__ __forceinline__ int atom_add_acq_rel_sys(int* addr, int v) {
+  int old;
+  asm volatile("atom.acq_rel.sys.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+  return old;
+}
 __device__ __forceinline__ int ld_acquire_sys(const int* addr) {
   int v;
   asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");

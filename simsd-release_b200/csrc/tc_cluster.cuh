@@ -34,7 +34,7 @@ namespace simsd {
 
 constexpr int TC_CL_MAX = 8;          // largest cluster (portable)
 constexpr int TC_AG_MAX_WORLD = 8;    // ranks of a fused column-parallel all-gather
-constexpr int TC_SIG_SLOTS = 32;      // signal counters per rank, used round robin
+constexpr int TC_SIG_SLOTS = 16;      // launch slots of a rank's signal block, used round robin
 constexpr int TC_CL_RED_ROWS = 144;   // >= S * rows one owner holds, for every S <= 8
 
 struct TcClusterArgs {
@@ -57,7 +57,9 @@ struct TcClusterArgs {
   // then the ranks' CTAs meet on counters in peer_sig (see the kernel's end)
   int world, rank, col_offset;
   void* peer_out[TC_AG_MAX_WORLD];
-  int* peer_sig[TC_AG_MAX_WORLD];  // each rank's signal block: TC_SIG_SLOTS counters, then its launch count
+  // each rank's signal block (ints): [0, SLOTS) ranks arrived, [SLOTS, 2 SLOTS)
+  // this rank's CTAs arrived, [2 SLOTS] this rank's launch count
+  int* peer_sig[TC_AG_MAX_WORLD];
 };
 
 template <int BMAX, int KS>
@@ -476,26 +478,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
       mbar_wait_cluster_drain(red_full_u32, done & 1, 100000000ull);
     }
     if (p.world > 1) {
-      // Fused all-gather: this CTA's stores to every rank are made visible
-      // (a CTA barrier, then one thread's system-scope fence and a release add
-      // on each rank's counter for this launch; the barrier orders the other
-      // threads' stores before them); CTA 0 of each rank then waits until all ranks' CTAs have
-      // added, so the launch completes only when this rank's y is whole.
-      // Counter slot = this rank's launch count mod TC_SIG_SLOTS, kept on the
-      // device (graph replays advance it); every rank launches the same
-      // sequence, so the slots agree.  The wait is bounded.
+      // Fused all-gather: the launch completes only when this rank's y is
+      // whole.  Each CTA counts itself on its own rank with a system-scope
+      // acquire-release add (after a CTA barrier, so it covers every epilogue
+      // thread's stores, local and remote); the rank's last CTA then adds 1,
+      // with release, to the rank counter of every rank; CTA 0 of each rank
+      // waits (bounded) until all ranks have added.  Slots follow this rank's
+      // launch count, kept on the device (graph replays advance it); every
+      // rank launches the same sequence, so the slots agree.
       griddep_wait();   // the previous launch's count update is visible (no-op without PDL)
-      named_bar_sync(1, 128);   // every epilogue thread's stores precede thread 0's release
+      named_bar_sync(1, 128);
       if (row == 0) {
-        __threadfence_system();
         int* my_sig = p.peer_sig[p.rank];
-        const int seq = *reinterpret_cast<volatile int*>(my_sig + TC_SIG_SLOTS);
+        const int seq = *reinterpret_cast<volatile int*>(my_sig + 2 * TC_SIG_SLOTS);
         const int slot = seq & (TC_SIG_SLOTS - 1);
-        for (int r = 0; r < p.world; ++r) red_add_release_sys(p.peer_sig[r] + slot, 1);
+        if (atom_add_acq_rel_sys(my_sig + TC_SIG_SLOTS + slot, 1) == (int)gridDim.x - 1) {
+          my_sig[TC_SIG_SLOTS + slot] = 0;   // every CTA of this launch has counted
+          for (int r = 0; r < p.world; ++r) red_add_release_sys(p.peer_sig[r] + slot, 1);
+        }
         if (blockIdx.x == 0) {
-          const int total = p.world * (int)gridDim.x;
           const uint64_t t0 = globaltimer_ns();
-          while (ld_acquire_sys(my_sig + slot) < total) {
+          while (ld_acquire_sys(my_sig + slot) < p.world) {
             if (globaltimer_ns() - t0 > SIMSD_WAIT_LIMIT_NS) {
               atomicOr(p.err, SIMSD_DEV_ERR_TIMEOUT);
               break;
@@ -503,7 +506,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
           }
           my_sig[slot] = 0;   // no rank adds to this slot again before this launch count comes round
           __threadfence_system();
-          *reinterpret_cast<volatile int*>(my_sig + TC_SIG_SLOTS) = seq + 1;
+          *reinterpret_cast<volatile int*>(my_sig + 2 * TC_SIG_SLOTS) = seq + 1;
         }
       }
     }
