@@ -238,6 +238,16 @@ __device__ __forceinline__ uint32_t cluster_count_x() {
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Split form: every thread arrives (releasing its shared-memory writes, e.g.
+// barrier initialisation) and later waits (acquiring the other CTAs'), so the
+// wait can sit right before the first remote access instead of on the start-up
+// path.  Each thread must wait once after it arrived, before the CTA exits.
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 // Address in CTA `rank`'s shared memory of the variable at local address `a`.
 __device__ __forceinline__ uint32_t mapa_shared(uint32_t a, uint32_t rank) {
   uint32_t d;

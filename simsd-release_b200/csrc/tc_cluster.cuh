@@ -160,8 +160,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
   }
   if (tid == 0) griddep_launch_dependents();
   tc_fence_before();
-  // barrier initialisation visible to the whole cluster before any remote use
-  cluster_sync_all();
+  // Barrier initialisation is released to the cluster here and acquired by the
+  // epilogue right before its first remote access (and by every other thread at
+  // its end), so no CTA waits for its peers on the start-up path.
+  cluster_arrive_release();
+  __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   if (p.trace && tid == 0) p.trace[blockIdx.x * 8 + 1] = globaltimer_ns();
@@ -260,6 +263,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
             mbar_wait_drain(smem_u32(&full_bar[s2]), (last_parity >> s2) & 1u, 100000000ull);
       }
     }
+    __syncwarp();
+    cluster_wait_acquire();   // pairs this warp's set-up arrive
   } else if (warp == 5) {
     // ================= MMA issuer
     if (lane == 0) {
@@ -299,6 +304,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
         mbar_wait_drain(smem_u32(drain_bar), 0, 100000000ull);
       }
     }
+    __syncwarp();
+    cluster_wait_acquire();   // pairs this warp's set-up arrive
   } else {
     // ================= epilogue warps 0-3: TMEM lanes 32*warp .. 32*warp+31
     const int row = tid;   // 0..127 == TMEM lane == accumulator (weight) row
@@ -312,6 +319,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
     const uint32_t red_full_u32 = smem_u32(red_full);
     const uint32_t red_free_u32 = smem_u32(red_free);
     auto swz = [](int lr, int j) { return BMAX >= 32 ? (j ^ (lr & 7)) : (j ^ ((lr >> 1) & 3)); };
+    bool cluster_acquired = false;
     // y[t, col] on this GPU, or on every rank's GPU for the fused all-gather
     auto put = [&](long long t, int col, float v) {
       if (p.world <= 1) {
@@ -374,6 +382,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
         continue;
       }
 
+      if (!cluster_acquired) {
+        cluster_wait_acquire();   // the peers' barriers are initialised
+        cluster_acquired = true;
+      }
       // -- 1. the owners have consumed this CTA's rows of the previous tile
       if (i > 0 && !named_bar_and(1, 128, mbar_wait_cluster(red_free_u32, (i - 1) & 1, abort_flag, p.err))) break;
       // -- 2. bytes this CTA receives for the tile: its rows from every peer
@@ -473,6 +485,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
       }
       ++done;
     }
+    if (!cluster_acquired) cluster_wait_acquire();
     if (S > 1 && done < n_tiles && row == 0) {
       // aborting: give peers that may still be sending to this CTA time to land
       mbar_wait_cluster_drain(red_full_u32, done & 1, 100000000ull);
