@@ -159,10 +159,11 @@ def make_inputs(dev, seed=7):
             for M in MS}
 
 
-def run_step(ws, xs, world, dist, ag=None):
+def run_step(ws, xs, world, dist, ag=None, on_result=None):
     """One sweep step.  world > 1: each linear is column-parallel, its output
     all-gathered by `ag` (FusedAllGather: fused into the GEMM over NVLink) or,
-    without it, by an NCCL all-gather after the local GEMM."""
+    without it, by an NCCL all-gather after the local GEMM.  `on_result(j, y)`
+    is called right after the j-th linear is launched."""
     from kernels.parallel import gather_columns
     from kernels.thin_linear_fused import thin_linear, thin_linear_silu_mul
     res = []
@@ -175,6 +176,8 @@ def run_step(ws, xs, world, dist, ag=None):
                 y = thin_linear_silu_mul(x, *ws[name]) if silu else thin_linear(x, ws[name])
                 if world > 1:
                     y = gather_columns(y)
+            if on_result is not None:
+                on_result(len(res), y)
             res.append(y)
     return res
 
@@ -289,19 +292,61 @@ def gpu_arm(args):
 
         # end to end through the public API: pinned host inputs -> device -> host outputs
         hx = {M: {K: xs[M][K].cpu().pin_memory() for K in (4096, 12288)} for M in MS}
-        houts = None
         h2d = sum(hx[M][K].numel() * 2 for M in MS for K in (4096, 12288))
         d2h = 0
         for M in MS:
             for _, K, N, silu in SHAPES:
                 d2h += M * ((N // 2) if silu else N) * 2
-        for _ in range(3):
-            dxs = {M: {K: hx[M][K].to(dev, non_blocking=True) for K in (4096, 12288)} for M in MS}
-            res = run_step(pool[0], dxs, world, dist, ag)
-            if houts is None:
-                houts = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
-            for h, r in zip(houts, res):
-                h.copy_(r, non_blocking=True)
+        # The step as a serving loop runs it: captured once per weight copy in a
+        # CUDA graph of public-API calls (as the reference's runners capture
+        # their verify step), with the host copies inside: the step's inputs
+        # copied from pinned host memory into static device buffers, and each
+        # result copied to pinned host memory on a side stream as soon as its
+        # linear is done, overlapping the next linears.
+        cs = torch.cuda.Stream(dev)
+        houts = [torch.empty((M, (N // 2) if silu else N), dtype=torch.bfloat16, pin_memory=True)
+                 for M in MS for _, K, N, silu in SHAPES]
+        sx = {M: {K: torch.empty_like(xs[M][K]) for K in (4096, 12288)} for M in MS}
+
+        hs = torch.cuda.Stream(dev)
+
+        def e2e_step(p):
+            main = torch.cuda.current_stream(dev)   # the capture stream while capturing
+            # inputs: copied per activation height on their own stream, each
+            # height's linears waiting only for its own rows
+            hs.wait_stream(main)
+            ready = {}
+            for M in MS:
+                with torch.cuda.stream(hs):
+                    for K in (4096, 12288):
+                        sx[M][K].copy_(hx[M][K], non_blocking=True)
+                    ready[M] = torch.cuda.Event()
+                    ready[M].record(hs)
+            per_m = len(SHAPES)
+
+            def out(j, y):
+                if (j + 1) % per_m == 0 and j + 1 < len(houts):
+                    main.wait_event(ready[MS[(j + 1) // per_m]])
+                cs.wait_stream(main)
+                with torch.cuda.stream(cs):
+                    houts[j].copy_(y, non_blocking=True)     # into pinned host buffers
+
+            main.wait_event(ready[MS[0]])
+            run_step(pool[p], sx, world, dist, ag, on_result=out)
+            main.wait_stream(cs)
+            main.wait_stream(hs)
+
+        for _ in range(2):
+            e2e_step(0)
+        torch.cuda.synchronize()
+        e2e_graphs = []
+        for p in range(POOL):
+            ge = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(ge):
+                e2e_step(p)
+            e2e_graphs.append(ge)
+        for i in range(3):
+            e2e_graphs[i % POOL].replay()
         torch.cuda.synchronize()
         if dist:
             dist.barrier()
@@ -309,10 +354,7 @@ def gpu_arm(args):
         e2e_steps = max(3, min(args.steps, 20))
         e2.record()
         for i in range(e2e_steps):
-            dxs = {M: {K: hx[M][K].to(dev, non_blocking=True) for K in (4096, 12288)} for M in MS}
-            res = run_step(pool[i % POOL], dxs, world, dist, ag)
-            for h, r in zip(houts, res):
-                h.copy_(r, non_blocking=True)   # into pinned host buffers
+            e2e_graphs[i % POOL].replay()
         e3.record()
         torch.cuda.synchronize()
         e2e_ms = e2.elapsed_time(e3) / e2e_steps
@@ -321,6 +363,8 @@ def gpu_arm(args):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_ms = float(t.item())
         del houts
+        e2e_graphs.clear()
+        del ge
         # CUDA graphs that hold NCCL calls must be gone before the process
         # group is destroyed, or destroy_process_group waits for good
         graphs.clear()
@@ -353,7 +397,9 @@ def gpu_arm(args):
         "frac_of_hbm_peak": round(value / world / pk["hbm_gbs"], 4),
         "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "path": "kernels.thin_linear_fused public API -> libsimsd_b200 C ABI, pinned host buffers"},
+                "path": "kernels.thin_linear_fused public API -> libsimsd_b200 C ABI, replayed from a CUDA graph "
+                        "with the copies inside: pinned host inputs -> device per activation height and each "
+                        "result -> pinned host on side streams, overlapping the linears"},
         "gpu_launches": args.steps * launches_per_step,
     }
     if per is not None:
