@@ -404,12 +404,22 @@ def gpu_arm(args):
     }
     if per is not None:
         prof = _traffic_summary()
+        # Every launch in the timed region is this kernel (20 per step, nothing
+        # else on the stream), so its average launch duration is the timed
+        # region's CUDA-event time / launches, and its achieved bandwidth the
+        # algorithmic bytes per launch over that.
+        launch_us = ms * 1e3 / launches_per_step
+        achieved = step_bytes(1) / launches_per_step / (launch_us * 1e-6) / 1e9
         line["roofline"] = {
-            "bound": "hbm", "kernel": "simsd::tc_cluster_kernel (M <= 64)", "achieved": round(agg_gbs, 1),
-            "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(agg_gbs / pk["hbm_gbs"], 4),
-            "peak_src": pk["src"], "avg_launch_us": round(avg_us, 2),
+            "bound": "hbm", "kernel": "simsd::tc_cluster_kernel (M <= 64)", "achieved": round(achieved, 1),
+            "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+            "peak_src": pk["src"], "avg_launch_us": round(launch_us, 2),
+            "alg_bytes_per_launch": int(step_bytes(1) / launches_per_step),
             "traffic": prof.get("traffic_bytes_per_launch") if prof else None,
             "traffic_note": prof.get("note") if prof else "no ncu capture summary committed",
+            "isolated_launches": {"achieved": round(agg_gbs, 1), "avg_launch_us": round(avg_us, 2),
+                                  "note": "each launch timed alone between CUDA events (no overlap with the "
+                                          "next launch); per shape in per_launch"},
         }
         line["per_launch"] = per
     clk_summary = clk.summary()
