@@ -116,6 +116,18 @@ def stream_ptr(dev: torch.device) -> int:
     return torch.cuda.current_stream(dev).cuda_stream
 
 
+_SIDE_STREAMS: dict[torch.device, torch.cuda.Stream] = {}
+
+
+def side_stream(dev: torch.device) -> torch.cuda.Stream:
+    """A second stream per device for work that overlaps the caller's stream
+    (callers order it with wait_stream on both sides)."""
+    s = _SIDE_STREAMS.get(dev)
+    if s is None:
+        s = _SIDE_STREAMS[dev] = torch.cuda.Stream(device=dev)
+    return s
+
+
 def device_guard(dev: torch.device):
     """`torch.cuda.device(dev)` when `dev` is not the current device (tensors of a
     sharded model may live elsewhere); a no-op context otherwise, which keeps the

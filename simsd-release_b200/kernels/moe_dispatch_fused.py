@@ -187,13 +187,24 @@ def moe_layer(x, w_router, router_bias, k, w_gate, w_up, w_down,
 
     The shared expert is the dense SwiGLU `down(silu(gate(x)) * up(x))`, run as
     two thin-linear launches; its output is added to the routed output in x.dtype.
+    It does not depend on the routing, so it runs on a side stream while the
+    router runs on the caller's stream (the router's kernels use a few SMs; the
+    shared expert's weight stream fills the rest); the caller's stream waits
+    for it before the dispatch.  Both orders of work are graph-capturable.
     """
     from .thin_linear_fused import thin_linear, thin_linear_silu_mul
-    ids, wts = moe_route(x, w_router, router_bias, k=k, renorm=renorm, scale=scale)
     add = None
     if shared is not None:
         sg, su, sd = shared
-        add = thin_linear(thin_linear_silu_mul(x, sg, su), sd)
+        main = torch.cuda.current_stream(x.device)
+        side = _lib.side_stream(x.device)
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            add = thin_linear(thin_linear_silu_mul(x, sg, su), sd)
+    ids, wts = moe_route(x, w_router, router_bias, k=k, renorm=renorm, scale=scale)
+    if add is not None:
+        main.wait_stream(side)
+        add.record_stream(main)
     return moe_dispatch(x, ids, wts, w_gate, w_up, w_down, add=add)
 
 
