@@ -370,6 +370,11 @@ __device__ __forceinline__ void store_f(void* p, int64_t i, float v, int dtype) 
   else
     reinterpret_cast<float*>(p)[i] = v;
 }
+// fp32 -> the bits of a bf16 (dtype 0) or fp16 (dtype 1), round to nearest even
+__device__ __forceinline__ uint16_t f32_to_16bit(float v, int dtype) {
+  if (dtype == 0) return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  return __half_as_ushort(__float2half_rn(v));
+}
 __device__ __forceinline__ float silu_mul(float g, float u) {
   return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
 }

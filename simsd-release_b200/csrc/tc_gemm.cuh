@@ -87,12 +87,15 @@ struct TcConfig {
   static constexpr int A_STAGE = KS * A_ATOM;
   static constexpr int B_STAGE = KS * B_ATOM;
   static constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
-  static constexpr int STAGES_RAW = (RING_KB * 1024) / STAGE_BYTES;
+  // the small ring gives up 8 KB so that two CTAs' tails still fit an SM
+  static constexpr int RING_BYTES = (RING_KB >= 196 ? RING_KB : RING_KB - 8) * 1024;
+  static constexpr int STAGES_RAW = RING_BYTES / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 10 ? 10 : STAGES_RAW;
   static constexpr int TMEM_COLS = (2 * BMAX) < 32 ? 32 : 2 * BMAX;
-  // tail: barriers (2*STAGES + 5) x 8, misc ints 16, prefixes 2 x (MAX_GROUPS+1), xbuf 64x16 fp32
+  // tail: barriers (2*STAGES + 5) x 8, misc ints 16, prefixes 2 x (MAX_GROUPS+1), xbuf 64x16 fp32,
+  // output staging 2 x 16 x 128 16-bit
   static constexpr int TAIL_BYTES =
-      (2 * STAGES + 5) * 8 + 64 + 2 * (TC_MAX_GROUPS + 1) * 4 + 16 + 64 * 16 * 4;
+      (2 * STAGES + 5) * 8 + 64 + 2 * (TC_MAX_GROUPS + 1) * 4 + 16 + 64 * 16 * 4 + 16 + 2 * 16 * 128 * 2;
   static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + TAIL_BYTES;
   static_assert(STAGES >= 2, "ring needs two stages");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
@@ -271,6 +274,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
   int* row_prefix = misc + 16;                       // [num_groups + 1]
   int* chunk_prefix = row_prefix + (TC_MAX_GROUPS + 1);
   float* xbuf = reinterpret_cast<float*>(chunk_prefix + (TC_MAX_GROUPS + 1) + 4);  // [16][64]
+  uint16_t* sout = reinterpret_cast<uint16_t*>((reinterpret_cast<uintptr_t>(xbuf + 16 * 64) + 15) &
+                                               ~uintptr_t(15));                      // [2][16][128]
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -508,6 +513,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
   } else {
     // ================= epilogue warps 0-3: TMEM lanes 32*warp .. 32*warp+31
     const int row = tid;  // 0..127 == TMEM lane == tile row
+    // 16-byte output pieces need a 16-byte aligned base and row stride
+    const bool out_vec = (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 && (p.ld_out & 7) == 0;
     int acc_iter = 0;
     for (int it = it_begin; it < it_end;) {
       const int tile = it / kb;
@@ -528,6 +535,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
       char* outp = reinterpret_cast<char*>(p.out);
 
       if (whole) {
+        // Each 16-row chunk of the accumulator is rounded into a shared staging
+        // buffer laid out like the output ([activation row][column], 16-bit),
+        // then written as 16-byte row pieces: a warp store covers whole output
+        // rows instead of one 2-byte column per thread.  Two staging buffers
+        // alternate, so one barrier per chunk orders writes and reads (the
+        // SiLU*mul path has a second one for the up half in xbuf).
+        const int odt = p.is_bf16 ? 0 : 1;
+        const int ncols = p.silu ? 64 : 128;
         for (int ch = 0; ch < nb; ++ch) {
           float v[16];
           tmem_ld16(t_base + ch * 16, v);
@@ -536,17 +551,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
             tc_fence_before();
             mbar_arrive(smem_u32(&acce_bar[a]));
           }
+          uint16_t* sb = sout + (ch & 1) * (16 * 128);
           if (!p.silu) {
             const int col = out_col0 + row;
-            if (col < p.rows_out) {
-              const float bv = p.bias ? load_f(p.bias, col, p.is_bf16 ? 0 : 1) : 0.0f;
+            const float bv = (p.bias && col < p.rows_out) ? load_f(p.bias, col, odt) : 0.0f;
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const int t = ch * 16 + j;
-                if (t < ti.nrows)
-                  store_f(outp, (long long)(ti.row0 + t) * p.ld_out + col, __fadd_rn(v[j], bv), p.is_bf16 ? 0 : 1);
-              }
-            }
+            for (int j = 0; j < 16; ++j) sb[j * 128 + row] = f32_to_16bit(__fadd_rn(v[j], bv), odt);
           } else {
             if (row >= 64) {
 #pragma unroll
@@ -554,18 +564,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
             }
             named_bar_sync(1, 128);
             if (row < 64) {
-              const int col = out_col0 + row;
-              if (col < p.rows_out) {
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                  const int t = ch * 16 + j;
-                  if (t < ti.nrows)
-                    store_f(outp, (long long)(ti.row0 + t) * p.ld_out + col, silu_mul(v[j], xbuf[j * 64 + row]),
-                            p.is_bf16 ? 0 : 1);
-                }
-              }
+              for (int j = 0; j < 16; ++j) sb[j * 64 + row] = f32_to_16bit(silu_mul(v[j], xbuf[j * 64 + row]), odt);
             }
-            named_bar_sync(1, 128);
+          }
+          named_bar_sync(1, 128);
+          // row pieces of 8 columns: ncols / 8 per activation row, 16 rows
+          const int per_row = ncols >> 3;
+          for (int pc = row; pc < 16 * per_row; pc += 128) {
+            const int j = pc / per_row, q = pc - j * per_row;
+            const int t = ch * 16 + j;
+            if (t >= ti.nrows) continue;
+            const int col = out_col0 + q * 8;
+            const uint16_t* src = sb + j * ncols + q * 8;
+            uint16_t* dst = reinterpret_cast<uint16_t*>(outp) + (long long)(ti.row0 + t) * p.ld_out + col;
+            if (out_vec && col + 8 <= p.rows_out) {
+              *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+            } else {
+              for (int e = 0; e < 8 && col + e < p.rows_out; ++e) dst[e] = src[e];
+            }
           }
         }
       } else {
