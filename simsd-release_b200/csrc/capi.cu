@@ -4,6 +4,7 @@
 #include <algorithm>
 #include <atomic>
 #include <initializer_list>
+#include <type_traits>
 #include <utility>
 #include <cstdio>
 #include <cmath>
@@ -793,7 +794,7 @@ int simsd_moe_route(const void* x, int64_t ldx, int x_dtype, const void* wr, int
   if (fast) {
     const int sms = sm_count_of(dev) > 0 ? sm_count_of(dev) : 148;
     int tt = T >= 16 * sms ? 16 : T >= 4 * sms ? 8 : 4;
-    auto smem_for = [&](int t) { return (size_t)t * H * 2 + (size_t)2 * t * E * sizeof(float); };
+    auto smem_for = [&](int t) { return (size_t)t * H * 4 + (size_t)2 * t * E * sizeof(float); };
     while (tt > 4 && smem_for(tt) > 200 * 1024) tt >>= 1;
     if (smem_for(tt) <= 200 * 1024) {
       const size_t smem = smem_for(tt);
@@ -802,7 +803,7 @@ int simsd_moe_route(const void* x, int64_t ldx, int x_dtype, const void* wr, int
       const long long bx = cdiv(T, tt);
       int ny = 1;
       if (logits != nullptr && bx * 2 <= sms) ny = (int)std::min<long long>(16, sms / bx);
-      const dim3 grid((unsigned)bx, (unsigned)ny), block(ROUTE_WARPS * 32);
+      const dim3 grid((unsigned)bx, (unsigned)ny), block(ROUTE_FAST_WARPS * 32);
       cudaStream_t st = (cudaStream_t)stream;
       auto go = [&](auto kern) -> int {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess)
@@ -813,16 +814,26 @@ int simsd_moe_route(const void* x, int64_t ldx, int x_dtype, const void* wr, int
         if (cudaFuncSetAttribute(route_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsmem) !=
             cudaSuccess)
           return SIMSD_ERR_LAUNCH;
-        return launch(route_topk_kernel, dim3((unsigned)cdiv(T, ROUTE_WARPS)), block, tsmem, st, a);
+        return launch(route_topk_kernel, dim3((unsigned)cdiv(T, ROUTE_WARPS)), dim3(ROUTE_WARPS * 32), tsmem, st, a);
       };
-      if (w_dtype == SIMSD_F32) {
-        if (tt == 16) return go(route_fast_kernel<16, float>);
-        if (tt == 8) return go(route_fast_kernel<8, float>);
-        return go(route_fast_kernel<4, float>);
-      }
-      if (tt == 16) return go(route_fast_kernel<16, uint16_t>);
-      if (tt == 8) return go(route_fast_kernel<8, uint16_t>);
-      return go(route_fast_kernel<4, uint16_t>);
+      auto by_w = [&](auto xdt) -> int {
+        constexpr int X = decltype(xdt)::value;
+        if (w_dtype == SIMSD_F32) {
+          if (tt == 16) return go(route_fast_kernel<16, X, 2>);
+          if (tt == 8) return go(route_fast_kernel<8, X, 2>);
+          return go(route_fast_kernel<4, X, 2>);
+        }
+        if (w_dtype == SIMSD_F16) {
+          if (tt == 16) return go(route_fast_kernel<16, X, 1>);
+          if (tt == 8) return go(route_fast_kernel<8, X, 1>);
+          return go(route_fast_kernel<4, X, 1>);
+        }
+        if (tt == 16) return go(route_fast_kernel<16, X, 0>);
+        if (tt == 8) return go(route_fast_kernel<8, X, 0>);
+        return go(route_fast_kernel<4, X, 0>);
+      };
+      if (x_dtype == SIMSD_F16) return by_w(std::integral_constant<int, 1>{});
+      return by_w(std::integral_constant<int, 0>{});
     }
   }
   const int smem = 2 * ROUTE_TOK * E * (int)sizeof(float);

@@ -108,7 +108,8 @@ __device__ __forceinline__ void load8(const void* base, long long idx, int dtype
 __device__ __forceinline__ void route_topk(const RouteArgs& p, const float* s_score, float* s_choice, int t0,
                                            int ntok) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int t = warp; t < ntok; t += ROUTE_WARPS) {
+  const int nwarps = blockDim.x >> 5;
+  for (int t = warp; t < ntok; t += nwarps) {
     const float* ch = s_choice + t * p.E;
     float wsel[32];
     int isel[32];
@@ -225,116 +226,159 @@ __global__ void __launch_bounds__(ROUTE_WARPS * 32) route_kernel(const RouteArgs
 }
 
 // Fast router for 16-bit activations with H % 8 == 0 and 16-byte aligned rows.
-// A CTA stages TT token rows in shared memory; each warp pass computes the
-// TT x (32/TT) logits of TT tokens and 32/TT experts with the same per-lane
-// chunk order as route_kernel, then a reduce-scatter butterfly leaves logit q of
-// the pass in lane q.  Its pairing tree is the one of the xor butterfly
-// (v_l + v_{l^m} for m = 16, 8, 4, 2, 1), so the logits are bit-identical to
-// route_kernel's and to the oracle's.  TT adapts to T so small batches still
-// spread over many SMs.
-template <int TT, typename WT>
-__global__ void __launch_bounds__(ROUTE_WARPS * 32) route_fast_kernel(const RouteArgs p) {
+// A CTA of ROUTE_FAST_WARPS warps stages TT token rows in shared memory as
+// fp32, four tokens to a 16-byte vector: xs[(i * TT/4 + q) * nchunks + c]
+// holds element 8c + i of tokens 4q .. 4q+3, so the lanes of a warp
+// (consecutive chunks c) read consecutive vectors and the inner loop converts
+// no activations.  Each warp pass computes the TT x (32/TT) logits of TT
+// tokens and 32/TT experts with the same per-lane chunk order as route_kernel;
+// the fp32 fmas of a token pair run as one packed __ffma2_rn, which rounds
+// each half exactly like __fmaf_rn, so every accumulator sees the same
+// sequence of correctly rounded fmas.  A reduce-scatter butterfly then leaves
+// logit q of the pass in lane q; its pairing tree is the one of the xor
+// butterfly (v_l + v_{l^m} for m = 16, 8, 4, 2, 1), so the logits are
+// bit-identical to route_kernel's and to the oracle's.  The activation and
+// weight types are template parameters (XDT: 0 bf16, 1 fp16; WDT: 0 bf16,
+// 1 fp16, 2 fp32) so the loop carries no per-element type dispatch.  The
+// weight chunks are fetched one step ahead, across a warp's passes too, and
+// each block walks its experts from a different starting group so the blocks
+// do not all read the same router rows at once.  TT adapts to T so small
+// batches still spread over many SMs.
+constexpr int ROUTE_FAST_WARPS = 16;
+
+template <int WDT>
+__device__ __forceinline__ float route_w_elem(const uint4 (&r)[WDT == 2 ? 2 : 1], int i) {
+  if constexpr (WDT == 2) {
+    const uint4 u = r[i >> 2];
+    const uint32_t b = (i & 3) == 0 ? u.x : (i & 3) == 1 ? u.y : (i & 3) == 2 ? u.z : u.w;
+    return __uint_as_float(b);
+  } else {
+    const uint4 u = r[0];
+    const int h = i >> 1;
+    const uint32_t b = h == 0 ? u.x : h == 1 ? u.y : h == 2 ? u.z : u.w;
+    if constexpr (WDT == 0) return __uint_as_float((i & 1) ? (b & 0xffff0000u) : (b << 16));
+    else return __half2float(__ushort_as_half((unsigned short)((i & 1) ? (b >> 16) : (b & 0xffffu))));
+  }
+}
+
+template <int TT, int XDT, int WDT>
+__global__ void __launch_bounds__(ROUTE_FAST_WARPS * 32) route_fast_kernel(const RouteArgs p) {
   griddep_launch_dependents();
   griddep_wait();
   constexpr int EE = 32 / TT;
+  constexpr int TQ = TT / 4;                       // 4-token vectors
   extern __shared__ __align__(16) unsigned char rsh[];
-  uint16_t* xs = reinterpret_cast<uint16_t*>(rsh);                       // [TT][H]
-  float* s_score = reinterpret_cast<float*>(rsh + (size_t)TT * p.H * 2);  // [TT][E]
+  float4* xs = reinterpret_cast<float4*>(rsh);                            // [8][TQ][nchunks]
+  float* s_score = reinterpret_cast<float*>(rsh + (size_t)TT * p.H * 4);  // [TT][E]
   float* s_choice = s_score + TT * p.E;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * TT;
   const int ntok = min(TT, p.T - t0);
-  const int H = p.H, E = p.E;
-  const int vec_per_row = H / 8;
+  const int E = p.E;
+  const int nchunks = p.H / 8;
 
-  // stage the token rows (16-byte vectors); rows past T are zero
-  for (int i = threadIdx.x; i < TT * vec_per_row; i += blockDim.x) {
-    const int t = i / vec_per_row, c = i - t * vec_per_row;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (t < ntok)
-      v = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.x) + (long long)(t0 + t) * p.ldx + c * 8);
-    reinterpret_cast<uint4*>(xs)[i] = v;
+  // stage the token rows as fp32 (rows past T are zero)
+  {
+    float* xf = reinterpret_cast<float*>(xs);
+    for (int idx = threadIdx.x; idx < TT * nchunks; idx += blockDim.x) {
+      const int t = idx / nchunks, c = idx - t * nchunks;
+      uint4 u = make_uint4(0, 0, 0, 0);
+      if (t < ntok)
+        u = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.x) + (long long)(t0 + t) * p.ldx + c * 8);
+      const uint32_t x4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        float lo, hi;
+        if constexpr (XDT == 0) {
+          lo = __uint_as_float(x4[h] << 16);
+          hi = __uint_as_float(x4[h] & 0xffff0000u);
+        } else {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&x4[h]));
+          lo = f.x;
+          hi = f.y;
+        }
+        xf[(((2 * h) * TQ + (t >> 2)) * nchunks + c) * 4 + (t & 3)] = lo;
+        xf[(((2 * h + 1) * TQ + (t >> 2)) * nchunks + c) * 4 + (t & 3)] = hi;
+      }
+    }
   }
   __syncthreads();
 
-  const int nchunks = vec_per_row;
   // experts of this block: all of them, or (grid.y > 1) a slice whose logits go
   // to p.logits for route_topk_kernel
   const int per = gridDim.y > 1 ? ((E + gridDim.y - 1) / gridDim.y + EE - 1) / EE * EE : E;
   const int ebeg = blockIdx.y * per, eend = min(E, ebeg + per);
-  for (int e0 = ebeg + warp * EE; e0 < eend; e0 += ROUTE_WARPS * EE) {
+  constexpr int WV = WDT == 2 ? 2 : 1;             // uint4 per 8-element chunk
+  // (fp32 weights of eight experts would not leave registers for a prefetch)
+  constexpr bool PREFETCH = !(WDT == 2 && EE > 4);
+  uint4 wraw[EE][WV], wnext[EE][WV];
+  auto load_w = [&](int e0, int c, uint4 (&dst)[EE][WV]) {
+#pragma unroll
+    for (int j = 0; j < EE; ++j) {
+      const int e = e0 + j;
+#pragma unroll
+      for (int q = 0; q < WV; ++q) {
+        if (e < eend && c < nchunks)
+          dst[j][q] = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(p.w) +
+                                                      ((long long)e * p.ldw + c * 8) * (WDT == 2 ? 4 : 2) + q * 16);
+        else
+          dst[j][q] = make_uint4(0, 0, 0, 0);
+      }
+    }
+  };
+  // The block's experts form NG groups of EE; warp w takes groups w, w + NW,
+  // ... rotated by a per-block offset.  Which warp computes a logit does not
+  // change its arithmetic.
+  const int NG = (eend - ebeg + EE - 1) / EE;
+  const int rot = NG > 0 ? (int)((blockIdx.x * 7u) % (unsigned)NG) : 0;
+  auto group_e0 = [&](int gi) { return ebeg + ((gi + rot) % NG) * EE; };
+  if (PREFETCH && warp < NG) load_w(group_e0(warp), lane, wraw);
+  for (int gi = warp; gi < NG; gi += ROUTE_FAST_WARPS) {
+    const int e0 = group_e0(gi);
+    float2 acc[EE][TT / 2];                          // (token 2u, token 2u+1) of expert e0 + j
+#pragma unroll
+    for (int j = 0; j < EE; ++j)
+#pragma unroll
+      for (int u = 0; u < TT / 2; ++u) acc[j][u] = make_float2(0.0f, 0.0f);
+    for (int c = lane; c < nchunks; c += 32) {
+      if (PREFETCH) {
+        // the next chunk of this pass, or the first chunk of the next pass
+        if (c + 32 < nchunks) load_w(e0, c + 32, wnext);
+        else if (gi + ROUTE_FAST_WARPS < NG) load_w(group_e0(gi + ROUTE_FAST_WARPS), lane, wnext);
+      } else {
+        load_w(e0, c, wraw);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float2 w2[EE];
+#pragma unroll
+        for (int j = 0; j < EE; ++j) {
+          const float w = route_w_elem<WDT>(wraw[j], i);
+          w2[j] = make_float2(w, w);
+        }
+#pragma unroll
+        for (int q = 0; q < TQ; ++q) {
+          const float4 xq = xs[(i * TQ + q) * nchunks + c];
+#pragma unroll
+          for (int j = 0; j < EE; ++j) {
+            acc[j][2 * q] = __ffma2_rn(make_float2(xq.x, xq.y), w2[j], acc[j][2 * q]);
+            acc[j][2 * q + 1] = __ffma2_rn(make_float2(xq.z, xq.w), w2[j], acc[j][2 * q + 1]);
+          }
+        }
+      }
+      if (PREFETCH) {
+#pragma unroll
+        for (int j = 0; j < EE; ++j)
+#pragma unroll
+          for (int q = 0; q < WV; ++q) wraw[j][q] = wnext[j][q];
+      }
+    }
+    // v[t * EE + j] = lane partial of token t, expert e0 + j
     float v[32];
 #pragma unroll
-    for (int q = 0; q < 32; ++q) v[q] = 0.0f;
-    // weight chunks are prefetched one iteration ahead (raw 16-byte vectors)
-    constexpr int WV = sizeof(WT) == 4 ? 2 : 1;        // uint4 per 8-element chunk
-    uint4 wraw[EE][WV], wnext[EE][WV];
-    auto load_w = [&](int c, uint4 (&dst)[EE][WV]) {
+    for (int t = 0; t < TT; ++t)
 #pragma unroll
-      for (int j = 0; j < EE; ++j) {
-        const int e = e0 + j;
-#pragma unroll
-        for (int q = 0; q < WV; ++q) {
-          if (e < eend && c < nchunks)
-            dst[j][q] = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(p.w) +
-                                                        ((long long)e * p.ldw + c * 8) * sizeof(WT) + q * 16);
-          else
-            dst[j][q] = make_uint4(0, 0, 0, 0);
-        }
-      }
-    };
-    load_w(lane, wraw);
-    for (int c = lane; c < nchunks; c += 32) {
-      load_w(c + 32, wnext);
-      float wv[EE][8];
-#pragma unroll
-      for (int j = 0; j < EE; ++j) {
-        if constexpr (sizeof(WT) == 4) {
-          wv[j][0] = __uint_as_float(wraw[j][0].x); wv[j][1] = __uint_as_float(wraw[j][0].y);
-          wv[j][2] = __uint_as_float(wraw[j][0].z); wv[j][3] = __uint_as_float(wraw[j][0].w);
-          wv[j][4] = __uint_as_float(wraw[j][1].x); wv[j][5] = __uint_as_float(wraw[j][1].y);
-          wv[j][6] = __uint_as_float(wraw[j][1].z); wv[j][7] = __uint_as_float(wraw[j][1].w);
-        } else {
-          const uint32_t w4[4] = {wraw[j][0].x, wraw[j][0].y, wraw[j][0].z, wraw[j][0].w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            if (p.w_dtype == 0) {
-              wv[j][2 * i] = __uint_as_float(w4[i] << 16);
-              wv[j][2 * i + 1] = __uint_as_float(w4[i] & 0xffff0000u);
-            } else {
-              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[i]));
-              wv[j][2 * i] = f.x;
-              wv[j][2 * i + 1] = f.y;
-            }
-          }
-        }
-      }
-#pragma unroll
-      for (int t = 0; t < TT; ++t) {
-        const uint4 u = reinterpret_cast<const uint4*>(xs)[t * vec_per_row + c];
-        const uint32_t x4[4] = {u.x, u.y, u.z, u.w};
-        float xv[8];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          if (p.x_dtype == 0) {
-            xv[2 * i] = __uint_as_float(x4[i] << 16);
-            xv[2 * i + 1] = __uint_as_float(x4[i] & 0xffff0000u);
-          } else {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&x4[i]));
-            xv[2 * i] = f.x;
-            xv[2 * i + 1] = f.y;
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-          for (int j = 0; j < EE; ++j) v[t * EE + j] = __fmaf_rn(xv[i], wv[j][i], v[t * EE + j]);
-      }
-#pragma unroll
-      for (int j = 0; j < EE; ++j)
-#pragma unroll
-        for (int q = 0; q < WV; ++q) wraw[j][q] = wnext[j][q];
-    }
+      for (int j = 0; j < EE; ++j) v[t * EE + j] = (t & 1) ? acc[j][t >> 1].y : acc[j][t >> 1].x;
     // reduce-scatter: after the step with offset m, a lane keeps the half of
     // its values whose index bit log2(m) equals its own lane bit
 #pragma unroll

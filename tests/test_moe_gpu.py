@@ -136,6 +136,23 @@ def test_router_bit_exact_vs_oracle(T, H, E, k, bias_std):
     assert np.array_equal(wts.cpu().numpy().view(np.uint32), ow.view(np.uint32))
 
 
+# token-group sizes 4 / 8 / 16 of the fast router (T >= 4 and 16 x 148 SMs pick
+# 8 and 16), 16-bit activations with bf16, fp16 or fp32 router weights
+@pytest.mark.parametrize("T,H,E,k,dtype,wdtype", [
+    (700, 1000, 40, 4, torch.bfloat16, torch.float32),
+    (2400, 512, 24, 2, torch.float16, None),
+    (2400, 256, 36, 3, torch.bfloat16, torch.float32),
+    (40, 520, 72, 6, torch.float16, torch.float32),
+    (3000, 264, 20, 5, torch.bfloat16, None)])
+def test_router_fast_variants_bit_exact(T, H, E, k, dtype, wdtype):
+    x, wr, b = _route_case(T, H, E, 0.2, seed=T + E, dtype=dtype, wdtype=wdtype)
+    ids, wts, lg = moe_route(x, wr, b, k=k, renorm=True, scale=1.5, return_logits=True)
+    oi, ow, ol = O.route(to_np(x), to_np(wr), b.cpu().numpy(), k, True, 1.5)
+    assert np.array_equal(lg.cpu().numpy().view(np.uint32), ol.view(np.uint32))
+    assert np.array_equal(ids.cpu().numpy(), oi)
+    assert np.array_equal(wts.cpu().numpy().view(np.uint32), ow.view(np.uint32))
+
+
 def test_router_fp32_inputs_and_no_renorm():
     x, wr, b = _route_case(20, 512, 48, 0.3, seed=9, dtype=torch.float32)
     ids, wts, lg = moe_route(x, wr, b, k=4, renorm=False, scale=1.0, return_logits=True)
