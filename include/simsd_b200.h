@@ -90,11 +90,13 @@ int simsd_set_launch_flags(int flags);
 int simsd_get_launch_flags(void);
 
 /*
- * Diagnostics (no counterpart in the reference): while `buf` is set, every
- * tensor-core GEMM launch whose grid fits writes 8 %globaltimer stamps (ns) per
- * CTA into buf[cta*8 + i]: entry, set-up done, first TMA issued, first MMA
- * stage ready, last TMA issued, last MMA committed, SM id (not a time), exit.
- * `bytes` >= 64 * grid.  NULL disables.  Not for concurrent use.
+ * Diagnostics (no counterpart in the reference): while `buf` is set, the
+ * tensor-core GEMM launches write 8 %globaltimer stamps (ns) per CTA into
+ * successive records of 64 * grid bytes (the first launch at buf[cta*8 + i],
+ * the next right after it, ...) while the buffer has room: entry, set-up done,
+ * first TMA issued, first MMA stage ready, last TMA issued, last MMA
+ * committed, SM id (not a time), exit.  Setting the buffer starts again at
+ * its head.  NULL disables.  Not for concurrent use.
  */
 int simsd_debug_set_trace(void* buf, size_t bytes);
 

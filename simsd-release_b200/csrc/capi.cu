@@ -27,6 +27,18 @@ int g_sm_count[kMaxDev];
 bool g_smem_attr[kMaxDev][40];
 unsigned long long* g_trace = nullptr;
 size_t g_trace_bytes = 0;
+size_t g_trace_used = 0;   // bytes of the trace buffer taken by earlier launches
+
+// The trace record of the next GEMM launch of `ctas` CTAs: the next free
+// 64 * ctas bytes of the buffer, or nullptr once it is full (or unset).
+unsigned long long* trace_slot(long long ctas) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  const size_t need = (size_t)ctas * 64;
+  if (g_trace == nullptr || g_trace_used + need > g_trace_bytes) return nullptr;
+  unsigned long long* t = g_trace + g_trace_used / 8;
+  g_trace_used += need;
+  return t;
+}
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 std::atomic<int> g_launch_flags{0};
@@ -177,7 +189,7 @@ int launch_tc_b(const TcGemmArgs& a, int grid, cudaStream_t s, int dev) {
   TcGemmArgs args = a;
   args.pdl = pdl_on() ? 1 : 0;
   args.prefetch = prefetch_stages();
-  args.trace = (g_trace && g_trace_bytes >= (size_t)grid * 64) ? g_trace : nullptr;
+  args.trace = trace_slot(grid);
   return launch(tc_gemm_kernel<BMAX, KS, RING>, dim3(grid), dim3(TC_THREADS), smem, s, args);
 }
 
@@ -370,7 +382,7 @@ int launch_cluster_b(const TcClusterArgs& a, int S, int C, cudaStream_t s, int d
   args.pdl = pdl_on() ? 1 : 0;
   args.prefetch = prefetch_stages();
   args.l2_ahead = l2_ahead_stages();
-  args.trace = (g_trace && g_trace_bytes >= (size_t)C * S * 64) ? g_trace : nullptr;
+  args.trace = trace_slot((long long)C * S);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(C * S));
   cfg.blockDim = dim3(TC_THREADS);
@@ -550,6 +562,7 @@ int simsd_debug_set_trace(void* buf, size_t bytes) {
   std::lock_guard<std::mutex> lk(g_mu);
   g_trace = reinterpret_cast<unsigned long long*>(buf);
   g_trace_bytes = buf ? bytes : 0;
+  g_trace_used = 0;
   return SIMSD_OK;
 }
 

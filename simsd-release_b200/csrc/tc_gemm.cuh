@@ -103,32 +103,45 @@ struct TcConfig {
 
 struct TileInfo {
   int group, rtile, row0, nrows;
+  bool reread;   // a later row chunk of this tile reads the same weight tile
 };
 
 // Tile j -> (group, output-column tile, first B row, B rows).  Tiles are
-// ordered (group, row chunk, column tile) so a CTA's consecutive tiles reuse
-// the same activation rows.
+// ordered (group, column tile, row chunk): the row chunks that share a weight
+// tile (a busy expert's rows beyond BMAX, or M > BMAX in single mode) run back
+// to back, mostly on one CTA, so the weight tile streams from HBM once and the
+// later chunks re-read it from L2.  The activation chunks are small and stay
+// L2-resident (evict_last), so walking them per column tile costs no HBM.
 template <int BMAX>
 __device__ __forceinline__ TileInfo decode_tile(int j, const TcGemmArgs& p,
                                                 const int* row_prefix, const int* chunk_prefix) {
   TileInfo ti;
-  const int chunk = j / p.row_tiles;
-  ti.rtile = j - chunk * p.row_tiles;
   if (p.group_counts == nullptr) {
+    const int nch = (p.single_rows + BMAX - 1) / BMAX;
+    ti.rtile = j / nch;
+    const int chunk = j - ti.rtile * nch;
     ti.group = 0;
     ti.row0 = chunk * BMAX;
     ti.nrows = min(BMAX, p.single_rows - ti.row0);
+    ti.reread = chunk + 1 < nch;
   } else {
-    // largest g with chunk_prefix[g] <= chunk (groups with zero chunks are skipped)
+    // group g holds tiles [chunk_prefix[g], chunk_prefix[g+1]) x row_tiles, so
+    // g is the largest with chunk_prefix[g] <= j / row_tiles (groups with zero
+    // chunks are skipped)
+    const int pc = j / p.row_tiles;
     int lo = 0, hi = p.num_groups - 1;
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
-      if (chunk_prefix[mid] <= chunk) lo = mid; else hi = mid - 1;
+      if (chunk_prefix[mid] <= pc) lo = mid; else hi = mid - 1;
     }
     ti.group = lo;
-    const int lc = chunk - chunk_prefix[lo];
+    const int nch = chunk_prefix[lo + 1] - chunk_prefix[lo];
+    const int local = j - chunk_prefix[lo] * p.row_tiles;
+    ti.rtile = local / nch;
+    const int lc = local - ti.rtile * nch;
     ti.row0 = row_prefix[lo] + lc * BMAX;
     ti.nrows = min(BMAX, row_prefix[lo + 1] - ti.row0);
+    ti.reread = lc + 1 < nch;
   }
   return ti;
 }
@@ -379,7 +392,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
   if (warp == 4) {
     // ================= TMA producer
     if (lane == 0) {
-      const uint64_t pol_w = policy_evict_first();
+      // weights stream through L2 evict-first, except for a tile that a later
+      // row chunk reads again (normal priority keeps it for that re-read)
+      const uint64_t pol_w_last = policy_evict_first();
+      const uint64_t pol_w_keep = policy_evict_normal();
       const uint64_t pol_x = policy_evict_last();
       int stage = 0;
       uint32_t phase = 0;
@@ -409,7 +425,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         const int kb0 = it - tile * kb;
         const int kb1 = min(kb, it_end - tile * kb);
         const TileInfo ti = decode_tile<BMAX>(tile, p, row_prefix, chunk_prefix);
-        const int nb = (ti.nrows + TC_BOX_ROWS - 1) / TC_BOX_ROWS;
+        const uint64_t pol_w = ti.reread ? pol_w_keep : pol_w_last;
         for (int k = kb0; k < kb1; k += KS) {
           const int na = min(KS, kb1 - k);
           if (!dep_ready && npend >= min(STAGES, p.prefetch)) flush_pending();
