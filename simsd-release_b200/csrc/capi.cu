@@ -291,6 +291,8 @@ bool any_split_tile(long long tiles, long long kb, long long grid) {
 }
 
 // ---------------------------------------------------------------- thin linear plan
+constexpr long long TC_MIN_ATOMS_PER_CTA = 8;
+
 struct ThinPlan {
   int bmax, row_tiles, kb, grid;
   long long tiles, iters;
@@ -305,8 +307,14 @@ ThinPlan plan_thin(int M, int N, int K, int epilogue, int split, int sms) {
   p.tiles = cdiv(M, p.bmax) * p.row_tiles;
   p.iters = p.tiles * p.kb;
   long long g;
-  if (split > 0) g = std::min<long long>(p.tiles * split, p.iters);
-  else g = std::min<long long>(sms > 0 ? sms : 148, p.iters);
+  if (split > 0) {
+    g = std::min<long long>(p.tiles * split, p.iters);
+  } else {
+    // at least TC_MIN_ATOMS_PER_CTA K atoms per CTA: a CTA's set-up and first
+    // ring fill cost a few microseconds, and every split tile adds fp32
+    // partials and a reduction, so a small GEMM uses fewer CTAs instead
+    g = std::min<long long>(sms > 0 ? sms : 148, p.iters / TC_MIN_ATOMS_PER_CTA);
+  }
   g = std::max<long long>(1, std::min<long long>(g, TC_MAX_GRID));
   p.grid = (int)g;
   p.ws_bytes = WS_COUNTER_BYTES + align256((size_t)2 * p.grid * p.bmax * 128 * sizeof(float));
@@ -810,12 +818,19 @@ int simsd_moe_route(const void* x, int64_t ldx, int x_dtype, const void* wr, int
     auto smem_for = [&](int t) { return (size_t)t * H * 4 + (size_t)2 * t * E * sizeof(float); };
     while (tt > 4 && smem_for(tt) > 200 * 1024) tt >>= 1;
     if (smem_for(tt) <= 200 * 1024) {
-      const size_t smem = smem_for(tt);
+      size_t smem = smem_for(tt);
       // few token blocks: split the experts over blocks as well (logits to
       // `logits`, then route_topk_kernel) so the router uses more SMs
       const long long bx = cdiv(T, tt);
       int ny = 1;
       if (logits != nullptr && bx * 2 <= sms) ny = (int)std::min<long long>(16, sms / bx);
+      // with the experts split, a block's router rows are staged in shared
+      // memory when they fit (4-token blocks only)
+      const int ee = 32 / tt;
+      const long long per = ((E + ny - 1) / ny + ee - 1) / ee * ee;
+      const size_t wbytes = (size_t)per * H * (w_dtype == SIMSD_F32 ? 4 : 2);
+      const bool wsm = ny > 1 && tt == 4 && smem + wbytes <= 200 * 1024;
+      if (wsm) smem += wbytes;
       const dim3 grid((unsigned)bx, (unsigned)ny), block(ROUTE_FAST_WARPS * 32);
       cudaStream_t st = (cudaStream_t)stream;
       auto go = [&](auto kern) -> int {
@@ -832,18 +847,18 @@ int simsd_moe_route(const void* x, int64_t ldx, int x_dtype, const void* wr, int
       auto by_w = [&](auto xdt) -> int {
         constexpr int X = decltype(xdt)::value;
         if (w_dtype == SIMSD_F32) {
-          if (tt == 16) return go(route_fast_kernel<16, X, 2>);
-          if (tt == 8) return go(route_fast_kernel<8, X, 2>);
-          return go(route_fast_kernel<4, X, 2>);
+          if (tt == 16) return go(route_fast_kernel<16, X, 2, false>);
+          if (tt == 8) return go(route_fast_kernel<8, X, 2, false>);
+          return wsm ? go(route_fast_kernel<4, X, 2, true>) : go(route_fast_kernel<4, X, 2, false>);
         }
         if (w_dtype == SIMSD_F16) {
-          if (tt == 16) return go(route_fast_kernel<16, X, 1>);
-          if (tt == 8) return go(route_fast_kernel<8, X, 1>);
-          return go(route_fast_kernel<4, X, 1>);
+          if (tt == 16) return go(route_fast_kernel<16, X, 1, false>);
+          if (tt == 8) return go(route_fast_kernel<8, X, 1, false>);
+          return wsm ? go(route_fast_kernel<4, X, 1, true>) : go(route_fast_kernel<4, X, 1, false>);
         }
-        if (tt == 16) return go(route_fast_kernel<16, X, 0>);
-        if (tt == 8) return go(route_fast_kernel<8, X, 0>);
-        return go(route_fast_kernel<4, X, 0>);
+        if (tt == 16) return go(route_fast_kernel<16, X, 0, false>);
+        if (tt == 8) return go(route_fast_kernel<8, X, 0, false>);
+        return wsm ? go(route_fast_kernel<4, X, 0, true>) : go(route_fast_kernel<4, X, 0, false>);
       };
       if (x_dtype == SIMSD_F16) return by_w(std::integral_constant<int, 1>{});
       return by_w(std::integral_constant<int, 0>{});

@@ -104,25 +104,36 @@ __device__ __forceinline__ void load8(const void* base, long long idx, int dtype
   for (int i = 0; i < 8; ++i) v[i] = (i < n_valid) ? load_f(base, idx + i, dtype) : 0.0f;
 }
 
-// top-k per token, one warp per token; lane l owns experts l, l+32, ...
-__device__ __forceinline__ void route_topk(const RouteArgs& p, const float* s_score, float* s_choice, int t0,
-                                           int ntok) {
+// top-k per token, one warp per token; lane l owns experts l, l+32, ... (NC
+// per lane, held in registers).  Each round takes the largest remaining choice
+// (ties to the lower expert id, NaN below every number); lane j keeps round
+// j's pick.  The weights are then normalised with the sum taken in round
+// order, (((w_0 + w_1) + w_2) + ...) + 1e-20, and lane j writes output j.
+template <int NC>
+__device__ __forceinline__ void route_topk_nc(const RouteArgs& p, const float* s_score, const float* s_choice,
+                                              int t0, int ntok) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwarps = blockDim.x >> 5;
   for (int t = warp; t < ntok; t += nwarps) {
     const float* ch = s_choice + t * p.E;
-    float wsel[32];
-    int isel[32];
+    float cv[NC];
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int e = lane + 32 * i;
+      float v = e < p.E ? ch[e] : 0.0f;
+      if (v != v) v = -__int_as_float(0x7f800000);
+      cv[i] = v;
+    }
     unsigned taken = 0u;
+    int my_id = -1;
+    float my_w = 0.0f;
     for (int j = 0; j < p.k; ++j) {
       float bb = 0.0f;
       int be = -1;
-      int i = 0;
-      for (int e = lane; e < p.E; e += 32, ++i) {
-        if ((taken >> i) & 1u) continue;
-        float v = ch[e];
-        if (v != v) v = -__int_as_float(0x7f800000);
-        if (be < 0 || v > bb) { bb = v; be = e; }
+#pragma unroll
+      for (int i = 0; i < NC; ++i) {
+        const int e = lane + 32 * i;
+        if (e < p.E && !((taken >> i) & 1u) && (be < 0 || cv[i] > bb)) { bb = cv[i]; be = e; }
       }
 #pragma unroll
       for (int m = 16; m > 0; m >>= 1) {
@@ -132,27 +143,33 @@ __device__ __forceinline__ void route_topk(const RouteArgs& p, const float* s_sc
         if (take) { bb = ob; be = oe; }
       }
       if (be >= 0 && (be & 31) == lane) taken |= 1u << (be >> 5);
-      isel[j] = be;
-      wsel[j] = (be >= 0) ? s_score[t * p.E + be] : 0.0f;
+      if (lane == j) {
+        my_id = be;
+        my_w = (be >= 0) ? s_score[t * p.E + be] : 0.0f;
+      }
     }
-    if (lane == 0) {
-      const bool norm = p.renorm && p.k > 1;
-      float denom = 1.0f;
-      if (norm) {
-        float sum = wsel[0];
-        for (int j = 1; j < p.k; ++j) sum = __fadd_rn(sum, wsel[j]);
-        denom = __fadd_rn(sum, 1e-20f);
-      }
-      for (int j = 0; j < p.k; ++j) {
-        float wj = wsel[j];
-        if (norm) wj = __fdiv_rn(wj, denom);
-        wj = __fmul_rn(wj, p.scale);
-        p.topk_ids[(long long)(t0 + t) * p.k + j] = isel[j];
-        p.topk_weight[(long long)(t0 + t) * p.k + j] = wj;
-      }
+    const bool norm = p.renorm && p.k > 1;
+    float denom = 1.0f;
+    if (norm) {
+      float sum = __shfl_sync(0xffffffffu, my_w, 0);
+      for (int j = 1; j < p.k; ++j) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, my_w, j));
+      denom = __fadd_rn(sum, 1e-20f);
+    }
+    if (lane < p.k) {
+      float wj = my_w;
+      if (norm) wj = __fdiv_rn(wj, denom);
+      wj = __fmul_rn(wj, p.scale);
+      p.topk_ids[(long long)(t0 + t) * p.k + lane] = my_id;
+      p.topk_weight[(long long)(t0 + t) * p.k + lane] = wj;
     }
     __syncwarp();
   }
+}
+
+__device__ __forceinline__ void route_topk(const RouteArgs& p, const float* s_score, const float* s_choice, int t0,
+                                           int ntok) {
+  if (p.E <= 256) route_topk_nc<8>(p, s_score, s_choice, t0, ntok);
+  else route_topk_nc<32>(p, s_score, s_choice, t0, ntok);
 }
 
 __global__ void __launch_bounds__(ROUTE_WARPS * 32) route_kernel(const RouteArgs p) {
@@ -261,7 +278,11 @@ __device__ __forceinline__ float route_w_elem(const uint4 (&r)[WDT == 2 ? 2 : 1]
   }
 }
 
-template <int TT, int XDT, int WDT>
+// WSM: the block's router rows are first copied into shared memory with all
+// loads in flight at once (the expert-split launch for few tokens, where a
+// warp's chain of dependent per-chunk weight loads would otherwise set the
+// time); the arithmetic is unchanged.
+template <int TT, int XDT, int WDT, bool WSM>
 __global__ void __launch_bounds__(ROUTE_FAST_WARPS * 32) route_fast_kernel(const RouteArgs p) {
   griddep_launch_dependents();
   griddep_wait();
@@ -271,6 +292,7 @@ __global__ void __launch_bounds__(ROUTE_FAST_WARPS * 32) route_fast_kernel(const
   float4* xs = reinterpret_cast<float4*>(rsh);                            // [8][TQ][nchunks]
   float* s_score = reinterpret_cast<float*>(rsh + (size_t)TT * p.H * 4);  // [TT][E]
   float* s_choice = s_score + TT * p.E;
+  uint4* wsm = reinterpret_cast<uint4*>(s_choice + TT * p.E);             // WSM: [per][nchunks][WV]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * TT;
   const int ntok = min(TT, p.T - t0);
@@ -309,8 +331,34 @@ __global__ void __launch_bounds__(ROUTE_FAST_WARPS * 32) route_fast_kernel(const
   const int per = gridDim.y > 1 ? ((E + gridDim.y - 1) / gridDim.y + EE - 1) / EE * EE : E;
   const int ebeg = blockIdx.y * per, eend = min(E, ebeg + per);
   constexpr int WV = WDT == 2 ? 2 : 1;             // uint4 per 8-element chunk
-  // (fp32 weights of eight experts would not leave registers for a prefetch)
-  constexpr bool PREFETCH = !(WDT == 2 && EE > 4);
+  auto gload_w = [&](int e, int c, int q) {
+    return *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(p.w) +
+                                           ((long long)e * p.ldw + c * 8) * (WDT == 2 ? 4 : 2) + q * 16);
+  };
+  if constexpr (WSM) {
+    const int total = (eend - ebeg) * nchunks * WV;
+    constexpr int UNR = 8;
+    for (int base = threadIdx.x; base < total; base += UNR * blockDim.x) {
+      uint4 tmp[UNR];
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const int idx = base + u * blockDim.x;
+        if (idx < total) {
+          const int el = idx / (nchunks * WV), r = idx - el * (nchunks * WV);
+          tmp[u] = gload_w(ebeg + el, r / WV, r % WV);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const int idx = base + u * blockDim.x;
+        if (idx < total) wsm[idx] = tmp[u];
+      }
+    }
+    __syncthreads();
+  }
+  // (fp32 weights of eight experts would not leave registers for a prefetch;
+  // staged weights need none)
+  constexpr bool PREFETCH = !WSM && !(WDT == 2 && EE > 4);
   uint4 wraw[EE][WV], wnext[EE][WV];
   auto load_w = [&](int e0, int c, uint4 (&dst)[EE][WV]) {
 #pragma unroll
@@ -318,11 +366,12 @@ __global__ void __launch_bounds__(ROUTE_FAST_WARPS * 32) route_fast_kernel(const
       const int e = e0 + j;
 #pragma unroll
       for (int q = 0; q < WV; ++q) {
-        if (e < eend && c < nchunks)
-          dst[j][q] = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(p.w) +
-                                                      ((long long)e * p.ldw + c * 8) * (WDT == 2 ? 4 : 2) + q * 16);
-        else
+        if (e < eend && c < nchunks) {
+          if constexpr (WSM) dst[j][q] = wsm[((e - ebeg) * nchunks + c) * WV + q];
+          else dst[j][q] = gload_w(e, c, q);
+        } else {
           dst[j][q] = make_uint4(0, 0, 0, 0);
+        }
       }
     }
   };
@@ -419,11 +468,28 @@ __global__ void __launch_bounds__(ROUTE_WARPS * 32) route_topk_kernel(const Rout
   float* s_choice = tsh + ROUTE_WARPS * p.E;   // [ROUTE_WARPS][E]
   const int t0 = blockIdx.x * ROUTE_WARPS;
   const int ntok = min(ROUTE_WARPS, p.T - t0);
-  for (int i = threadIdx.x; i < ntok * p.E; i += blockDim.x) {
-    const int t = i / p.E, e = i - t * p.E;
-    const float sc = sigmoid_fixed(p.logits[(long long)(t0 + t) * p.E + e]);
-    s_score[i] = sc;
-    s_choice[i] = p.bias ? __fadd_rn(sc, p.bias[e]) : sc;
+  // the block's logits are contiguous: load UNR of them per thread before
+  // any arithmetic, so the loads are in flight together
+  const int n = ntok * p.E;
+  const float* lg = p.logits + (long long)t0 * p.E;
+  constexpr int UNR = 8;
+  for (int base = threadIdx.x; base < n; base += UNR * blockDim.x) {
+    float v[UNR], b[UNR];
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) {
+      const int i = base + u * blockDim.x;
+      v[u] = i < n ? lg[i] : 0.0f;
+      b[u] = (i < n && p.bias) ? p.bias[i % p.E] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) {
+      const int i = base + u * blockDim.x;
+      if (i < n) {
+        const float sc = sigmoid_fixed(v[u]);
+        s_score[i] = sc;
+        s_choice[i] = p.bias ? __fadd_rn(sc, b[u]) : sc;
+      }
+    }
   }
   __syncthreads();
   route_topk(p, s_score, s_choice, t0, ntok);
