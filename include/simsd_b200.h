@@ -100,6 +100,14 @@ int simsd_get_launch_flags(void);
  */
 int simsd_debug_set_trace(void* buf, size_t bytes);
 
+/*
+ * Diagnostics: the cluster plan simsd_thin_linear uses for an M <= 64 thin
+ * linear (S CTAs per cluster, C clusters; S = 0 when no plan fits) and, when
+ * `max_clusters_by_s` is not NULL, the clusters of size 1..8 that fit the
+ * device at once (8 ints).
+ */
+int simsd_debug_cluster_plan(int M, int N, int K, int silu, int* S, int* C, int* max_clusters_by_s);
+
 /* Number of SMs of the current device (0 if there is none). */
 int simsd_device_sm_count(void);
 

@@ -429,11 +429,27 @@ int launch_cluster(int bmax, const TcClusterArgs& a, int S, int C, cudaStream_t 
 struct ClusterPlan {
   int S = 0, C = 0;
 };
+// SIMSD_TC_MAX_CTAS caps the CTAs of a cluster launch (measurement knob;
+// default: no cap beyond what fits)
+int cluster_cta_cap() {
+  static const int v = [] {
+    const char* e = getenv("SIMSD_TC_MAX_CTAS");
+    const int n = e ? atoi(e) : 0;
+    return n > 0 ? n : 1 << 30;
+  }();
+  return v;
+}
+
+// Cluster plan: tile c, c + C, ... to cluster c, the K blocks of each split
+// over the S ranks; the S with the fewest K blocks per CTA (then the most
+// CTAs).  Whole tiles per cluster leave the SMs that no cluster fills free for
+// the next launch's CTAs, which fetch their first weight stages there while
+// this launch drains (programmatic dependent launch).
 ClusterPlan plan_cluster(int bmax, long long tiles, int kb, int dev) {
   ClusterPlan best;
   long long best_cost = -1, best_ctas = 0;
   for (int S = 1; S <= TC_CL_MAX && S <= kb; ++S) {
-    const long long cmax = max_clusters(bmax, S, dev);
+    const long long cmax = std::min<long long>(max_clusters(bmax, S, dev), cluster_cta_cap() / S);
     if (cmax <= 0) continue;
     const long long c0 = std::min(cmax, tiles);
     const long long w = cdiv(tiles, c0);
@@ -571,6 +587,19 @@ int simsd_debug_set_trace(void* buf, size_t bytes) {
   g_trace = reinterpret_cast<unsigned long long*>(buf);
   g_trace_bytes = buf ? bytes : 0;
   g_trace_used = 0;
+  return SIMSD_OK;
+}
+
+int simsd_debug_cluster_plan(int M, int N, int K, int silu, int* S, int* C, int* max_clusters_by_s) {
+  const int dev = current_device();
+  if (dev < 0) return SIMSD_ERR_DEVICE;
+  if (M < 1 || M > 64 || N < 1 || K < 1 || !S || !C) return SIMSD_ERR_SHAPE;
+  const int bmax = pick_bmax_rows(M);
+  const ClusterPlan cp = plan_cluster(bmax, silu ? cdiv(N, 64) : cdiv(N, 128), (int)cdiv(K, 64), dev);
+  *S = cp.S;
+  *C = cp.C;
+  if (max_clusters_by_s)
+    for (int s2 = 1; s2 <= TC_CL_MAX; ++s2) max_clusters_by_s[s2 - 1] = max_clusters(bmax, s2, dev);
   return SIMSD_OK;
 }
 

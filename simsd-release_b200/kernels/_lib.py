@@ -49,6 +49,7 @@ SIGNATURES: dict[str, tuple] = {
     "simsd_device_sm_count": (_I, []),
     "simsd_set_launch_flags": (_I, [_I]),
     "simsd_get_launch_flags": (_I, []),
+    "simsd_debug_cluster_plan": (_I, [_I, _I, _I, _I, _P, _P, _P]),
     "simsd_debug_set_trace": (_I, [_P, _S]),
     "simsd_workspace_header_bytes": (_S, []),
     "simsd_workspace_init": (_I, [_P, _S, _P]),
