@@ -632,14 +632,15 @@ def verify_bench(dev, steps: int) -> dict:
                        "2048-token KV prefix of uniform random ids; CUDA-graph replay",
            "unit": "tok/s", "bytes_per_forward": fwd_bytes}
 
-    def timed(label):
+    def timed(label, fn=None):
+        fn = fn or h.window_logits
         with torch.inference_mode():
             for _ in range(3):
-                h.window_logits()
+                fn()
             torch.cuda.synchronize()
             gr = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gr):
-                out = h.window_logits()
+                out = fn()
             for _ in range(3):
                 gr.replay()
             torch.cuda.synchronize()
@@ -651,20 +652,26 @@ def verify_bench(dev, steps: int) -> dict:
             e1.record()
             torch.cuda.synchronize()
             ms = e0.elapsed_time(e1) / n
-            acc = h.accept(out, drafts)
+            acc = h.accept(out, drafts) if out.ndim == 2 else h.accept_ids(out, drafts)
         del gr
         res[label] = {"ms_per_forward": round(ms, 3), "tok_s": round(K * BL / (ms * 1e-3), 1),
                       "weight_stream_gbs": round(fwd_bytes / ms / 1e6, 1),
                       "accepted": [a[1] for a in acc]}
 
     timed("reference_cublas")
+    # the whole greedy step: forward, lm_head and the argmax of every row
+    timed("reference_cublas_greedy", h.window_argmax_via_logits)
     fused_toggle.apply_to_model(model, True, fuse_gate_up=True)
     fused_toggle.warmup(model, BL, extra_M=(2 * BL * K,))
     timed("ours")
+    timed("ours_greedy_fused_head", h.window_argmax)
     fused_toggle.apply_to_model(model, False)
     res["value"] = res["ours"]["tok_s"]
     res["speedup_vs_cublas"] = round(res["reference_cublas"]["ms_per_forward"] / res["ours"]["ms_per_forward"], 3)
-    res["identical_accepted_tokens"] = res["ours"]["accepted"] == res["reference_cublas"]["accepted"]
+    res["greedy_step_speedup_vs_cublas"] = round(res["reference_cublas_greedy"]["ms_per_forward"]
+                                                 / res["ours_greedy_fused_head"]["ms_per_forward"], 3)
+    res["identical_accepted_tokens"] = (res["ours"]["accepted"] == res["reference_cublas"]["accepted"]
+                                        == res["ours_greedy_fused_head"]["accepted"])
     del h, model
     torch.cuda.empty_cache()
     return res

@@ -272,6 +272,21 @@ int simsd_thin_linear_allgather(const void* x, int64_t ldx_m, int64_t ldx_k, con
                                 void* const* peer_signal, void* workspace, size_t workspace_bytes,
                                 void* stream);
 
+/*
+ * Greedy verify head: idx[m] = argmax_n round(x[m] . w[n] (+ bias[n])), the
+ * rounding to `dtype` (the logits tensor the reference's lm_head returns), ties
+ * to the lowest n (torch.argmax) — without writing the [M, N] logits.  Replaces
+ * the reference's `lm_head(hidden)` followed by softmax / argmax on the accepted
+ * rows (speculative_decoding/cache_aware.py:1193-1196, mrs.py:138): softmax is
+ * monotonic, so its argmax is the logits' argmax.  M <= 64, K >= 64, bf16/fp16
+ * with TMA-describable layouts, else SIMSD_ERR_UNSUPPORTED (use
+ * simsd_thin_linear and an argmax).  Uses the workspace header's argmax slots
+ * (zero between calls: after a device error, re-initialise the workspace).
+ */
+int simsd_thin_linear_argmax(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w, int64_t ldw_n,
+                             int64_t ldw_k, const void* bias, int64_t* idx, int M, int N, int K, int dtype,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- expert parallelism (no counterpart in the reference, which runs the MoE
  * layer on one GPU): experts split over `world` ranks in contiguous blocks of
  * E / world, tokens routed on their owner rank, rows exchanged with all-to-all

@@ -477,7 +477,8 @@ bool cluster_enabled() {
 // SIMSD_ERR_UNSUPPORTED when no cluster plan fits.
 int thin_cluster(const void* x, long long ldx_m, const void* w, long long ldw_n, const void* w_up, const void* bias,
                  void* y, long long ldy, int M, int N, int K, int dtype, bool silu, int* err, void* const* peer_y,
-                 int col_offset, int world, int rank, void* const* peer_sig, cudaStream_t s, int dev) {
+                 int col_offset, int world, int rank, void* const* peer_sig, cudaStream_t s, int dev,
+                 unsigned long long* amax_keys = nullptr, long long* amax_idx = nullptr, int* amax_count = nullptr) {
   const int bmax = pick_bmax_rows(M);
   const long long row_tiles = silu ? cdiv(N, 64) : cdiv(N, 128);
   const int kb = (int)cdiv(K, 64);
@@ -504,6 +505,9 @@ int thin_cluster(const void* x, long long ldx_m, const void* w, long long ldw_n,
   a.row_tiles = (int)row_tiles;
   a.silu = silu ? 1 : 0;
   a.is_bf16 = dtype == SIMSD_BF16 ? 1 : 0;
+  a.amax_keys = amax_keys;
+  a.amax_idx = amax_idx;
+  a.amax_count = amax_count;
   a.world = world;
   a.rank = rank;
   a.col_offset = col_offset;
@@ -1284,6 +1288,26 @@ int simsd_thin_linear_allgather(const void* x, int64_t ldx_m, int64_t ldx_k, con
   int* err = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + WS_ERR_OFFSET);
   return thin_cluster(x, ldx_m, w, ldw_n, w_up, bias, peer_y[rank], ldy, M, N, K, dtype, silu, err, peer_y,
                       col_offset, world, rank, peer_signal, (cudaStream_t)stream, dev);
+}
+
+int simsd_thin_linear_argmax(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w, int64_t ldw_n,
+                             int64_t ldw_k, const void* bias, int64_t* idx, int M, int N, int K, int dtype,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  if (M < 1 || N < 1 || K < 1) return SIMSD_ERR_SHAPE;
+  if (dtype != SIMSD_BF16 && dtype != SIMSD_F16) return SIMSD_ERR_UNSUPPORTED;
+  if (x == nullptr || w == nullptr || idx == nullptr) return SIMSD_ERR_SHAPE;
+  if (workspace == nullptr || workspace_bytes < (size_t)WS_COUNTER_BYTES) return SIMSD_ERR_WORKSPACE;
+  if (M > 64 || K < 64 || !cluster_enabled() ||
+      !thin_tc_possible(x, ldx_m, ldx_k, w, ldw_n, ldw_k, nullptr, M, N, K, dtype))
+    return SIMSD_ERR_UNSUPPORTED;
+  const int dev = current_device();
+  if (dev < 0) return SIMSD_ERR_DEVICE;
+  char* ws = reinterpret_cast<char*>(workspace);
+  int* err = reinterpret_cast<int*>(ws + WS_ERR_OFFSET);
+  auto* keys = reinterpret_cast<unsigned long long*>(ws + WS_ARGMAX_OFFSET);
+  int* count = reinterpret_cast<int*>(ws + WS_ARGMAX_OFFSET + 64 * 8);
+  return thin_cluster(x, ldx_m, w, ldw_n, nullptr, bias, nullptr, 0, M, N, K, dtype, false, err, nullptr, 0, 1, 0,
+                      nullptr, (cudaStream_t)stream, dev, keys, reinterpret_cast<long long*>(idx), count);
 }
 
 }  // extern "C"

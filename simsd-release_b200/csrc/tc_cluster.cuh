@@ -51,6 +51,13 @@ struct TcClusterArgs {
   int row_tiles;             // output tiles (128 weight rows, or 64 gate + 64 up rows)
   int silu, is_bf16, pdl, prefetch;
   int l2_ahead;              // ring stages of weights requested into L2 ahead of the ring
+  // argmax mode (amax_keys != nullptr, plain epilogue, world 1): y is not
+  // written; amax_idx[t] = the first column of the largest output of row t
+  // after rounding to the output type (torch.argmax over the rounded logits).
+  // amax_keys [rows] and amax_count are zero before the launch and again after.
+  unsigned long long* amax_keys;
+  long long* amax_idx;
+  int* amax_count;
   unsigned long long* trace; // optional: 8 %globaltimer stamps per CTA (diagnostics)
   // column-parallel all-gather (world > 1): every output element is stored at
   // column col_offset + col of each rank's y (peer_out[r], NVLink mappings),
@@ -70,7 +77,7 @@ struct TcClusterConfig {
   static constexpr int B_STAGE = KS * B_ATOM;
   static constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
   static constexpr int RED_BYTES = TC_CL_RED_ROWS * BMAX * 4;
-  static constexpr int TAIL_BYTES = 2 * 10 * 8 + 8 * 8 + 64 + 64 * 16 * 4;
+  static constexpr int TAIL_BYTES = 2 * 10 * 8 + 8 * 8 + 64 + 64 * 16 * 4 + 64 * 8;
   static constexpr int STAGES_RAW = (227 * 1024 - 1024 - RED_BYTES - TAIL_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 10 ? 10 : STAGES_RAW;
   static constexpr int TMEM_COLS = (2 * BMAX) < 32 ? 32 : 2 * BMAX;
@@ -103,6 +110,18 @@ struct RowOwner {
   }
 };
 
+// Argmax key of output column `col` with value v: the value rounded to the
+// output type, in an order-preserving unsigned form (NaN above everything, the
+// two zeros equal), then 0xffffffff - col so that equal values keep the lowest
+// column under a max.
+__device__ __forceinline__ unsigned long long amax_key(float v, int col, int odt) {
+  float r = odt == 0 ? __bfloat162float(__float2bfloat16_rn(v)) : __half2float(__float2half_rn(v));
+  if (r == 0.0f) r = 0.0f;
+  const uint32_t b = __float_as_uint(r);
+  const uint32_t k = (r != r) ? 0xffffffffu : ((b & 0x80000000u) ? ~b : (b | 0x80000000u));
+  return ((unsigned long long)k << 32) | (unsigned long long)(0xffffffffu - (uint32_t)col);
+}
+
 template <int BMAX, int KS>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_constant__ TcClusterArgs p) {
   using Cfg = TcClusterConfig<BMAX, KS>;
@@ -123,6 +142,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc);
   volatile int* abort_flag = misc + 1;
   float* xbuf = reinterpret_cast<float*>(misc + 16);  // [16][64]
+  unsigned long long* amax_best = reinterpret_cast<unsigned long long*>(xbuf + 16 * 64);  // [64]
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -320,9 +340,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
     const uint32_t red_free_u32 = smem_u32(red_free);
     auto swz = [](int lr, int j) { return BMAX >= 32 ? (j ^ (lr & 7)) : (j ^ ((lr >> 1) & 3)); };
     bool cluster_acquired = false;
-    // y[t, col] on this GPU, or on every rank's GPU for the fused all-gather
+    // y[t, col] on this GPU, or on every rank's GPU for the fused all-gather,
+    // or (argmax mode) the CTA's running maximum of row t
+    if (p.amax_keys != nullptr && row < BMAX) amax_best[row] = 0ull;   // before the first tile's barrier
     auto put = [&](long long t, int col, float v) {
-      if (p.world <= 1) {
+      if (p.amax_keys != nullptr) {
+        atomicMax(&amax_best[t], amax_key(v, col, odt));
+      } else if (p.world <= 1) {
         store_f(outp, t * p.ld_out + col, v, odt);
       } else {
         for (int r = 0; r < p.world; ++r) store_f(p.peer_out[r], t * p.ld_out + p.col_offset + col, v, odt);
@@ -484,6 +508,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
             if (r != q) mbar_arrive_remote(mapa_shared(red_free_u32, (uint32_t)r));
       }
       ++done;
+    }
+    if (p.amax_keys != nullptr) {
+      // every CTA adds its maxima to the launch's keys and counts itself; the
+      // last one turns the keys into column indices and zeroes them again
+      volatile int* sh_amax_last = misc + 5;
+      named_bar_sync(1, 128);
+      if (row < nrows_all && amax_best[row] != 0ull) atomicMax(&p.amax_keys[row], amax_best[row]);
+      __threadfence();
+      named_bar_sync(1, 128);
+      if (row == 0) *sh_amax_last = atomicAdd(p.amax_count, 1) == (int)gridDim.x - 1 ? 1 : 0;
+      named_bar_sync(1, 128);
+      if (*sh_amax_last) {
+        __threadfence();
+        if (row < nrows_all) {
+          const unsigned long long k = atomicExch(&p.amax_keys[row], 0ull);
+          p.amax_idx[row] = (long long)(0xffffffffu - (uint32_t)(k & 0xffffffffull));
+        }
+        if (row == 0) atomicExch(p.amax_count, 0);
+      }
     }
     if (!cluster_acquired) cluster_wait_acquire();
     if (S > 1 && done < n_tiles && row == 0) {

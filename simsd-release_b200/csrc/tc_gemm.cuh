@@ -46,7 +46,8 @@ constexpr int TC_MAX_GROUPS = 1024;
 constexpr int TC_MAX_GRID = 1024;          // CTAs per launch (segments per tile <= this)
 constexpr int WS_COUNTER_BYTES = 256 * 1024;          // head of every workspace (reserved)
 constexpr int WS_ERR_OFFSET = WS_COUNTER_BYTES - 64;  // device error word
-constexpr int WS_MAX_COUNTERS = (WS_COUNTER_BYTES - 256) / 4;  // per-tile arrival counters from offset 0
+constexpr int WS_ARGMAX_OFFSET = WS_COUNTER_BYTES - 4096;    // argmax keys [64] u64, then its launch counter
+constexpr int WS_MAX_COUNTERS = WS_ARGMAX_OFFSET / 4;          // per-tile arrival counters from offset 0
 constexpr int TC_TABLE_INTS = 2 * (TC_MAX_GROUPS + 1);
 
 struct alignas(64) TcGemmArgs {

@@ -161,15 +161,20 @@ class SDARVerifyModel(nn.Module):
                     p.copy_(torch.randn(p.shape, generator=g, device=device, dtype=torch.float32).mul_(0.02))
         return m.eval()
 
-    def forward(self, ids, positions, mask, past=None):
-        """ids [1, L]; positions [L]; mask [1, 1, L, L_past + L] bool; past: list of (k, v)."""
+    def hidden(self, ids, positions, mask, past=None):
+        """The final-norm hidden states [1, L, H] (the lm_head input) and the KV."""
         h = self.embed_tokens(ids)
         cos, sin = rope_cos_sin(positions, self.s.head_dim, self.s.rope_theta, h.dtype)
         kvs = []
         for i, layer in enumerate(self.layers):
             h, kv = layer(h, cos, sin, mask, None if past is None else past[i])
             kvs.append(kv)
-        return self.lm_head(self.norm(h)), kvs
+        return self.norm(h), kvs
+
+    def forward(self, ids, positions, mask, past=None):
+        """ids [1, L]; positions [L]; mask [1, 1, L, L_past + L] bool; past: list of (k, v)."""
+        h, kvs = self.hidden(ids, positions, mask, past)
+        return self.lm_head(h), kvs
 
 
 # ------------------------------------------------------------------ verify sequence
@@ -300,6 +305,28 @@ class VerifyHarness:
     def window_logits(self):
         logits, _ = self.model(self.win_ids, self.win_pos, self.window_mask, self.past)
         return logits[0]
+
+    def window_argmax(self):
+        """The greedy target token of every window row, [L] int64, with the fused
+        lm_head + argmax (no [L, vocab] logits)."""
+        from .thin_linear_fused import thin_linear_argmax
+        h, _ = self.model.hidden(self.win_ids, self.win_pos, self.window_mask, self.past)
+        return thin_linear_argmax(h[0], self.model.lm_head.weight)
+
+    def window_argmax_via_logits(self):
+        """The same from the logits, as the reference does (lm_head, then argmax)."""
+        return self.window_logits().float().argmax(-1)
+
+    def accept_ids(self, target_ids, draft_blocks):
+        """accept() from per-row greedy targets [L] instead of logits."""
+        out = []
+        for k in range(self.K):
+            arg = target_ids[self.mask_rows(k)].tolist()
+            acc, n, bonus = greedy_match_verify(list(draft_blocks[k]), arg)
+            out.append((acc, n, bonus))
+            if bonus is not None:
+                break
+        return out
 
     def mask_rows(self, k: int) -> slice:
         start = k * 2 * self.bl + self.bl

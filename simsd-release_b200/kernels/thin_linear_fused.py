@@ -186,6 +186,51 @@ def thin_linear_silu_mul(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tens
     return y.view(out_shape)
 
 
+def thin_linear_argmax(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """`F.linear(x, w, bias).argmax(-1)` without the [..., N] logits: the greedy
+    verify head (lm_head then argmax, speculative_decoding/cache_aware.py:1193-1196,
+    mrs.py:138).  Each logit is rounded to x.dtype as F.linear's output would be;
+    ties go to the lowest index, as torch.argmax.  -> int64 [...].
+
+    One launch of the M <= 64 tensor-core kernel whose epilogue keeps a running
+    maximum per row; other requests (M > 64, fp32, odd layouts) run thin_linear
+    and an argmax on the device.
+    """
+    if torch.is_grad_enabled() and (x.requires_grad or w.requires_grad or (bias is not None and bias.requires_grad)):
+        raise RuntimeError("thin_linear_argmax is a forward-only inference kernel.")
+    if x.dtype != w.dtype or (bias is not None and bias.dtype != x.dtype):
+        raise TypeError(f"dtype mismatch: x={x.dtype} w={w.dtype}")
+    if w.ndim != 2 or x.shape[-1] != w.shape[1]:
+        raise ValueError(f"K mismatch: x[..., {x.shape[-1]}] vs w{tuple(w.shape)}")
+    N, K = w.shape
+    dev = _lib.require_cuda(x, w, bias)
+    lead = x.shape[:-1]
+    M = 1
+    for d in lead:
+        M *= d
+    idx = torch.empty((M,), device=dev, dtype=torch.int64)
+    if M == 0:
+        return idx.view(lead)
+    if N == 0:
+        raise ValueError("argmax over zero output columns")
+    x2 = x.reshape(M, K)
+    if bias is not None and bias.stride(0) != 1:
+        bias = bias.contiguous()
+    rc = _lib.SIMSD_ERR_UNSUPPORTED
+    if x.dtype in (torch.bfloat16, torch.float16):
+        code = _lib.dtype_code(x.dtype)
+        with _lib.device_guard(dev):
+            ws = _lib.workspace(dev, _lib.lib().simsd_workspace_header_bytes())
+            rc = _lib.lib().simsd_thin_linear_argmax(
+                x2.data_ptr(), x2.stride(0), x2.stride(1), w.data_ptr(), w.stride(0), w.stride(1),
+                bias.data_ptr() if bias is not None else None, idx.data_ptr(), M, N, K, code,
+                ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
+    if rc == _lib.SIMSD_ERR_UNSUPPORTED:
+        return thin_linear(x2, w, bias).argmax(-1).view(lead)
+    _lib.check(rc, "thin_linear_argmax")
+    return idx.view(lead)
+
+
 def should_fuse(M: int, N: int, K: int) -> bool:
     """Route this call to the thin kernel (True) or to cuBLAS `F.linear` (False).
 

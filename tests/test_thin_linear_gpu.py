@@ -21,7 +21,8 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from kernels import _lib, fused_toggle
-from kernels.thin_linear_fused import FUSE_MAX_M, ThinLinear, should_fuse, thin_linear, thin_linear_silu_mul
+from kernels.thin_linear_fused import (FUSE_MAX_M, ThinLinear, should_fuse, thin_linear, thin_linear_argmax,
+                                      thin_linear_silu_mul)
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -443,6 +444,82 @@ def test_inkernel_reduction_matches_fixup_kernel_bitwise(M, K, N, silu):
             _lib.set_inkernel_reduce(prev)
         torch.cuda.synchronize()
     assert all(torch.equal(g, ref) for g in got)
+
+
+# ------------------------------------------------------------------ greedy head
+# thin_linear_argmax = argmax over the rounded logits that thin_linear itself
+# returns (same plan, same summation order), ties to the lowest column.
+@pytest.mark.parametrize("M,N,K,dtype,bias", [
+    (32, 151936, 4096, torch.bfloat16, False),   # SDAR-8B lm_head over the 32 verify rows
+    (4, 151936, 4096, torch.bfloat16, False),
+    (1, 1000, 64, torch.bfloat16, False),
+    (16, 12345, 1024, torch.float16, True),      # ragged last tile, fp16, bias
+    (64, 50000, 512, torch.bfloat16, True),
+    (7, 300, 130, torch.bfloat16, False),        # K*2 not a multiple of 16: the device-argmax path
+])
+def test_argmax_head_equals_argmax_of_thin_linear(M, N, K, dtype, bias):
+    x = rnd(M, K, dtype=dtype, seed=M + N)
+    w = rnd(N, K, dtype=dtype, scale=0.02, seed=K)
+    b = rnd(N, dtype=dtype, scale=0.1, seed=3) if bias else None
+    with torch.inference_mode():
+        ref = thin_linear(x, w, b).argmax(-1)
+        got = thin_linear_argmax(x, w, b)
+        again = thin_linear_argmax(x, w, b)      # the argmax slots are zero again after a call
+    torch.cuda.synchronize()
+    assert got.dtype == torch.int64 and got.shape == (M,)
+    assert torch.equal(got, ref) and torch.equal(again, ref)
+
+
+def test_argmax_head_ties_and_zeros():
+    M, N, K = 8, 4096, 1024
+    x = rnd(M, K, seed=11)
+    w = rnd(N, K, scale=0.02, seed=12)
+    w[300] = (x[0].float() * 0.05).to(w.dtype)   # row 0's maximum, by far
+    w[3000] = w[300]                             # an exact tie: the lower column wins
+    w[77] = w[300] * 0                           # all-zero row
+    with torch.inference_mode():
+        got = thin_linear_argmax(x, w)
+        zero = thin_linear_argmax(torch.zeros_like(x), w)
+    torch.cuda.synchronize()
+    assert int(got[0]) == 300
+    assert torch.equal(got, thin_linear(x, w).argmax(-1))
+    assert torch.equal(zero, torch.zeros(M, dtype=torch.int64, device=DEV))   # all logits 0: column 0
+
+
+def test_argmax_head_vs_fp32_reference():
+    """Against a plain fp32 reference: the same column, or a near-tie (the two
+    logits within 2 bf16 ulps of the larger, where rounding decides)."""
+    M, N, K = 32, 151936, 4096
+    x = rnd(M, K, seed=21)
+    w = rnd(N, K, scale=0.02, seed=22)
+    with torch.inference_mode():
+        got = thin_linear_argmax(x, w).cpu()
+    ref_logits = (x.float() @ w.float().T).to(torch.bfloat16).float().cpu()
+    ref = ref_logits.argmax(-1)
+    for m in range(M):
+        g, r = int(got[m]), int(ref[m])
+        if g != r:
+            a, c = float(ref_logits[m, g]), float(ref_logits[m, r])
+            assert abs(a - c) <= 2 * 2 ** -7 * max(abs(a), abs(c)), (m, g, r, a, c)
+
+
+def test_argmax_head_in_graph_replay():
+    x = rnd(32, 4096, seed=31)
+    w = rnd(20000, 4096, scale=0.02, seed=32)
+    with torch.inference_mode():
+        ref = thin_linear_argmax(x, w)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            thin_linear_argmax(x, w)
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            out = thin_linear_argmax(x, w)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+    assert torch.equal(out, ref)
 
 
 def test_no_device_errors_recorded():

@@ -125,3 +125,32 @@ def test_bf16_flips_only_at_near_ties_and_graph_replay():
     finally:
         del h
         torch.cuda.empty_cache()
+
+
+def test_bf16_fused_greedy_head():
+    """The fused lm_head + argmax (thin_linear_argmax on the final hidden states)
+    against the logits path (cuBLAS lm_head, then argmax): the same token on
+    every row except where the two bf16 logits round differently, which is only
+    possible where the logits' top two are within two bf16 ulps.  Acceptance
+    from the fused targets follows the same rule as from logits."""
+    torch.cuda.empty_cache()
+    h = _setup(torch.bfloat16)
+    try:
+        sets = _draft_sets(h)[:3]
+        fused_toggle.apply_to_model(h.model, True, fuse_gate_up=True)
+        with torch.inference_mode():
+            for d in sets:
+                h.set_drafts(d, h.smaps)
+                fused = h.window_argmax()
+                lg = h.window_logits().float()
+                torch.cuda.synchronize()
+                via = lg.argmax(-1)
+                for r in torch.nonzero(fused != via).flatten().tolist():
+                    a, b = float(lg[r, fused[r]]), float(lg[r, via[r]])
+                    assert abs(a - b) <= 2 * 2 ** -7 * max(abs(a), abs(b)), (r, a, b)
+                if torch.equal(fused, via):
+                    assert h.accept_ids(fused, d) == h.accept(lg, d)
+        fused_toggle.apply_to_model(h.model, False)
+    finally:
+        del h
+        torch.cuda.empty_cache()
