@@ -612,7 +612,7 @@ def verify_bench(dev, steps: int) -> dict:
     tok/s = K*bl / forward latency (CUDA-graph replay of the 32-row window
     forward through all 36 layers + lm_head).  Measured twice on the same
     weights: the reference path (stock nn.Linear = cuBLAS) and ours
-    (fused_toggle with the fused gate/up, PDL).  Algorithmic bytes per forward:
+    (fused_toggle with the fused gate/up and merged q/k/v, PDL).  Algorithmic bytes per forward:
     every linear weight + lm_head + the embedding rows + the KV prefix.
     """
     from kernels import fused_toggle
@@ -661,7 +661,7 @@ def verify_bench(dev, steps: int) -> dict:
     timed("reference_cublas")
     # the whole greedy step: forward, lm_head and the argmax of every row
     timed("reference_cublas_greedy", h.window_argmax_via_logits)
-    fused_toggle.apply_to_model(model, True, fuse_gate_up=True)
+    fused_toggle.apply_to_model(model, True, fuse_gate_up=True, fuse_qkv=True)
     fused_toggle.warmup(model, BL, extra_M=(2 * BL * K,))
     timed("ours")
     timed("ours_greedy_fused_head", h.window_argmax)

@@ -287,6 +287,21 @@ int simsd_thin_linear_argmax(const void* x, int64_t ldx_m, int64_t ldx_k, const 
                              int64_t ldw_k, const void* bias, int64_t* idx, int M, int N, int K, int dtype,
                              void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Linears that share their input, in one launch: y[:, off_i : off_i + n[i]] =
+ * x . w[i]^T for i < parts (<= 3), off_i = n[0] + ... + n[i-1] — the merged
+ * q/k/v projection (the reference measured its merged qkv at -138 us per
+ * forward, kernels/workspace/thin_linear/CONTRACT.md:287-289) without copying
+ * the three weights into one.  w[i] [n[i], K] row-major with row stride
+ * ldw_n[i] (unit K stride); every part but the last a multiple of 128 rows; y
+ * row stride ldy >= the total width.  M <= 64, K >= 64, bf16/fp16 with
+ * TMA-describable layouts, else SIMSD_ERR_UNSUPPORTED (use simsd_thin_linear
+ * per part).
+ */
+int simsd_thin_linear_cat(const void* x, int64_t ldx_m, int64_t ldx_k, int parts, const void* const* w,
+                          const int64_t* ldw_n, const int* n, void* y, int64_t ldy, int M, int K, int dtype,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- expert parallelism (no counterpart in the reference, which runs the MoE
  * layer on one GPU): experts split over `world` ranks in contiguous blocks of
  * E / world, tokens routed on their owner rank, rows exchanged with all-to-all

@@ -475,10 +475,20 @@ bool cluster_enabled() {
 // checked by thin_tc_possible).  world > 1: the fused all-gather variant, with
 // peer outputs / signal blocks and this rank's column offset.  Returns
 // SIMSD_ERR_UNSUPPORTED when no cluster plan fits.
+// Up to three weights whose outputs are concatenated along N (plain epilogue):
+// w[i] [n[i], K] with row stride ldw[i]; every part but the last a multiple of 128 rows.
+struct CatSpec {
+  int parts = 0;
+  const void* w[3] = {nullptr, nullptr, nullptr};
+  long long ldw[3] = {0, 0, 0};
+  int n[3] = {0, 0, 0};
+};
+
 int thin_cluster(const void* x, long long ldx_m, const void* w, long long ldw_n, const void* w_up, const void* bias,
                  void* y, long long ldy, int M, int N, int K, int dtype, bool silu, int* err, void* const* peer_y,
                  int col_offset, int world, int rank, void* const* peer_sig, cudaStream_t s, int dev,
-                 unsigned long long* amax_keys = nullptr, long long* amax_idx = nullptr, int* amax_count = nullptr) {
+                 unsigned long long* amax_keys = nullptr, long long* amax_idx = nullptr, int* amax_count = nullptr,
+                 const CatSpec* cat = nullptr) {
   const int bmax = pick_bmax_rows(M);
   const long long row_tiles = silu ? cdiv(N, 64) : cdiv(N, 128);
   const int kb = (int)cdiv(K, 64);
@@ -492,8 +502,19 @@ int thin_cluster(const void* x, long long ldx_m, const void* w, long long ldw_n,
   const uint64_t xd[2] = {(uint64_t)K, (uint64_t)M}, xs[1] = {(uint64_t)lx * 2};
   const uint64_t wd[2] = {(uint64_t)K, (uint64_t)N}, wsb[1] = {(uint64_t)lw * 2};
   int rc = encode_map(&a.tmB, x, dtype, 2, xd, xs, (uint32_t)bmax);
-  if (rc == SIMSD_OK) rc = encode_map(&a.tmA0, w, dtype, 2, wd, wsb, silu ? 64 : 128);
-  if (rc == SIMSD_OK && silu) rc = encode_map(&a.tmA1, w_up, dtype, 2, wd, wsb, 64);
+  if (cat != nullptr && cat->parts > 1) {
+    CUtensorMap* maps[3] = {&a.tmA0, &a.tmA1, &a.tmA2};
+    for (int i = 0; i < cat->parts && rc == SIMSD_OK; ++i) {
+      const long long li = cat->n[i] > 1 ? cat->ldw[i] : ((K * 2 + 15) / 16) * 8;
+      const uint64_t di[2] = {(uint64_t)K, (uint64_t)cat->n[i]}, si[1] = {(uint64_t)li * 2};
+      rc = encode_map(maps[i], cat->w[i], dtype, 2, di, si, 128);
+    }
+    a.cat_t1 = cat->n[0] / 128;
+    a.cat_t2 = cat->parts > 2 ? (cat->n[0] + cat->n[1]) / 128 : 1 << 30;
+  } else {
+    if (rc == SIMSD_OK) rc = encode_map(&a.tmA0, w, dtype, 2, wd, wsb, silu ? 64 : 128);
+    if (rc == SIMSD_OK && silu) rc = encode_map(&a.tmA1, w_up, dtype, 2, wd, wsb, 64);
+  }
   if (rc != SIMSD_OK) return rc;
   a.out = y;
   a.bias = bias;
@@ -1308,6 +1329,35 @@ int simsd_thin_linear_argmax(const void* x, int64_t ldx_m, int64_t ldx_k, const 
   int* count = reinterpret_cast<int*>(ws + WS_ARGMAX_OFFSET + 64 * 8);
   return thin_cluster(x, ldx_m, w, ldw_n, nullptr, bias, nullptr, 0, M, N, K, dtype, false, err, nullptr, 0, 1, 0,
                       nullptr, (cudaStream_t)stream, dev, keys, reinterpret_cast<long long*>(idx), count);
+}
+
+int simsd_thin_linear_cat(const void* x, int64_t ldx_m, int64_t ldx_k, int parts, const void* const* w,
+                          const int64_t* ldw_n, const int* n, void* y, int64_t ldy, int M, int K, int dtype,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  if (M < 1 || K < 1 || parts < 1 || parts > 3 || w == nullptr || ldw_n == nullptr || n == nullptr)
+    return SIMSD_ERR_SHAPE;
+  if (dtype != SIMSD_BF16 && dtype != SIMSD_F16) return SIMSD_ERR_UNSUPPORTED;
+  if (x == nullptr || y == nullptr) return SIMSD_ERR_SHAPE;
+  if (workspace == nullptr || workspace_bytes < (size_t)WS_COUNTER_BYTES) return SIMSD_ERR_WORKSPACE;
+  if (M > 64 || K < 64 || !cluster_enabled()) return SIMSD_ERR_UNSUPPORTED;
+  CatSpec cs;
+  cs.parts = parts;
+  long long N = 0;
+  for (int i = 0; i < parts; ++i) {
+    if (w[i] == nullptr || n[i] < 1) return SIMSD_ERR_SHAPE;
+    if (i + 1 < parts && n[i] % 128 != 0) return SIMSD_ERR_UNSUPPORTED;
+    if (!thin_tc_possible(x, ldx_m, ldx_k, w[i], ldw_n[i], 1, nullptr, M, n[i], K, dtype)) return SIMSD_ERR_UNSUPPORTED;
+    cs.w[i] = w[i];
+    cs.ldw[i] = ldw_n[i];
+    cs.n[i] = n[i];
+    N += n[i];
+  }
+  if (N >= (1LL << 31) || ldy < N) return SIMSD_ERR_SHAPE;
+  const int dev = current_device();
+  if (dev < 0) return SIMSD_ERR_DEVICE;
+  int* err = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + WS_ERR_OFFSET);
+  return thin_cluster(x, ldx_m, w[0], ldw_n[0], nullptr, nullptr, y, ldy, M, (int)N, K, dtype, false, err, nullptr,
+                      0, 1, 0, nullptr, (cudaStream_t)stream, dev, nullptr, nullptr, nullptr, &cs);
 }
 
 }  // extern "C"

@@ -39,7 +39,12 @@ constexpr int TC_CL_RED_ROWS = 144;   // >= S * rows one owner holds, for every 
 
 struct TcClusterArgs {
   CUtensorMap tmA0;          // weights (gate rows when silu): 2-D {K, N}
-  CUtensorMap tmA1;          // up rows (silu only)
+  CUtensorMap tmA1;          // up rows (silu), or the second weight of a concatenation
+  CUtensorMap tmA2;          // the third weight of a concatenation
+  // concatenated weights (plain epilogue): output tiles [0, cat_t1) read tmA0,
+  // [cat_t1, cat_t2) tmA1 and [cat_t2, row_tiles) tmA2, each from its row 0,
+  // into one y of the concatenated width; cat_t1 == 0: one weight
+  int cat_t1, cat_t2;
   CUtensorMap tmB;           // activations: 2-D {K, M}
   void* out;                 // y, row stride ld_out elements
   const void* bias;          // [rows_out] or nullptr
@@ -110,6 +115,21 @@ struct RowOwner {
   }
 };
 
+// Tensor map and first weight row of plain output tile `rtile` (one weight, or
+// the part of a concatenation the tile falls in).
+__device__ __forceinline__ const CUtensorMap* weight_map(const TcClusterArgs& p, int rtile, int& row0) {
+  if (p.cat_t1 > 0 && rtile >= p.cat_t1) {
+    if (rtile >= p.cat_t2) {
+      row0 = (rtile - p.cat_t2) * 128;
+      return &p.tmA2;
+    }
+    row0 = (rtile - p.cat_t1) * 128;
+    return &p.tmA1;
+  }
+  row0 = rtile * 128;
+  return &p.tmA0;
+}
+
 // Argmax key of output column `col` with value v: the value rounded to the
 // output type, in an order-preserving unsigned form (NaN above everything, the
 // two zeros equal), then 0xffffffff - col so that equal values keep the lowest
@@ -171,7 +191,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
   }
   if (warp == 4 && lane == 0) {
     prefetch_tmap(&p.tmA0);
-    if (p.silu) prefetch_tmap(&p.tmA1);
+    if (p.silu || p.cat_t1 > 0) prefetch_tmap(&p.tmA1);
+    if (p.cat_t1 > 0) prefetch_tmap(&p.tmA2);
     prefetch_tmap(&p.tmB);
   }
   if (warp == 5) {
@@ -242,7 +263,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
                 tma_prefetch_l2_2d(&p.tmA0, (pk + at) * 64, prt * 64, pol_w);
                 tma_prefetch_l2_2d(&p.tmA1, (pk + at) * 64, prt * 64, pol_w);
               } else {
-                tma_prefetch_l2_2d(&p.tmA0, (pk + at) * 64, prt * 128, pol_w);
+                int pr0;
+                const CUtensorMap* pm = weight_map(p, prt, pr0);
+                tma_prefetch_l2_2d(pm, (pk + at) * 64, pr0, pol_w);
               }
             }
           }
@@ -260,7 +283,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
               tma_load_2d(a_dst, &p.tmA0, fb, k0, rtile * 64, pol_w);
               tma_load_2d(a_dst + 8192, &p.tmA1, fb, k0, rtile * 64, pol_w);
             } else {
-              tma_load_2d(a_dst, &p.tmA0, fb, k0, rtile * 128, pol_w);
+              int r0;
+              const CUtensorMap* wm = weight_map(p, rtile, r0);
+              tma_load_2d(a_dst, wm, fb, k0, r0, pol_w);
             }
             if (dep_ready) tma_load_2d(b_dst + at * Cfg::B_ATOM, &p.tmB, fb, k0, 0, pol_x);
           }

@@ -69,6 +69,7 @@ SIGNATURES: dict[str, tuple] = {
     "simsd_ipc_open": (_I, [_P, ctypes.POINTER(_P)]),
     "simsd_ipc_close": (_I, [_P]),
     "simsd_thin_linear_argmax": (_I, [_P, _L, _L, _P, _L, _L, _P, _P, _I, _I, _I, _I, _P, _S, _P]),
+    "simsd_thin_linear_cat": (_I, [_P, _L, _L, _I, _P, _P, _P, _P, _L, _I, _I, _I, _P, _S, _P]),
     "simsd_thin_linear_allgather": (_I, [_P, _L, _L, _P, _L, _L, _P, _P, _P, _L, _I, _I, _I, _I, _I, _I, _I, _I,
                                          _P, _P, _S, _P]),
     "simsd_moe_ep_plan": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P]),

@@ -13,10 +13,16 @@ alias the original parameters (no copy; `state_dict()` unchanged).  It is
 idempotent, returns the number of modules swapped or restored, and must run
 before CUDA-graph capture, which freezes whatever forward is installed.
 
-One addition: `apply_to_model(..., fuse_gate_up=True)` also patches SwiGLU MLP
-modules (attributes gate_proj / up_proj / down_proj and a SiLU `act_fn`, as
-`SDARMLP` in sdar/modeling_sdar.py:99-119) so gate and up run as one kernel
-reading both weights once, with the SiLU*mul applied before the single rounding.
+Two additions:
+* `apply_to_model(..., fuse_gate_up=True)` also patches SwiGLU MLP modules
+  (attributes gate_proj / up_proj / down_proj and a SiLU `act_fn`, as `SDARMLP`
+  in sdar/modeling_sdar.py:99-119) so gate and up run as one kernel reading both
+  weights once, with the SiLU*mul applied before the single rounding;
+* `apply_to_model(..., fuse_qkv=True)` makes the q_proj / k_proj / v_proj of
+  each attention module (bias-free, as SDAR's, sdar/modeling_sdar.py:197-302)
+  share one launch: the first of the three called on an input computes all
+  three (`thin_linear_cat`, the weights are not copied) and the other two
+  return their parts of that output when called on the same input tensor.
 """
 from __future__ import annotations
 
@@ -24,7 +30,7 @@ import torch
 import torch.nn as nn
 
 from ._lib import reset_workspace
-from .thin_linear_fused import ThinLinear, should_fuse, thin_linear_silu_mul
+from .thin_linear_fused import ThinLinear, should_fuse, thin_linear_cat, thin_linear_silu_mul
 
 DEFAULT_TARGETS = (
     "q_proj", "k_proj", "v_proj", "o_proj",
@@ -74,10 +80,64 @@ def _patch_mlps(model: nn.Module) -> list[nn.Module]:
     return patched
 
 
+class _QKVShare:
+    """The merged launch of one attention module's q/k/v: its input and outputs
+    until each of the three projections has taken its part."""
+
+    def __init__(self):
+        self.parts: list["_QKVPart"] = []
+        self.x = None
+        self.out = None
+        self.taken = [False, False, False]
+
+
+class _QKVPart(ThinLinear):
+    """q_proj, k_proj or v_proj (index i) of a merged q/k/v; aliases the
+    original parameters like ThinLinear (same `state_dict()` keys and tensors)."""
+
+    def __init__(self, linear: nn.Linear, share: _QKVShare, i: int, config=None):
+        super().__init__(linear, config=config)
+        self.__dict__["_share"] = share   # plain attribute: not a submodule, not in state_dict
+        self.__dict__["_i"] = i
+
+    def forward(self, x):
+        sh, i = self._share, self._i
+        if sh.x is x and sh.out is not None and not sh.taken[i]:
+            sh.taken[i] = True
+            out = sh.out[i]
+            if all(sh.taken):
+                sh.x = sh.out = None
+            return out
+        M = x.numel() // x.shape[-1] if x.shape[-1] else 0
+        if self.config is None and should_fuse(M, self.out_features, self.in_features):
+            sh.out = thin_linear_cat(x, [p.weight for p in sh.parts])
+            sh.x = x
+            sh.taken = [j == i for j in range(3)]
+            return sh.out[i]
+        return super().forward(x)
+
+
+def _merge_qkv(model: nn.Module, saved: dict[str, nn.Module], config) -> None:
+    for name, mod in model.named_modules():
+        parts = [getattr(mod, a, None) for a in ("q_proj", "k_proj", "v_proj")]
+        if not all(isinstance(p, ThinLinear) for p in parts):
+            continue
+        if any(p.bias is not None for p in parts) or len({p.in_features for p in parts}) != 1:
+            continue
+        paths = [f"{name}.{a}" if name else a for a in ("q_proj", "k_proj", "v_proj")]
+        if not all(p in saved for p in paths):
+            continue
+        share = _QKVShare()
+        for i, (attr, path) in enumerate(zip(("q_proj", "k_proj", "v_proj"), paths)):
+            new = _QKVPart(saved[path], share, i, config=config)
+            share.parts.append(new)
+            setattr(mod, attr, new)
+
+
 def apply_to_model(model: nn.Module, enable: bool = True,
                    targets=DEFAULT_TARGETS,
                    config: tuple[int, int, int, int] | None = None,
-                   fuse_gate_up: bool = False) -> int:
+                   fuse_gate_up: bool = False, fuse_qkv: bool = False) -> int:
     """Swap the target `nn.Linear` modules for `ThinLinear` (or restore them).
 
     Idempotent in both directions.  Returns the number of modules swapped (or
@@ -105,6 +165,8 @@ def apply_to_model(model: nn.Module, enable: bool = True,
         _ORIGINALS[key] = saved
         if fuse_gate_up:
             _MLP_PATCHED[key] = _patch_mlps(model)
+        if fuse_qkv:
+            _merge_qkv(model, saved, config)
     return len(saved)
 
 

@@ -18,6 +18,8 @@ There is no CPU path: CUDA tensors only, and a missing library raises.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -229,6 +231,57 @@ def thin_linear_argmax(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | No
         return thin_linear(x2, w, bias).argmax(-1).view(lead)
     _lib.check(rc, "thin_linear_argmax")
     return idx.view(lead)
+
+
+def thin_linear_cat(x: torch.Tensor, weights) -> list[torch.Tensor]:
+    """[F.linear(x, w) for w in weights] (up to three weights of the same K) from
+    one launch, as views into one [..., sum N] output — the merged q/k/v
+    projection without concatenating the weights.  Falls back to one
+    thin_linear per weight when the kernel cannot take the request (M > 64,
+    fp32, a part other than the last not a multiple of 128 rows, odd layouts).
+    """
+    ws_ = list(weights)
+    if torch.is_grad_enabled() and (x.requires_grad or any(w.requires_grad for w in ws_)):
+        raise RuntimeError("thin_linear_cat is a forward-only inference kernel.")
+    if not 1 <= len(ws_) <= 3:
+        raise ValueError("one to three weights")
+    K = x.shape[-1]
+    for w in ws_:
+        if w.dtype != x.dtype:
+            raise TypeError(f"dtype mismatch: x={x.dtype} w={w.dtype}")
+        if w.ndim != 2 or w.shape[1] != K:
+            raise ValueError(f"K mismatch: x[..., {K}] vs w{tuple(w.shape)}")
+    dev = _lib.require_cuda(x, *ws_)
+    lead = x.shape[:-1]
+    M = 1
+    for d in lead:
+        M *= d
+    ns = [w.shape[0] for w in ws_]
+    y = torch.empty((M, sum(ns)), device=dev, dtype=x.dtype)
+    rc = _lib.SIMSD_ERR_UNSUPPORTED
+    if M > 0 and x.dtype in (torch.bfloat16, torch.float16) and all(w.stride(1) == 1 for w in ws_):
+        x2 = x.reshape(M, K)
+        P = len(ws_)
+        wp = (ctypes.c_void_p * P)(*[w.data_ptr() for w in ws_])
+        lw = (ctypes.c_int64 * P)(*[w.stride(0) for w in ws_])
+        nn_ = (ctypes.c_int * P)(*ns)
+        with _lib.device_guard(dev):
+            nbytes = _lib.thin_workspace_size(torch.cuda.current_device(), M, sum(ns), K,
+                                              _lib.dtype_code(x.dtype), _lib.EPI_NONE, 0)
+            ws = _lib.workspace(dev, nbytes)
+            rc = _lib.lib().simsd_thin_linear_cat(
+                x2.data_ptr(), x2.stride(0), x2.stride(1), P, wp, lw, nn_, y.data_ptr(), y.stride(0), M, K,
+                _lib.dtype_code(x.dtype), ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
+    outs, off = [], 0
+    if rc == _lib.SIMSD_ERR_UNSUPPORTED:
+        for w in ws_:
+            outs.append(thin_linear(x, w))
+        return outs
+    _lib.check(rc, "thin_linear_cat")
+    for n in ns:
+        outs.append(y[:, off:off + n].view(*lead, n))
+        off += n
+    return outs
 
 
 def should_fuse(M: int, N: int, K: int) -> bool:

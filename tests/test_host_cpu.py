@@ -129,6 +129,35 @@ def test_gate_up_patch_installs_and_removes():
         assert torch.allclose(y, m(x))
 
 
+class _Attn(nn.Module):
+    def __init__(self, bias=False):
+        super().__init__()
+        self.q_proj = nn.Linear(64, 128, bias=bias)
+        self.k_proj = nn.Linear(64, 32, bias=bias)
+        self.v_proj = nn.Linear(64, 32, bias=bias)
+        self.o_proj = nn.Linear(128, 64, bias=False)
+
+    def forward(self, x):
+        return self.q_proj(x), self.k_proj(x), self.v_proj(x)
+
+
+def test_qkv_merge_installs_aliases_and_restores():
+    m = nn.Sequential(_Attn(), _Attn(bias=True))
+    before = {k: v for k, v in m.state_dict(keep_vars=True).items()}
+    assert fused_toggle.apply_to_model(m, True, fuse_qkv=True) == 8
+    merged = [type(getattr(m[0], a)).__name__ for a in ("q_proj", "k_proj", "v_proj")]
+    assert merged == ["_QKVPart"] * 3                  # bias-free attention: merged
+    assert type(m[1].q_proj).__name__ == "ThinLinear"  # with biases: plain swap
+    after = m.state_dict(keep_vars=True)
+    assert set(after) == set(before) and all(after[k] is before[k] for k in before)
+    x = torch.randn(FUSE_MAX_M + 1, 64)                 # above the guard: stock math on CPU
+    with torch.inference_mode():
+        q, k, v = m[0](x)
+    assert torch.allclose(q, torch.nn.functional.linear(x, m[0].q_proj.weight))
+    assert fused_toggle.apply_to_model(m, False) == 8
+    assert isinstance(m[0].q_proj, nn.Linear) and not isinstance(m[0].q_proj, fused_toggle.ThinLinear)
+
+
 class LLaDA2MoeSparseMoeBlock(nn.Module):     # same class name the toggle looks for
     def __init__(self, E=4, H=32, I=16):
         super().__init__()

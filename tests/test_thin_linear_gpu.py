@@ -22,7 +22,7 @@ import torch.nn.functional as F
 
 from kernels import _lib, fused_toggle
 from kernels.thin_linear_fused import (FUSE_MAX_M, ThinLinear, should_fuse, thin_linear, thin_linear_argmax,
-                                      thin_linear_silu_mul)
+                                      thin_linear_cat, thin_linear_silu_mul)
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -520,6 +520,57 @@ def test_argmax_head_in_graph_replay():
             g.replay()
         torch.cuda.synchronize()
     assert torch.equal(out, ref)
+
+
+# ------------------------------------------------------------------ merged q/k/v
+@pytest.mark.parametrize("M,K,ns,dtype", [
+    (32, 4096, (4096, 1024, 1024), torch.bfloat16),   # SDAR-8B q/k/v at the verify M
+    (4, 4096, (4096, 1024, 1024), torch.bfloat16),
+    (64, 4096, (4096, 1024, 1024), torch.bfloat16),
+    (1, 2048, (2048, 1024, 1024), torch.float16),     # SDAR-1.7B draft
+    (16, 1024, (256, 1000), torch.bfloat16),          # two parts, ragged last
+    (8, 512, (384,), torch.bfloat16),                 # one part
+    (8, 512, (100, 128, 64), torch.bfloat16),         # first part not 128-aligned: per-part fallback
+    (96, 1024, (256, 128, 128), torch.bfloat16),      # M > 64: per-part fallback
+])
+def test_qkv_cat_matches_f_linear(M, K, ns, dtype):
+    x = rnd(M, K, dtype=dtype, seed=M + K)
+    ws = [rnd(n, K, dtype=dtype, scale=0.02, seed=10 + i) for i, n in enumerate(ns)]
+    with torch.inference_mode():
+        outs = thin_linear_cat(x, ws)
+        again = thin_linear_cat(x, ws)
+        refs = [F.linear(x, w) for w in ws]
+    torch.cuda.synchronize()
+    for o, a, r in zip(outs, again, refs):
+        assert o.shape == r.shape and o.dtype == r.dtype
+        assert float((o.float() - r.float()).abs().max()) <= tol(r)
+        assert torch.equal(o, a)                      # bit-identical across calls
+    assert_oracle(x, torch.cat(ws, 0), torch.cat([o.reshape(M, -1) for o in outs], -1))
+
+
+def test_qkv_merge_in_attention_module():
+    class Attn(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.q_proj = nn.Linear(4096, 4096, bias=False)
+            self.k_proj = nn.Linear(4096, 1024, bias=False)
+            self.v_proj = nn.Linear(4096, 1024, bias=False)
+
+        def forward(self, h):
+            return self.q_proj(h), self.k_proj(h), self.v_proj(h)
+
+    m = Attn().to(DEV, torch.bfloat16)
+    h = rnd(1, 32, 4096, seed=5)
+    with torch.inference_mode():
+        ref = m(h)
+        assert fused_toggle.apply_to_model(m, True, fuse_qkv=True) == 3
+        got = m(h)
+        got2 = m(h.clone())                           # a new input tensor: a new merged launch
+        fused_toggle.apply_to_model(m, False)
+    for g, g2, r in zip(got, got2, ref):
+        assert g.shape == r.shape
+        assert float((g.float() - r.float()).abs().max()) <= tol(r)
+        assert torch.equal(g, g2)
 
 
 def test_no_device_errors_recorded():

@@ -90,7 +90,7 @@ def test_bf16_flips_only_at_near_ties_and_graph_replay():
     try:
         sets = _draft_sets(h)[:3]
         ref = [_logits(h, d) for d in sets]
-        fused_toggle.apply_to_model(h.model, True, fuse_gate_up=True)
+        fused_toggle.apply_to_model(h.model, True, fuse_gate_up=True, fuse_qkv=True)
         with _lib.weights_static():
             fused_toggle.warmup(h.model, BL, extra_M=(2 * BL * K,))
             ours = [_logits(h, d) for d in sets]
@@ -137,7 +137,7 @@ def test_bf16_fused_greedy_head():
     h = _setup(torch.bfloat16)
     try:
         sets = _draft_sets(h)[:3]
-        fused_toggle.apply_to_model(h.model, True, fuse_gate_up=True)
+        fused_toggle.apply_to_model(h.model, True, fuse_gate_up=True, fuse_qkv=True)
         with torch.inference_mode():
             for d in sets:
                 h.set_drafts(d, h.smaps)
