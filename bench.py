@@ -612,7 +612,9 @@ def verify_bench(dev, steps: int) -> dict:
     tok/s = K*bl / forward latency (CUDA-graph replay of the 32-row window
     forward through all 36 layers + lm_head).  Measured twice on the same
     weights: the reference path (stock nn.Linear = cuBLAS) and ours
-    (fused_toggle with the fused gate/up and merged q/k/v, PDL).  Algorithmic bytes per forward:
+    (fused_toggle with the fused gate/up and merged q/k/v, PDL, and the fused
+    layer ops: RMSNorm + residual, q/k norm + rotary + cache write).  Both use a
+    static KV cache.  Algorithmic bytes per forward:
     every linear weight + lm_head + the embedding rows + the KV prefix.
     """
     from kernels import fused_toggle
@@ -663,8 +665,10 @@ def verify_bench(dev, steps: int) -> dict:
     timed("reference_cublas_greedy", h.window_argmax_via_logits)
     fused_toggle.apply_to_model(model, True, fuse_gate_up=True, fuse_qkv=True)
     fused_toggle.warmup(model, BL, extra_M=(2 * BL * K,))
+    h.fused = True          # RMSNorms with the residual add, q/k norm + rotary + cache write
     timed("ours")
     timed("ours_greedy_fused_head", h.window_argmax)
+    h.fused = False
     fused_toggle.apply_to_model(model, False)
     res["value"] = res["ours"]["tok_s"]
     res["speedup_vs_cublas"] = round(res["reference_cublas"]["ms_per_forward"] / res["ours"]["ms_per_forward"], 3)
@@ -821,11 +825,18 @@ def profile_verify(args):
     drafts = [torch.randint(0, SDAR_8B.vocab, (4,), generator=g).tolist() for _ in range(4)]
     smaps = [torch.randperm(4, generator=g).tolist() for _ in range(4)]
     h = VerifyHarness(model, prompt, drafts, smaps, 4)
-    if args.profile_verify == "ours":
-        fused_toggle.apply_to_model(model, True, fuse_gate_up=True)
+    ours = args.profile_verify == "ours"
+    if ours:
+        fused_toggle.apply_to_model(model, True, fuse_gate_up=True, fuse_qkv=True)
+    step = h.window_argmax if ours else h.window_argmax_via_logits
     with torch.inference_mode():
-        for _ in range(args.profile_launches + 1):
-            h.window_logits()
+        step()
+        torch.cuda.synchronize()
+        # the greedy verify steps to capture: ncu --nvtx --nvtx-include "verify_step/"
+        for _ in range(args.profile_launches):
+            torch.cuda.nvtx.range_push("verify_step")
+            step()
+            torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
     print(f"profile verify ({args.profile_verify}) done")
 

@@ -302,6 +302,29 @@ int simsd_thin_linear_cat(const void* x, int64_t ldx_m, int64_t ldx_k, int parts
                           const int64_t* ldw_n, const int* n, void* y, int64_t ldy, int M, int K, int dtype,
                           void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Layer ops of the verify forward around its linears (sdar/modeling_sdar.py with
+ * the fp32 RMSNorm of sdar/run_native_tp2.py:34-51):
+ *
+ * simsd_rmsnorm: per row r < rows, h = x[r] (res == NULL) or h = round(x[r] +
+ * res[r]) (also stored to h_out when not NULL), y[r] = w * round(h_f32 *
+ * rsqrt(mean(h_f32^2) + eps)), the product rounded to dtype.  n <= 16384.
+ *
+ * simsd_qk_norm_rope: the attention front end for L tokens at positions pos..
+ * pos+L-1 of one sequence, head_dim 128.  qkv [L, (Hq + 2 Hk) * 128] (row stride
+ * ldqkv; q heads, k heads, v heads) -> q_out [Hq, L, 128] = rope(rmsnorm(q)),
+ * k_cache[g, pos + t] = rope(rmsnorm(k)), v_cache[g, pos + t] = v (caches
+ * [Hk, cache_cap, 128]); rope(x) = round(round(x cos) + round(rotate_half(x) sin))
+ * with cos/sin [L, 128] in dtype.  Replaces the per-layer q_norm / k_norm,
+ * rotary embedding and KV-cache write (sdar/modeling_sdar.py:197-302 with the
+ * reference's static cache writes, speculative_decoding/cache_aware.py).
+ */
+int simsd_rmsnorm(const void* x, int64_t ldx, const void* res, int64_t ldres, void* h_out, int64_t ldh,
+                  const void* w, void* y, int64_t ldy, int rows, int n, float eps, int dtype, void* stream);
+int simsd_qk_norm_rope(const void* qkv, int64_t ldqkv, int L, int Hq, int Hk, int head_dim, const void* q_weight,
+                       const void* k_weight, const void* cos, const void* sin, float eps, void* q_out, void* k_cache,
+                       void* v_cache, int64_t cache_cap, int pos, int dtype, void* stream);
+
 /* ---- expert parallelism (no counterpart in the reference, which runs the MoE
  * layer on one GPU): experts split over `world` ranks in contiguous blocks of
  * E / world, tokens routed on their owner rank, rows exchanged with all-to-all

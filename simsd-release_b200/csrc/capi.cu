@@ -12,6 +12,7 @@
 #include <mutex>
 
 #include "moe.cuh"
+#include "norm.cuh"
 #include "simsd_b200.h"
 #include "simt_gemm.cuh"
 #include "tc_cluster.cuh"
@@ -1358,6 +1359,63 @@ int simsd_thin_linear_cat(const void* x, int64_t ldx_m, int64_t ldx_k, int parts
   int* err = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + WS_ERR_OFFSET);
   return thin_cluster(x, ldx_m, w[0], ldw_n[0], nullptr, nullptr, y, ldy, M, (int)N, K, dtype, false, err, nullptr,
                       0, 1, 0, nullptr, (cudaStream_t)stream, dev, nullptr, nullptr, nullptr, &cs);
+}
+
+int simsd_rmsnorm(const void* x, int64_t ldx, const void* res, int64_t ldres, void* h_out, int64_t ldh,
+                  const void* w, void* y, int64_t ldy, int rows, int n, float eps, int dtype, void* stream) {
+  if (rows < 0 || n < 1 || n > 16384) return SIMSD_ERR_SHAPE;
+  if (dtype != SIMSD_BF16 && dtype != SIMSD_F16) return SIMSD_ERR_DTYPE;
+  if (rows == 0) return SIMSD_OK;
+  if (!x || !w || !y || ldx < n || ldy < n || (res && ldres < n) || (h_out && ldh < n)) return SIMSD_ERR_SHAPE;
+  RmsNormArgs a;
+  a.x = x;
+  a.res = res;
+  a.h_out = h_out;
+  a.w = w;
+  a.y = y;
+  a.ldx = ldx;
+  a.ldres = ldres;
+  a.ldh = ldh;
+  a.ldy = ldy;
+  a.rows = rows;
+  a.n = n;
+  a.dtype = dtype;
+  a.eps = eps;
+  const int smem = (n + NORM_THREADS / 32) * (int)sizeof(float);
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return SIMSD_ERR_LAUNCH;
+  return launch(rmsnorm_kernel, dim3((unsigned)rows), dim3(NORM_THREADS), smem, (cudaStream_t)stream, a);
+}
+
+int simsd_qk_norm_rope(const void* qkv, int64_t ldqkv, int L, int Hq, int Hk, int head_dim, const void* q_weight,
+                       const void* k_weight, const void* cos, const void* sin, float eps, void* q_out, void* k_cache,
+                       void* v_cache, int64_t cache_cap, int pos, int dtype, void* stream) {
+  if (L < 0 || Hq < 1 || Hk < 1 || head_dim != 128 || pos < 0) return SIMSD_ERR_SHAPE;
+  if (dtype != SIMSD_BF16 && dtype != SIMSD_F16) return SIMSD_ERR_DTYPE;
+  if (L == 0) return SIMSD_OK;
+  if (!qkv || !q_weight || !k_weight || !cos || !sin || !q_out || !k_cache || !v_cache) return SIMSD_ERR_SHAPE;
+  if (ldqkv < (int64_t)(Hq + 2 * Hk) * head_dim || cache_cap < (int64_t)pos + L) return SIMSD_ERR_SHAPE;
+  QkRopeArgs a;
+  a.qkv = qkv;
+  a.qw = q_weight;
+  a.kw = k_weight;
+  a.cos = cos;
+  a.sin = sin;
+  a.q_out = q_out;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.ldqkv = ldqkv;
+  a.cache_cap = cache_cap;
+  a.L = L;
+  a.Hq = Hq;
+  a.Hk = Hk;
+  a.pos = pos;
+  a.dtype = dtype;
+  a.eps = eps;
+  const long long units = (long long)L * (Hq + 2 * Hk);
+  return launch(qk_norm_rope_kernel, dim3((unsigned)cdiv(units, QKR_WARPS)), dim3(QKR_WARPS * 32), 0,
+                (cudaStream_t)stream, a);
 }
 
 }  // extern "C"

@@ -93,7 +93,10 @@ class Attention(nn.Module):
         self.q_norm = RMSNorm(s.head_dim, s.eps)
         self.k_norm = RMSNorm(s.head_dim, s.eps)
 
-    def forward(self, h, cos, sin, mask, past=None):
+    def forward(self, h, cos, sin, mask, past=None, cache=None, pos=0):
+        """past: prefix (k, v) to concatenate; cache: static (k_cache, v_cache)
+        [1, Hk, cap, D] whose rows [pos, pos + L) take this call's k/v and whose
+        rows [0, pos + L) are attended (the reference's static block cache)."""
         B, L, _ = h.shape
         s = self.s
         q = self.q_norm(self.q_proj(h).view(B, L, s.heads, s.head_dim)).transpose(1, 2)
@@ -102,12 +105,31 @@ class Attention(nn.Module):
         c, si = cos[None, None], sin[None, None]
         q = q * c + _rotate_half(q) * si
         k = k * c + _rotate_half(k) * si
-        if past is not None:
+        if cache is not None:
+            cache[0][:, :, pos:pos + L].copy_(k)
+            cache[1][:, :, pos:pos + L].copy_(v)
+            k, v = cache[0][:, :, :pos + L], cache[1][:, :, :pos + L]
+        elif past is not None:
             k = torch.cat([past[0], k], dim=2)
             v = torch.cat([past[1], v], dim=2)
         o = F.scaled_dot_product_attention(q, k, v, attn_mask=mask, scale=s.head_dim ** -0.5, enable_gqa=True)
         o = o.transpose(1, 2).reshape(B, L, -1)
         return self.o_proj(o), (k, v)
+
+    def forward_fused(self, x, cos, sin, mask, cache, pos):
+        """The same with libsimsd_b200's layer ops: one merged q/k/v launch, then
+        q/k RMSNorm + rotary + the cache write in one kernel (B = 1)."""
+        from .layer_ops import qk_norm_rope
+        from .thin_linear_fused import thin_linear_cat
+        _, L, H = x.shape
+        s = self.s
+        qkv = thin_linear_cat(x.reshape(L, H), [self.q_proj.weight, self.k_proj.weight, self.v_proj.weight],
+                              whole=True)
+        q = qk_norm_rope(qkv, s.heads, s.kv_heads, self.q_norm.weight, self.k_norm.weight, cos, sin, self.q_norm.eps,
+                         cache[0][0], cache[1][0], pos)
+        k, v = cache[0][:, :, :pos + L], cache[1][:, :, :pos + L]
+        o = F.scaled_dot_product_attention(q[None], k, v, attn_mask=mask, scale=s.head_dim ** -0.5, enable_gqa=True)
+        return self.o_proj(o.transpose(1, 2).reshape(1, L, -1))
 
 
 class MLP(nn.Module):
@@ -130,8 +152,8 @@ class DecoderLayer(nn.Module):
         self.input_layernorm = RMSNorm(s.hidden, s.eps)
         self.post_attention_layernorm = RMSNorm(s.hidden, s.eps)
 
-    def forward(self, h, cos, sin, mask, past=None):
-        a, kv = self.self_attn(self.input_layernorm(h), cos, sin, mask, past)
+    def forward(self, h, cos, sin, mask, past=None, cache=None, pos=0):
+        a, kv = self.self_attn(self.input_layernorm(h), cos, sin, mask, past, cache, pos)
         h = h + a
         h = h + self.mlp(self.post_attention_layernorm(h))
         return h, kv
@@ -161,13 +183,32 @@ class SDARVerifyModel(nn.Module):
                     p.copy_(torch.randn(p.shape, generator=g, device=device, dtype=torch.float32).mul_(0.02))
         return m.eval()
 
-    def hidden(self, ids, positions, mask, past=None):
-        """The final-norm hidden states [1, L, H] (the lm_head input) and the KV."""
+    def hidden(self, ids, positions, mask, past=None, caches=None, pos=0, fused=False):
+        """The final-norm hidden states [1, L, H] (the lm_head input) and the KV.
+
+        caches: per-layer static (k_cache, v_cache) written at rows [pos, pos+L).
+        fused (with caches): libsimsd_b200's layer ops — RMSNorms fused with the
+        residual add before them, the merged q/k/v launch and the q/k norm +
+        rotary + cache-write kernel — in place of the torch expressions.
+        """
         h = self.embed_tokens(ids)
         cos, sin = rope_cos_sin(positions, self.s.head_dim, self.s.rope_theta, h.dtype)
+        if fused and caches is not None:
+            from .layer_ops import rmsnorm
+            n = len(self.layers)
+            x = rmsnorm(h, self.layers[0].input_layernorm.weight, self.layers[0].input_layernorm.eps)
+            for i, layer in enumerate(self.layers):
+                a = layer.self_attn.forward_fused(x, cos, sin, mask, caches[i], pos)
+                pn = layer.post_attention_layernorm
+                h, x = rmsnorm(a, pn.weight, pn.eps, residual=h)
+                m = layer.mlp(x)
+                nn_ = self.layers[i + 1].input_layernorm if i + 1 < n else self.norm
+                h, x = rmsnorm(m, nn_.weight, nn_.eps, residual=h)
+            return x, None
         kvs = []
         for i, layer in enumerate(self.layers):
-            h, kv = layer(h, cos, sin, mask, None if past is None else past[i])
+            h, kv = layer(h, cos, sin, mask, None if past is None else past[i],
+                          None if caches is None else caches[i], pos)
             kvs.append(kv)
         return self.norm(h), kvs
 
@@ -290,6 +331,18 @@ class VerifyHarness:
             _, self.past = model(self.ids[:, : self.P], self.pos[: self.P], self.prefix_mask)
         self.win_ids = self.ids[:, self.P:].clone()
         self.win_pos = self.pos[self.P:].clone()
+        # static per-layer KV caches (the reference's static block cache): the
+        # prefix rows once, the window rows rewritten by every verify forward
+        cap = self.P + self.win_ids.shape[1]
+        self.caches = []
+        for k, v in self.past:
+            kc = torch.zeros((1, k.shape[1], cap, k.shape[3]), dtype=k.dtype, device=dev)
+            vc = torch.zeros_like(kc)
+            kc[:, :, : self.P].copy_(k)
+            vc[:, :, : self.P].copy_(v)
+            self.caches.append((kc, vc))
+        self.past = None
+        self.fused = False      # True: libsimsd_b200's layer ops around the linears
 
     def set_drafts(self, draft_blocks, step_maps):
         """Replace the window's draft tokens / step maps in place (graph-safe)."""
@@ -302,16 +355,19 @@ class VerifyHarness:
         self.win_ids.copy_(torch.tensor(w, device=dev)[None])
         self.window_mask.copy_(full[self.P:, :][None, None])
 
+    def window_hidden(self):
+        h, _ = self.model.hidden(self.win_ids, self.win_pos, self.window_mask, caches=self.caches, pos=self.P,
+                                 fused=self.fused)
+        return h
+
     def window_logits(self):
-        logits, _ = self.model(self.win_ids, self.win_pos, self.window_mask, self.past)
-        return logits[0]
+        return self.model.lm_head(self.window_hidden())[0]
 
     def window_argmax(self):
         """The greedy target token of every window row, [L] int64, with the fused
         lm_head + argmax (no [L, vocab] logits)."""
         from .thin_linear_fused import thin_linear_argmax
-        h, _ = self.model.hidden(self.win_ids, self.win_pos, self.window_mask, self.past)
-        return thin_linear_argmax(h[0], self.model.lm_head.weight)
+        return thin_linear_argmax(self.window_hidden()[0], self.model.lm_head.weight)
 
     def window_argmax_via_logits(self):
         """The same from the logits, as the reference does (lm_head, then argmax)."""

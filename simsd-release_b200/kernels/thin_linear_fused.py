@@ -233,12 +233,13 @@ def thin_linear_argmax(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | No
     return idx.view(lead)
 
 
-def thin_linear_cat(x: torch.Tensor, weights) -> list[torch.Tensor]:
+def thin_linear_cat(x: torch.Tensor, weights, whole: bool = False):
     """[F.linear(x, w) for w in weights] (up to three weights of the same K) from
     one launch, as views into one [..., sum N] output — the merged q/k/v
     projection without concatenating the weights.  Falls back to one
     thin_linear per weight when the kernel cannot take the request (M > 64,
     fp32, a part other than the last not a multiple of 128 rows, odd layouts).
+    `whole=True` returns the concatenated [..., sum N] output instead.
     """
     ws_ = list(weights)
     if torch.is_grad_enabled() and (x.requires_grad or any(w.requires_grad for w in ws_)):
@@ -276,8 +277,10 @@ def thin_linear_cat(x: torch.Tensor, weights) -> list[torch.Tensor]:
     if rc == _lib.SIMSD_ERR_UNSUPPORTED:
         for w in ws_:
             outs.append(thin_linear(x, w))
-        return outs
+        return torch.cat(outs, -1) if whole else outs
     _lib.check(rc, "thin_linear_cat")
+    if whole:
+        return y.view(*lead, sum(ns))
     for n in ns:
         outs.append(y[:, off:off + n].view(*lead, n))
         off += n

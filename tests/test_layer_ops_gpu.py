@@ -1,0 +1,83 @@
+"""GPU parity of the verify forward's layer ops (kernels/layer_ops.py) against
+the torch expressions they replace (the harness's fp32 RMSNorm and rotary
+embedding, kernels/sdar_verify.py): elementwise steps are bit-exact; the
+RMSNorm mean square is an fp32 sum in the kernel's own order, so an output may
+differ from torch's by one rounding step of the output type."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from kernels.layer_ops import qk_norm_rope, rmsnorm
+from kernels.sdar_verify import RMSNorm, _rotate_half, rope_cos_sin
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _ulp_close(a: torch.Tensor, b: torch.Tensor, frac_max: float = 0.01):
+    """Equal, or one bf16/fp16 step apart at a small fraction of the elements."""
+    a, b = a.float(), b.float()
+    diff = (a - b).abs()
+    step = torch.maximum(a.abs(), b.abs()) * 2 ** -7 + 1e-30   # one bf16 step (fp16: finer)
+    assert bool((diff <= step).all()), float((diff / step).max())
+    assert float((diff > 0).float().mean()) <= frac_max
+
+
+@pytest.mark.parametrize("rows,n,dtype", [(32, 4096, torch.bfloat16), (1, 4096, torch.bfloat16),
+                                          (7, 1000, torch.float16), (64, 2048, torch.bfloat16)])
+def test_rmsnorm_matches_torch(rows, n, dtype):
+    g = torch.Generator(device=DEV).manual_seed(rows + n)
+    x = (torch.randn(rows, n, generator=g, device=DEV) * 3).to(dtype)
+    r = torch.randn(rows, n, generator=g, device=DEV).to(dtype)
+    norm = RMSNorm(n, 1e-6).to(DEV, dtype)
+    with torch.no_grad():
+        norm.weight.copy_((torch.randn(n, generator=g, device=DEV) * 0.5 + 1).to(dtype))
+    with torch.inference_mode():
+        y = rmsnorm(x, norm.weight, 1e-6)
+        h, y2 = rmsnorm(x, norm.weight, 1e-6, residual=r)
+        ref = norm(x)
+        href = r + x
+        ref2 = norm(href)
+    torch.cuda.synchronize()
+    _ulp_close(y, ref)
+    assert torch.equal(h, href)
+    _ulp_close(y2, ref2)
+
+
+def test_qk_norm_rope_matches_torch():
+    L, Hq, Hk, D, P = 32, 32, 8, 128, 100
+    g = torch.Generator(device=DEV).manual_seed(5)
+    bf = torch.bfloat16
+    qkv = torch.randn(L, (Hq + 2 * Hk) * D, generator=g, device=DEV).to(bf)
+    qn, kn = RMSNorm(D, 1e-6).to(DEV, bf), RMSNorm(D, 1e-6).to(DEV, bf)
+    with torch.no_grad():
+        qn.weight.copy_((torch.randn(D, generator=g, device=DEV) * 0.3 + 1).to(bf))
+        kn.weight.copy_((torch.randn(D, generator=g, device=DEV) * 0.3 + 1).to(bf))
+    pos = torch.arange(P, P + L, device=DEV)
+    cos, sin = rope_cos_sin(pos, D, 1e6, bf)
+    kc = torch.zeros(Hk, P + L, D, dtype=bf, device=DEV)
+    vc = torch.zeros_like(kc)
+    with torch.inference_mode():
+        q = qk_norm_rope(qkv, Hq, Hk, qn.weight, kn.weight, cos, sin, 1e-6, kc, vc, P)
+        x = qkv.view(1, L, Hq + 2 * Hk, D)
+        qr = qn(x[:, :, :Hq]).transpose(1, 2)
+        kr = kn(x[:, :, Hq:Hq + Hk]).transpose(1, 2)
+        vr = x[:, :, Hq + Hk:].transpose(1, 2)
+        c, s = cos[None, None], sin[None, None]
+        qr = qr * c + _rotate_half(qr) * s
+        kr = kr * c + _rotate_half(kr) * s
+    torch.cuda.synchronize()
+
+    def close_rows(a, b):
+        # the rotary sum can cancel, so its rounding step is measured on the
+        # head row's scale: within one bf16 step of the row's largest value
+        a, b = a.float(), b.float()
+        scale = b.abs().amax(-1, keepdim=True) * 2 ** -7 + 1e-30
+        assert bool(((a - b).abs() <= scale).all())
+        assert float(((a - b) != 0).float().mean()) <= 0.05
+
+    close_rows(q, qr[0])
+    close_rows(kc[:, P:], kr[0])
+    assert torch.equal(vc[:, P:], vr[0])
+    assert bool((kc[:, :P] == 0).all()) and bool((vc[:, :P] == 0).all())   # other rows untouched

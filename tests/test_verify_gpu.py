@@ -91,6 +91,7 @@ def test_bf16_flips_only_at_near_ties_and_graph_replay():
         sets = _draft_sets(h)[:3]
         ref = [_logits(h, d) for d in sets]
         fused_toggle.apply_to_model(h.model, True, fuse_gate_up=True, fuse_qkv=True)
+        h.fused = True          # and the fused layer ops (norms, q/k norm + rotary + cache write)
         with _lib.weights_static():
             fused_toggle.warmup(h.model, BL, extra_M=(2 * BL * K,))
             ours = [_logits(h, d) for d in sets]
@@ -105,6 +106,7 @@ def test_bf16_flips_only_at_near_ties_and_graph_replay():
                 assert torch.equal(out.float(), ours[0])
             del g
         fused_toggle.apply_to_model(h.model, False)
+        h.fused = False
         # fp32 truth for the same weights
         h32 = VerifyHarness(h.model.float(), h.prompt, sets[0], h.smaps, BL)
         h32.smaps = h.smaps
@@ -138,6 +140,7 @@ def test_bf16_fused_greedy_head():
     try:
         sets = _draft_sets(h)[:3]
         fused_toggle.apply_to_model(h.model, True, fuse_gate_up=True, fuse_qkv=True)
+        h.fused = True
         with torch.inference_mode():
             for d in sets:
                 h.set_drafts(d, h.smaps)
