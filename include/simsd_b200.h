@@ -325,6 +325,23 @@ int simsd_qk_norm_rope(const void* qkv, int64_t ldqkv, int L, int Hq, int Hk, in
                        const void* k_weight, const void* cos, const void* sin, float eps, void* q_out, void* k_cache,
                        void* v_cache, int64_t cache_cap, int pos, int dtype, void* stream);
 
+/*
+ * Verify attention over a static KV cache with native GQA (no expanded K/V):
+ *   o[t, h, :] = softmax_j(scale * q[h, t] . k[g, j], keys j < Lk with
+ *                mask[t * ldmask + j] != 0) v[g, j],  g = h / (Hq / Hk)
+ * q [Hq, L, 128], k_cache / v_cache [Hk, cache_cap, 128], o [L, Hq, 128] (the
+ * layout the output projection reads), all bf16 contiguous; mask bytes
+ * (torch.bool) [L, ldmask].  Split over 128-key chunks (flash decoding) on the
+ * tensor cores, chunks merged by a second kernel; fp32 softmax.  A row with
+ * every key masked comes out as zeros.  (Hq / Hk) * L <= 128, else
+ * SIMSD_ERR_UNSUPPORTED.  Replaces SDPA with enable_gqa over the reference's
+ * expanded KV (speculative_decoding/cache_aware.py:195-215).
+ */
+size_t simsd_verify_attention_workspace_size(int Hq, int Hk, int L, int Lk);
+int simsd_verify_attention(const void* q, const void* k_cache, const void* v_cache, int64_t cache_cap, int Hq,
+                           int Hk, int L, int Lk, const uint8_t* mask, int64_t ldmask, float scale, void* o,
+                           int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- expert parallelism (no counterpart in the reference, which runs the MoE
  * layer on one GPU): experts split over `world` ranks in contiguous blocks of
  * E / world, tokens routed on their owner rank, rows exchanged with all-to-all

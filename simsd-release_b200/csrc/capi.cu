@@ -13,6 +13,7 @@
 
 #include "moe.cuh"
 #include "norm.cuh"
+#include "attn.cuh"
 #include "simsd_b200.h"
 #include "simt_gemm.cuh"
 #include "tc_cluster.cuh"
@@ -1416,6 +1417,59 @@ int simsd_qk_norm_rope(const void* qkv, int64_t ldqkv, int L, int Hq, int Hk, in
   const long long units = (long long)L * (Hq + 2 * Hk);
   return launch(qk_norm_rope_kernel, dim3((unsigned)cdiv(units, QKR_WARPS)), dim3(QKR_WARPS * 32), 0,
                 (cudaStream_t)stream, a);
+}
+
+size_t simsd_verify_attention_workspace_size(int Hq, int Hk, int L, int Lk) {
+  if (Hq < 1 || Hk < 1 || L < 1 || Lk < 1) return WS_COUNTER_BYTES;
+  const long long nch = cdiv(Lk, ATT_KC);
+  return WS_COUNTER_BYTES + align256((size_t)Hk * nch * ATT_R * (ATT_D + 2) * sizeof(float));
+}
+
+int simsd_verify_attention(const void* q, const void* k_cache, const void* v_cache, int64_t cache_cap, int Hq,
+                           int Hk, int L, int Lk, const uint8_t* mask, int64_t ldmask, float scale, void* o,
+                           int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  if (Hq < 1 || Hk < 1 || L < 1 || Lk < 1 || Hq % Hk != 0) return SIMSD_ERR_SHAPE;
+  if (dtype != SIMSD_BF16) return SIMSD_ERR_UNSUPPORTED;
+  if ((Hq / Hk) * L > ATT_R) return SIMSD_ERR_UNSUPPORTED;
+  if (!q || !k_cache || !v_cache || !mask || !o || cache_cap < Lk || ldmask < Lk) return SIMSD_ERR_SHAPE;
+  auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+  if (!al16(q) || !al16(k_cache) || !al16(v_cache) || !al16(o)) return SIMSD_ERR_ALIGN;
+  const int nch = (int)cdiv(Lk, ATT_KC);
+  if (workspace == nullptr || workspace_bytes < simsd_verify_attention_workspace_size(Hq, Hk, L, Lk))
+    return SIMSD_ERR_WORKSPACE;
+  AttnArgs a;
+  a.q = q;
+  a.k = k_cache;
+  a.v = v_cache;
+  a.mask = mask;
+  a.o = o;
+  a.part_o = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + WS_COUNTER_BYTES);
+  a.part_ml = a.part_o + (size_t)Hk * nch * ATT_R * ATT_D;
+  a.cap = cache_cap;
+  a.ldm = ldmask;
+  a.Hq = Hq;
+  a.Hk = Hk;
+  a.L = L;
+  a.Lk = Lk;
+  a.nchunks = nch;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  constexpr int smem = 3 * 32768;
+  {
+    static bool done[kMaxDev];
+    const int dev = current_device();
+    if (dev < 0) return SIMSD_ERR_DEVICE;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!done[dev]) {
+      if (cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        return SIMSD_ERR_LAUNCH;
+      done[dev] = true;
+    }
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = launch(attn_split_kernel, dim3((unsigned)nch, (unsigned)Hk), dim3(ATT_THREADS), smem, st, a);
+  if (rc != SIMSD_OK) return rc;
+  const long long units = (long long)Hk * (Hq / Hk) * L;
+  return launch(attn_combine_kernel, dim3((unsigned)cdiv(units, 8)), dim3(256), 0, st, a);
 }
 
 }  // extern "C"

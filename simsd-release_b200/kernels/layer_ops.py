@@ -76,3 +76,30 @@ def qk_norm_rope(qkv: torch.Tensor, heads: int, kv_heads: int, q_weight: torch.T
             _lib.stream_ptr(dev))
     _lib.check(rc, "qk_norm_rope")
     return q
+
+
+def verify_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, Lk: int, mask: torch.Tensor,
+                     scale: float) -> torch.Tensor:
+    """GQA attention of q [Hq, L, 128] over keys [0, Lk) of k_cache / v_cache
+    [Hk, cap, 128] under mask [L, >= Lk] (bool, True = attend) -> o [L, Hq * 128],
+    the layout the output projection reads.  bf16, contiguous operands."""
+    Hq, L, D = q.shape
+    Hk = k_cache.shape[0]
+    if q.dtype != torch.bfloat16 or k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
+        raise TypeError("verify_attention takes bf16 q / k_cache / v_cache")
+    if D != 128 or k_cache.shape != v_cache.shape or k_cache.shape[2] != 128 or Hq % Hk != 0:
+        raise ValueError("head_dim 128, Hq a multiple of Hk, k_cache and v_cache alike")
+    if mask.dtype != torch.bool or mask.ndim != 2 or mask.shape[0] != L or mask.shape[1] < Lk or mask.stride(1) != 1:
+        raise ValueError(f"mask must be a bool [{L}, >= {Lk}] with unit column stride")
+    if not (q.is_contiguous() and k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("q, k_cache and v_cache must be contiguous")
+    dev = _lib.require_cuda(q, k_cache, v_cache, mask)
+    o = torch.empty((L, Hq * D), dtype=q.dtype, device=dev)
+    L_ = _lib.lib()
+    with _lib.device_guard(dev):
+        ws = _lib.workspace(dev, L_.simsd_verify_attention_workspace_size(Hq, Hk, L, Lk))
+        rc = L_.simsd_verify_attention(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[1], Hq, Hk,
+                                       L, Lk, mask.data_ptr(), mask.stride(0), float(scale), o.data_ptr(),
+                                       _lib.dtype_code(q.dtype), ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
+    _lib.check(rc, "verify_attention")
+    return o

@@ -118,8 +118,9 @@ class Attention(nn.Module):
 
     def forward_fused(self, x, cos, sin, mask, cache, pos):
         """The same with libsimsd_b200's layer ops: one merged q/k/v launch, then
-        q/k RMSNorm + rotary + the cache write in one kernel (B = 1)."""
-        from .layer_ops import qk_norm_rope
+        q/k RMSNorm + rotary + the cache write in one kernel, then GQA attention
+        straight over the static cache (B = 1)."""
+        from .layer_ops import qk_norm_rope, verify_attention
         from .thin_linear_fused import thin_linear_cat
         _, L, H = x.shape
         s = self.s
@@ -127,9 +128,8 @@ class Attention(nn.Module):
                               whole=True)
         q = qk_norm_rope(qkv, s.heads, s.kv_heads, self.q_norm.weight, self.k_norm.weight, cos, sin, self.q_norm.eps,
                          cache[0][0], cache[1][0], pos)
-        k, v = cache[0][:, :, :pos + L], cache[1][:, :, :pos + L]
-        o = F.scaled_dot_product_attention(q[None], k, v, attn_mask=mask, scale=s.head_dim ** -0.5, enable_gqa=True)
-        return self.o_proj(o.transpose(1, 2).reshape(1, L, -1))
+        o = verify_attention(q, cache[0][0], cache[1][0], pos + L, mask[0, 0], s.head_dim ** -0.5)
+        return self.o_proj(o.view(1, L, -1))
 
 
 class MLP(nn.Module):

@@ -8,7 +8,7 @@ from __future__ import annotations
 import pytest
 import torch
 
-from kernels.layer_ops import qk_norm_rope, rmsnorm
+from kernels.layer_ops import qk_norm_rope, rmsnorm, verify_attention
 from kernels.sdar_verify import RMSNorm, _rotate_half, rope_cos_sin
 
 pytestmark = pytest.mark.gpu
@@ -81,3 +81,41 @@ def test_qk_norm_rope_matches_torch():
     close_rows(kc[:, P:], kr[0])
     assert torch.equal(vc[:, P:], vr[0])
     assert bool((kc[:, :P] == 0).all()) and bool((vc[:, :P] == 0).all())   # other rows untouched
+
+
+@pytest.mark.parametrize("Hq,Hk,L,Lk,cap,pmask", [(32, 8, 32, 2080, 2080, 0.0), (32, 8, 32, 2080, 2100, 0.3),
+                                                  (16, 8, 8, 300, 320, 0.5), (32, 8, 4, 129, 129, 0.0),
+                                                  (8, 8, 16, 1000, 1000, 0.9)])
+def test_verify_attention_matches_fp32_reference(Hq, Hk, L, Lk, cap, pmask):
+    g = torch.Generator(device=DEV).manual_seed(Lk + L)
+    bf = torch.bfloat16
+    q = torch.randn(Hq, L, 128, generator=g, device=DEV).to(bf)
+    kc = torch.randn(Hk, cap, 128, generator=g, device=DEV).to(bf)
+    vc = torch.randn(Hk, cap, 128, generator=g, device=DEV).to(bf)
+    mask = torch.rand(L, Lk + 5, generator=g, device=DEV) >= pmask
+    mask[:, 0] = True                                   # every row sees a key
+    mask[0, 1:] = False                                 # row 0: one key only
+    scale = 128 ** -0.5
+    with torch.inference_mode():
+        o = verify_attention(q, kc, vc, Lk, mask, scale).view(L, Hq, 128)
+    G = Hq // Hk
+    kf = kc[:, :Lk].float().repeat_interleave(G, 0)
+    vf = vc[:, :Lk].float().repeat_interleave(G, 0)
+    s = (q.float() @ kf.transpose(1, 2)) * scale
+    s = s.masked_fill(~mask[None, :, :Lk], float("-inf"))
+    ref = (torch.softmax(s, -1) @ vf).transpose(0, 1)  # [L, Hq, 128]
+    err = float((o.float() - ref).abs().max())
+    assert err <= 2 ** -7 * float(ref.abs().max()) + 2e-2, err
+
+
+def test_verify_attention_fully_masked_row_is_zero():
+    bf = torch.bfloat16
+    g = torch.Generator(device=DEV).manual_seed(3)
+    q = torch.randn(32, 32, 128, generator=g, device=DEV).to(bf)
+    kc = torch.randn(8, 500, 128, generator=g, device=DEV).to(bf)
+    vc = torch.randn(8, 500, 128, generator=g, device=DEV).to(bf)
+    mask = torch.ones(32, 500, dtype=torch.bool, device=DEV)
+    mask[5] = False
+    with torch.inference_mode():
+        o = verify_attention(q, kc, vc, 500, mask, 0.1).view(32, 32, 128)
+    assert bool((o[5] == 0).all()) and bool(torch.isfinite(o.float()).all())
