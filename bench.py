@@ -828,6 +828,7 @@ def profile_verify(args):
     ours = args.profile_verify == "ours"
     if ours:
         fused_toggle.apply_to_model(model, True, fuse_gate_up=True, fuse_qkv=True)
+        h.fused = True
     step = h.window_argmax if ours else h.window_argmax_via_logits
     with torch.inference_mode():
         step()

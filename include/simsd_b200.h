@@ -62,6 +62,7 @@ extern "C" {
 /* ---- launch flags (process-wide) */
 #define SIMSD_LAUNCH_PDL 1   /* programmatic dependent launch, see simsd_set_launch_flags */
 #define SIMSD_LAUNCH_INKERNEL_REDUCE 2  /* split-K tiles summed inside the GEMM, see below */
+#define SIMSD_LAUNCH_GROUPED_FIXUP 4    /* MoE grouped GEMMs: split tiles summed by a second kernel */
 
 /* Library version string. */
 const char* simsd_version(void);
@@ -82,7 +83,11 @@ const char* simsd_status_string(int status);
  * SIMSD_LAUNCH_INKERNEL_REDUCE: a tile whose K range is split over several CTAs
  * is summed by the last of them to finish (counted per tile in the workspace
  * header) instead of by a separate reduction kernel launched after the GEMM.
- * Same summation order, so the two give identical bits.
+ * Same summation order, so the two give identical bits.  The MoE dispatch's
+ * grouped GEMMs always sum split tiles inside the GEMM (whether any tile is
+ * split depends on the routing, which the host does not read, so a reduction
+ * kernel would be launched for nothing at most token counts), unless
+ * SIMSD_LAUNCH_GROUPED_FIXUP asks for the separate kernel (same bits).
  */
 int simsd_set_launch_flags(int flags);
 

@@ -158,6 +158,10 @@ int prefetch_stages() {
 inline bool use_counters() {
   return (g_launch_flags.load(std::memory_order_relaxed) & SIMSD_LAUNCH_INKERNEL_REDUCE) != 0;
 }
+// grouped (MoE) GEMMs: in-kernel reduction unless SIMSD_LAUNCH_GROUPED_FIXUP
+inline bool use_counters_grouped() {
+  return (g_launch_flags.load(std::memory_order_relaxed) & SIMSD_LAUNCH_GROUPED_FIXUP) == 0;
+}
 
 // Weight stages the cluster GEMM requests into L2 ahead of its shared-memory
 // ring: SIMSD_TC_L2_AHEAD overrides the default.
@@ -604,7 +608,7 @@ const char* simsd_status_string(int s) {
 }
 
 int simsd_set_launch_flags(int flags) {
-  return g_launch_flags.exchange(flags & (SIMSD_LAUNCH_PDL | SIMSD_LAUNCH_INKERNEL_REDUCE));
+  return g_launch_flags.exchange(flags & (SIMSD_LAUNCH_PDL | SIMSD_LAUNCH_INKERNEL_REDUCE | SIMSD_LAUNCH_GROUPED_FIXUP));
 }
 
 int simsd_get_launch_flags(void) { return g_launch_flags.load(); }
@@ -1090,7 +1094,7 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
     a.ld_out = I;
     a.partials = reinterpret_cast<float*>(ws + plan.off_part);
     a.tables = reinterpret_cast<int*>(ws + plan.off_tables);
-    a.counters = use_counters() && plan.max_chunks * cdiv(I, 64) <= WS_MAX_COUNTERS ? reinterpret_cast<int*>(ws) : nullptr;
+    a.counters = use_counters_grouped() && plan.max_chunks * cdiv(I, 64) <= WS_MAX_COUNTERS ? reinterpret_cast<int*>(ws) : nullptr;
     a.err = err;
     a.group_counts = counts;
     a.num_groups = E;
@@ -1124,7 +1128,7 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
     d.ld_out = H;
     d.partials = a.partials;
     d.tables = a.tables;
-    d.counters = use_counters() && plan.max_chunks * cdiv(H, 128) <= WS_MAX_COUNTERS ? reinterpret_cast<int*>(ws) : nullptr;
+    d.counters = use_counters_grouped() && plan.max_chunks * cdiv(H, 128) <= WS_MAX_COUNTERS ? reinterpret_cast<int*>(ws) : nullptr;
     d.err = err;
     d.group_counts = counts;
     d.num_groups = E;

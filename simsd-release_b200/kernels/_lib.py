@@ -32,6 +32,7 @@ PATH_AUTO, PATH_TC, PATH_SIMT = 0, 1, 2
 
 LAUNCH_PDL = 1
 LAUNCH_INKERNEL_REDUCE = 2
+LAUNCH_GROUPED_FIXUP = 4
 IPC_HANDLE_BYTES = 64
 SIGNAL_BYTES = 256
 
@@ -229,6 +230,12 @@ def set_pdl(enable: bool) -> bool:
     """Launch kernels as programmatic dependents (weights must not be written by the
     kernel right before each call on the same stream).  Returns the previous setting."""
     return _set_flag(LAUNCH_PDL, enable)
+
+
+def set_grouped_fixup(enable: bool) -> bool:
+    """MoE grouped GEMMs: sum split tiles in a separate reduction kernel instead of
+    inside the GEMM (the default); same bits.  Returns the previous setting."""
+    return _set_flag(LAUNCH_GROUPED_FIXUP, enable)
 
 
 def set_inkernel_reduce(enable: bool) -> bool:

@@ -289,23 +289,25 @@ def test_dispatch_deterministic_and_noncontiguous_x():
     assert torch.equal(a, b) and torch.equal(a, c)
 
 
-@pytest.mark.parametrize("T,conc", [(64, None), (256, None), (300, 0.05)])
+@pytest.mark.parametrize("T,conc", [(1, None), (2, None), (4, 0.3), (64, None), (300, 0.05)])
 def test_dispatch_inkernel_reduction_matches_fixup_kernel_bitwise(T, conc):
-    """Grouped GEMM tiles split over CTAs give the same bits whether their last
-    contributor or the separate reduction kernel sums them."""
+    """Grouped GEMM tiles split over CTAs (few tokens: fewer tiles than two per
+    CTA) give the same bits whether their last contributor (the default) or the
+    separate reduction kernel sums them."""
     k, E, H, I = 8, 256, 2048, 512
     ids, w = routing(T, k, E, seed=T, conc=conc)
     g = torch.Generator(device=DEV).manual_seed(T + 1)
     x = torch.randn(T, H, device=DEV, generator=g).to(torch.bfloat16)
     wg, wu, wd = experts(E, H, I, torch.bfloat16, seed=T + 2)
     with torch.inference_mode():
-        ref = moe_dispatch(x, ids, w, wg, wu, wd)
-        prev = _lib.set_inkernel_reduce(True)
+        got = moe_dispatch(x, ids, w, wg, wu, wd)
+        prev = _lib.set_grouped_fixup(True)
         try:
-            got = moe_dispatch(x, ids, w, wg, wu, wd)
+            ref = moe_dispatch(x, ids, w, wg, wu, wd)
         finally:
-            _lib.set_inkernel_reduce(prev)
-    assert torch.equal(got, ref)
+            _lib.set_grouped_fixup(prev)
+        again = moe_dispatch(x, ids, w, wg, wu, wd)      # counters left at zero: same again
+    assert torch.equal(got, ref) and torch.equal(again, ref)
 
 
 def test_dispatch_all_tokens_one_expert_and_empty():
