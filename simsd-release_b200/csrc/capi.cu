@@ -1001,9 +1001,9 @@ MoePlan plan_moe(int T, int k, int E, int H, int I, int dtype, int sms, bool tc)
   // re-read its weights.
   const double avg = E > 0 ? (double)S / E : (double)S;
   const double want = avg + 4.0 * std::sqrt(avg) + 8.0;
-  p.bmax = want <= 16 ? 16 : want <= 32 ? 32 : want <= 64 ? 64 : 128;
-  // SIMSD_MOE_BMAX (16, 32, 64, 128) overrides the choice (measurement knob)
-  p.bmax = env_choice("SIMSD_MOE_BMAX", {16, 32, 64, 128}, p.bmax);
+  p.bmax = want <= 16 ? 16 : want <= 32 ? 32 : want <= 64 ? 64 : want <= 128 ? 128 : 256;
+  // SIMSD_MOE_BMAX (16, 32, 64, 128, 256) overrides the choice (measurement knob)
+  p.bmax = env_choice("SIMSD_MOE_BMAX", {16, 32, 64, 128, 256}, p.bmax);
   p.grid = std::max(1, std::min(sms > 0 ? sms : 148, TC_MAX_GRID));
   size_t o = WS_COUNTER_BYTES;
   p.off_counts = o; o = align256(o + (size_t)E * 4);
