@@ -207,7 +207,9 @@ def test_dispatch_golden_reference_outputs():
 
 
 @pytest.mark.parametrize("T,k,E,H,I,conc", [(16, 8, 256, 2048, 512, None), (64, 8, 256, 2048, 512, 0.2),
-                                            (32, 4, 16, 256, 128, None), (8, 8, 64, 512, 192, 0.05)])
+                                            (32, 4, 16, 256, 128, None), (8, 8, 64, 512, 192, 0.05),
+                                            (1024, 2, 8, 512, 256, None),     # ~256 rows per expert: 256-row tiles
+                                            (600, 4, 16, 256, 192, 0.3)])     # busy experts split in 128/256-row chunks
 def test_dispatch_vs_oracle(T, k, E, H, I, conc):
     ids, w = routing(T, k, E, seed=T * k + E, conc=conc)
     g = torch.Generator(device=DEV).manual_seed(E + H)
