@@ -524,9 +524,10 @@ def moe_bench(dev, steps: int, cpu_seconds: float | None) -> dict:
     bf = torch.bfloat16
     wr = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(bf)
     bias = torch.randn(E, generator=g, device=dev) * MOE["bias_std"]
+    # each pool: the E routed experts and the shared expert stacked as expert E
+    # (stack_shared_expert's layout), so the shared expert runs in the grouped GEMMs
     pools = [tuple((torch.randn(*sh, generator=g, device=dev) * 0.02).to(bf)
-                   for sh in ((E, I, H), (E, I, H), (E, H, I))) for _ in range(POOL)]
-    shared = tuple((torch.randn(*sh, generator=g, device=dev) * 0.02).to(bf) for sh in ((I, H), (I, H), (H, I)))
+                   for sh in ((E + 1, I, H), (E + 1, I, H), (E + 1, H, I))) for _ in range(POOL)]
     pk = peaks()
     tc_peak = float(json.loads((REPO / "MEASURED_PEAKS.json").read_text())["bf16_tflops"]) * 1e12 \
         if (REPO / "MEASURED_PEAKS.json").exists() else 1.59e15
@@ -539,13 +540,13 @@ def moe_bench(dev, steps: int, cpu_seconds: float | None) -> dict:
             n_active = int(torch.unique(ids).numel())
             for _ in range(3):
                 for p in pools:
-                    moe_layer(x, wr, bias, k, *p, shared=shared)
+                    moe_layer(x, wr, bias, k, *p, shared_stacked=True)
             torch.cuda.synchronize()
             graphs = []
             for p in pools:
                 gr = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(gr):
-                    moe_layer(x, wr, bias, k, *p, shared=shared)
+                    moe_layer(x, wr, bias, k, *p, shared_stacked=True)
                 graphs.append(gr)
             for i in range(4):
                 graphs[i % POOL].replay()
@@ -567,8 +568,8 @@ def moe_bench(dev, steps: int, cpu_seconds: float | None) -> dict:
             tot_t += ms
             del graphs
     res = {"workload": "MoE layer, BASELINE configs[2]: H=2048, E=256, top-8 sigmoid+bias(N(0,0.1)) router, "
-                       "I=512 SiLU*mul experts + 1 shared expert, bf16, CUDA-graph replay over 2 expert-weight "
-                       "pools (2 x 1.6 GB)",
+                       "I=512 SiLU*mul experts + 1 shared expert (stacked as expert E, run in the same grouped "
+                       "GEMMs), bf16, CUDA-graph replay over 2 expert-weight pools (2 x 1.6 GB)",
            "metric": "MoE layer HBM GB/s (algorithmic bytes: active experts + shared + router + activations)",
            "value": round(tot_b / tot_t / 1e6, 1), "unit": "GB/s",
            "frac_hbm_peak": round(tot_b / tot_t / 1e6 / pk["hbm_gbs"], 4), "per_T": out}

@@ -198,6 +198,16 @@ int simsd_moe_route(const void* x, int64_t ldx, int x_dtype, const void* wr, int
                     void* stream);
 
 /*
+ * simsd_moe_route with the outputs at row stride ld_topk (>= k, or >= k + 1 with
+ * extra_id) and, when extra_id >= 0, column k of every row set to (extra_id,
+ * 1.0): the always-on shared expert stacked after the routed ones, for
+ * simsd_moe_dispatch_shared_last.
+ */
+int simsd_moe_route_ex(const void* x, int64_t ldx, int x_dtype, const void* wr, int64_t ldw, int w_dtype,
+                       const float* bias, int T, int H, int E, int k, int renorm, float scale, int64_t* topk_ids,
+                       float* topk_weight, int64_t ld_topk, int extra_id, float* logits, void* stream);
+
+/*
  * Expert align: per-expert counts, offsets and the stable slot permutation.
  * Replaces _align - kernels/moe_dispatch_fused.py:93-132 (bit-exact).
  *
@@ -241,6 +251,19 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids,
                        int64_t ldd_h, void* out, int64_t ld_out, const void* add,
                        int64_t ld_add, int T, int k, int E, int H, int I, int dtype,
                        void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * simsd_moe_dispatch whose last routing column (k - 1) is an always-on shared
+ * expert stacked as an expert of w_gate / w_up / w_down: its rows run in the
+ * same grouped GEMMs as the routed experts, and the combine adds its output
+ * unweighted to the rounded sum of the other columns — cast(cast(sum) +
+ * shared), the reference model's `moe_infer(...) + shared_experts(x)`.
+ */
+int simsd_moe_dispatch_shared_last(const void* x, int64_t ldx, const int64_t* topk_ids, const float* topk_weight,
+                                   const void* w_gate, const void* w_up, int64_t ldg_e, int64_t ldg_i,
+                                   const void* w_down, int64_t ldd_e, int64_t ldd_h, void* out, int64_t ld_out,
+                                   int T, int k, int E, int H, int I, int dtype, void* workspace,
+                                   size_t workspace_bytes, void* stream);
 
 /* ---- column-parallel thin linear with the all-gather fused in (no counterpart in
  * the reference).  Each rank of a node holds rows [rank*N, (rank+1)*N) of the

@@ -846,7 +846,15 @@ int simsd_thin_linear_noalloc(const void* x, int64_t ldx_m, int64_t ldx_k, const
 int simsd_moe_route(const void* x, int64_t ldx, int x_dtype, const void* wr, int64_t ldw, int w_dtype,
                     const float* bias, int T, int H, int E, int k, int renorm, float scale, int64_t* topk_ids,
                     float* topk_weight, float* logits, void* stream) {
+  return simsd_moe_route_ex(x, ldx, x_dtype, wr, ldw, w_dtype, bias, T, H, E, k, renorm, scale, topk_ids, topk_weight,
+                            k, -1, logits, stream);
+}
+
+int simsd_moe_route_ex(const void* x, int64_t ldx, int x_dtype, const void* wr, int64_t ldw, int w_dtype,
+                       const float* bias, int T, int H, int E, int k, int renorm, float scale, int64_t* topk_ids,
+                       float* topk_weight, int64_t ld_topk, int extra_id, float* logits, void* stream) {
   if (T < 0 || H < 1 || E < 1 || E > 1024 || k < 1 || k > 32 || k > E) return SIMSD_ERR_SHAPE;
+  if (ld_topk < k + (extra_id >= 0 ? 1 : 0) || ld_topk > (1 << 20) || extra_id > 1024) return SIMSD_ERR_SHAPE;
   if (x_dtype < 0 || x_dtype > 2 || w_dtype < 0 || w_dtype > 2) return SIMSD_ERR_DTYPE;
   if (T == 0) return SIMSD_OK;
   if (!x || !wr || !topk_ids || !topk_weight) return SIMSD_ERR_SHAPE;
@@ -867,6 +875,8 @@ int simsd_moe_route(const void* x, int64_t ldx, int x_dtype, const void* wr, int
   a.w_dtype = w_dtype;
   a.renorm = renorm;
   a.scale = scale;
+  a.ldo = (int)ld_topk;
+  a.extra_id = extra_id;
   const int dev = current_device();
   if (dev < 0) return SIMSD_ERR_DEVICE;
   auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
@@ -1029,11 +1039,38 @@ size_t simsd_moe_workspace_size(int T, int k, int E, int H, int I, int dtype) {
   return plan_moe(T, k, E, H, I, dtype, sms, dtype != SIMSD_F32).total;
 }
 
+static int moe_dispatch_impl(const void* x, int64_t ldx, const int64_t* topk_ids, const float* topk_weight,
+                             const void* w_gate, const void* w_up, int64_t ldg_e, int64_t ldg_i, const void* w_down,
+                             int64_t ldd_e, int64_t ldd_h, void* out, int64_t ld_out, const void* add,
+                             int64_t ld_add, int T, int k, int E, int H, int I, int dtype, void* workspace,
+                             size_t workspace_bytes, void* stream, int shared_last);
+
 int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, const float* topk_weight,
                        const void* w_gate, const void* w_up, int64_t ldg_e, int64_t ldg_i, const void* w_down,
                        int64_t ldd_e, int64_t ldd_h, void* out, int64_t ld_out, const void* add, int64_t ld_add,
                        int T, int k, int E, int H, int I, int dtype, void* workspace, size_t workspace_bytes,
                        void* stream) {
+  return moe_dispatch_impl(x, ldx, topk_ids, topk_weight, w_gate, w_up, ldg_e, ldg_i, w_down, ldd_e, ldd_h, out,
+                           ld_out, add, ld_add, T, k, E, H, I, dtype, workspace, workspace_bytes, stream, 0);
+}
+
+int simsd_moe_dispatch_shared_last(const void* x, int64_t ldx, const int64_t* topk_ids, const float* topk_weight,
+                                   const void* w_gate, const void* w_up, int64_t ldg_e, int64_t ldg_i,
+                                   const void* w_down, int64_t ldd_e, int64_t ldd_h, void* out, int64_t ld_out,
+                                   int T, int k, int E, int H, int I, int dtype, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+  if (k < 2) return SIMSD_ERR_SHAPE;
+  return moe_dispatch_impl(x, ldx, topk_ids, topk_weight, w_gate, w_up, ldg_e, ldg_i, w_down, ldd_e, ldd_h, out,
+                           ld_out, nullptr, 0, T, k, E, H, I, dtype, workspace, workspace_bytes, stream, 1);
+}
+
+// The dispatch; shared_last: column k-1 of every row is an always-on (shared)
+// expert whose output is added unweighted after the routed sum is rounded.
+static int moe_dispatch_impl(const void* x, int64_t ldx, const int64_t* topk_ids, const float* topk_weight,
+                             const void* w_gate, const void* w_up, int64_t ldg_e, int64_t ldg_i, const void* w_down,
+                             int64_t ldd_e, int64_t ldd_h, void* out, int64_t ld_out, const void* add,
+                             int64_t ld_add, int T, int k, int E, int H, int I, int dtype, void* workspace,
+                             size_t workspace_bytes, void* stream, int shared_last) {
   if (T < 0 || k < 1 || E < 1 || E > 1024 || H < 1 || I < 1) return SIMSD_ERR_SHAPE;
   if (dtype != SIMSD_BF16 && dtype != SIMSD_F16 && dtype != SIMSD_F32) return SIMSD_ERR_DTYPE;
   if (workspace == nullptr || workspace_bytes < (size_t)WS_COUNTER_BYTES) return SIMSD_ERR_WORKSPACE;
@@ -1188,11 +1225,11 @@ int simsd_moe_dispatch(const void* x, int64_t ldx, const int64_t* topk_ids, cons
   if (vec) {
     if (prefer_shared(combine_vec_kernel, dev, 6) != SIMSD_OK) return SIMSD_ERR_LAUNCH;
     return launch(combine_vec_kernel, dim3((unsigned)T), dim3(128), 0, s, (const void*)ys, (long long)H, (const int*)s2r,
-                  topk_weight, out, (long long)ld_out, add, (long long)ld_add, T, k, H, dtype);
+                  topk_weight, out, (long long)ld_out, add, (long long)ld_add, T, k, H, dtype, shared_last);
   }
   if (prefer_shared(combine_kernel, dev, 7) != SIMSD_OK) return SIMSD_ERR_LAUNCH;
   return launch(combine_kernel, dim3((unsigned)T), dim3(256), 0, s, (const void*)ys, (long long)H, (const int*)s2r,
-                topk_weight, out, (long long)ld_out, add, (long long)ld_add, T, k, H, dtype);
+                topk_weight, out, (long long)ld_out, add, (long long)ld_add, T, k, H, dtype, shared_last);
 }
 
 int simsd_moe_ep_plan(const int64_t* topk_ids, int S, int E, int world, int capacity, int32_t* send_slot,
@@ -1247,11 +1284,11 @@ int simsd_moe_combine(const void* ys, int64_t ldys, const int32_t* slot_row, con
   if (vec) {
     if (prefer_shared(combine_vec_kernel, dev, 6) != SIMSD_OK) return SIMSD_ERR_LAUNCH;
     return launch(combine_vec_kernel, dim3((unsigned)T), dim3(128), 0, s, ys, (long long)ldys, (const int*)slot_row,
-                  topk_weight, out, (long long)ld_out, add, (long long)ld_add, T, k, H, dtype);
+                  topk_weight, out, (long long)ld_out, add, (long long)ld_add, T, k, H, dtype, 0);
   }
   if (prefer_shared(combine_kernel, dev, 7) != SIMSD_OK) return SIMSD_ERR_LAUNCH;
   return launch(combine_kernel, dim3((unsigned)T), dim3(256), 0, s, ys, (long long)ldys, (const int*)slot_row,
-                topk_weight, out, (long long)ld_out, add, (long long)ld_add, T, k, H, dtype);
+                topk_weight, out, (long long)ld_out, add, (long long)ld_add, T, k, H, dtype, 0);
 }
 
 int simsd_ipc_alloc(size_t bytes, void** dev_ptr) {

@@ -70,6 +70,8 @@ struct RouteArgs {
   int x_dtype, w_dtype;   // 0 bf16, 1 fp16, 2 fp32
   int renorm;
   float scale;
+  int ldo;                // row stride of topk_ids / topk_weight (>= k)
+  int extra_id;           // >= 0: column k of every row gets this id with weight 1 (an always-on expert)
 };
 
 constexpr int ROUTE_TOK = 16;    // tokens per CTA
@@ -159,8 +161,12 @@ __device__ __forceinline__ void route_topk_nc(const RouteArgs& p, const float* s
       float wj = my_w;
       if (norm) wj = __fdiv_rn(wj, denom);
       wj = __fmul_rn(wj, p.scale);
-      p.topk_ids[(long long)(t0 + t) * p.k + lane] = my_id;
-      p.topk_weight[(long long)(t0 + t) * p.k + lane] = wj;
+      p.topk_ids[(long long)(t0 + t) * p.ldo + lane] = my_id;
+      p.topk_weight[(long long)(t0 + t) * p.ldo + lane] = wj;
+    }
+    if (p.extra_id >= 0 && lane == 0) {
+      p.topk_ids[(long long)(t0 + t) * p.ldo + p.k] = p.extra_id;
+      p.topk_weight[(long long)(t0 + t) * p.ldo + p.k] = 1.0f;
     }
     __syncwarp();
   }
@@ -678,18 +684,29 @@ __global__ void gather_rows_kernel(const void* x, long long ldx, const int* sort
 // output) the result is cast(fp32(cast(sum)) + fp32(add[t, h])), i.e. the
 // x.dtype addition `moe_out + shared_out`.
 __global__ void combine_kernel(const void* ys, long long ldys, const int* slot_to_row, const float* w, void* out,
-                               long long ld_out, const void* add, long long ld_add, int T, int k, int H, int dtype) {
+                               long long ld_out, const void* add, long long ld_add, int T, int k, int H, int dtype,
+                               int shared_last) {
   griddep_launch_dependents();
   griddep_wait();
   const int t = blockIdx.x;
   if (t >= T) return;
+  const int kr = shared_last ? k - 1 : k;
   for (int h = threadIdx.x; h < H; h += blockDim.x) {
     float acc = 0.0f;
-    for (int j = 0; j < k; ++j) {
+    for (int j = 0; j < kr; ++j) {
       const int row = slot_to_row[(long long)t * k + j];
       if (row < 0) continue;
       const float y = load_f(ys, (long long)row * ldys + h, dtype);
       acc = __fadd_rn(acc, __fmul_rn(y, w[(long long)t * k + j]));
+    }
+    if (shared_last) {
+      const int row = slot_to_row[(long long)t * k + k - 1];
+      if (row >= 0) {
+        float r = acc;
+        if (dtype == 0) r = __bfloat162float(__float2bfloat16_rn(acc));
+        else if (dtype == 1) r = __half2float(__float2half_rn(acc));
+        acc = __fadd_rn(r, load_f(ys, (long long)row * ldys + h, dtype));
+      }
     }
     if (add) {
       float r = acc;
@@ -722,9 +739,11 @@ __device__ __forceinline__ float round_to_dtype(float v, int dtype) {
   return dtype == 0 ? __bfloat162float(__float2bfloat16_rn(v)) : __half2float(__float2half_rn(v));
 }
 
+// shared_last: column k-1 is an always-on (shared) expert, added unweighted to
+// the rounded sum of the other columns, as `add` is.
 __global__ void combine_vec_kernel(const void* ys, long long ldys, const int* slot_to_row, const float* w, void* out,
                                    long long ld_out, const void* add, long long ld_add, int T, int k, int H,
-                                   int dtype) {
+                                   int dtype, int shared_last) {
   griddep_launch_dependents();
   griddep_wait();
   __shared__ int s_row[32];
@@ -741,7 +760,8 @@ __global__ void combine_vec_kernel(const void* ys, long long ldys, const int* sl
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-    for (int j = 0; j < k; ++j) {
+    const int kr = shared_last ? k - 1 : k;
+    for (int j = 0; j < kr; ++j) {
       const int row = s_row[j];
       if (row < 0) continue;
       float y[8];
@@ -749,6 +769,12 @@ __global__ void combine_vec_kernel(const void* ys, long long ldys, const int* sl
       const float wj = s_w[j];
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], __fmul_rn(y[i], wj));
+    }
+    if (shared_last && s_row[k - 1] >= 0) {
+      float a[8];
+      unpack8(*reinterpret_cast<const uint4*>(yb + (long long)s_row[k - 1] * ldys + h8 * 8), dtype, a);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(round_to_dtype(acc[i], dtype), a[i]);
     }
     if (add) {
       float a[8];

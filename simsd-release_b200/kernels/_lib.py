@@ -59,9 +59,11 @@ SIGNATURES: dict[str, tuple] = {
     "simsd_thin_linear": (_I, [_P, _L, _L, _P, _L, _L, _P, _P, _P, _L, _I, _I, _I, _I, _I, _I, _I,
                                _P, _S, _P]),
     "simsd_thin_linear_noalloc": (_I, [_P, _L, _L, _P, _L, _L, _P, _P, _P, _L, _I, _I, _I, _I, _I, _P]),
+    "simsd_moe_route_ex": (_I, [_P, _L, _I, _P, _L, _I, _P, _I, _I, _I, _I, _I, _F, _P, _P, _L, _I, _P, _P]),
     "simsd_moe_route": (_I, [_P, _L, _I, _P, _L, _I, _P, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P]),
     "simsd_moe_align": (_I, [_P, _I, _I, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P]),
     "simsd_moe_workspace_size": (_S, [_I, _I, _I, _I, _I, _I]),
+    "simsd_moe_dispatch_shared_last": (_I, [_P, _L, _P, _P, _P, _P, _L, _L, _P, _L, _L, _P, _L, _I, _I, _I, _I, _I, _I, _P, _S, _P]),
     "simsd_moe_dispatch": (_I, [_P, _L, _P, _P, _P, _P, _L, _L, _P, _L, _L, _P, _L, _P, _L, _I, _I,
                                 _I, _I, _I, _I, _P, _S, _P]),
     "simsd_ipc_alloc": (_I, [_S, ctypes.POINTER(_P)]),

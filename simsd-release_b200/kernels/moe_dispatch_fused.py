@@ -85,12 +85,14 @@ def _align(topk_ids: torch.Tensor, E: int, num_tiles: int):
 
 def moe_route(x: torch.Tensor, w_router: torch.Tensor, bias: torch.Tensor | None = None,
               k: int = 8, renorm: bool = True, scale: float = 1.0,
-              return_logits: bool = False):
+              return_logits: bool = False, extra_expert: int | None = None):
     """Top-k sigmoid router: (topk_ids [T,k] int64, topk_weight [T,k] fp32[, logits [T,E] fp32]).
 
     score = sigmoid(x . w_router^T) in fp32; experts chosen by score + bias
     (ties to the lower id); weights = chosen scores, renormalised (+1e-20) when
     `renorm` and k > 1, then times `scale` (the routed scaling factor).
+    `extra_expert` (an id): a (k+1)-th column of that id with weight 1 is
+    appended to every row (the always-on shared expert of moe_layer).
     """
     if x.ndim != 2 or w_router.ndim != 2 or x.shape[1] != w_router.shape[1]:
         raise ValueError(f"x [T,H] and w_router [E,H] expected, got {tuple(x.shape)} / {tuple(w_router.shape)}")
@@ -107,28 +109,33 @@ def moe_route(x: torch.Tensor, w_router: torch.Tensor, bias: torch.Tensor | None
         x = x.contiguous()
     if w_router.stride(1) != 1:
         w_router = w_router.contiguous()
-    ids = torch.empty((T, k), dtype=torch.int64, device=dev)
-    wts = torch.empty((T, k), dtype=torch.float32, device=dev)
+    kc = k + (1 if extra_expert is not None else 0)
+    ids = torch.empty((T, kc), dtype=torch.int64, device=dev)
+    wts = torch.empty((T, kc), dtype=torch.float32, device=dev)
     # always handed to the library: with few tokens it splits the experts over
     # blocks and passes the logits through this buffer to its top-k kernel
     logits = torch.empty((T, E), dtype=torch.float32, device=dev)
     with _lib.device_guard(dev):
-        rc = _lib.lib().simsd_moe_route(
+        rc = _lib.lib().simsd_moe_route_ex(
             x.data_ptr(), x.stride(0), _lib.dtype_code(x.dtype),
             w_router.data_ptr(), w_router.stride(0), _lib.dtype_code(w_router.dtype),
             bias.data_ptr() if bias is not None else None, T, H, E, k, int(bool(renorm)),
-            ctypes.c_float(scale), ids.data_ptr(), wts.data_ptr(),
-            logits.data_ptr(), _lib.stream_ptr(dev))
+            ctypes.c_float(scale), ids.data_ptr(), wts.data_ptr(), kc,
+            -1 if extra_expert is None else int(extra_expert), logits.data_ptr(), _lib.stream_ptr(dev))
     _lib.check(rc, "moe_route")
     return (ids, wts, logits) if return_logits else (ids, wts)
 
 
-def moe_dispatch(x, topk_ids, topk_weight, w_gate, w_up, w_down, add=None):
+def moe_dispatch(x, topk_ids, topk_weight, w_gate, w_up, w_down, add=None, shared_last: bool = False):
     """Drop-in for ``LLaDA2MoeSparseMoeBlock.moe_infer`` on stacked weights.
 
     x (T, H); topk_ids (T, k) int64; topk_weight (T, k) fp32;
     w_gate/w_up (E, I, H); w_down (E, H, I) -> (T, H) in x.dtype.
     `add` (T, H), optional: added in x.dtype after the combine (shared expert).
+    `shared_last`: the last column of topk_ids names a shared expert stacked
+    with the routed ones (moe_route(..., extra_expert=E)); its output is added
+    unweighted after the routed sum is rounded, as `add` would be, but it runs
+    inside the same grouped GEMMs.
     """
     if x.ndim != 2 or topk_ids.ndim != 2 or topk_weight.shape != topk_ids.shape:
         raise ValueError("x (T,H), topk_ids (T,k) and topk_weight (T,k) expected")
@@ -167,6 +174,18 @@ def moe_dispatch(x, topk_ids, topk_weight, w_gate, w_up, w_down, add=None):
         if add.stride(1) != 1:
             add = add.contiguous()
     L = _lib.lib()
+    if shared_last:
+        if add is not None or k < 2:
+            raise ValueError("shared_last takes no `add` and needs at least one routed column")
+        with _lib.device_guard(dev):
+            ws = _lib.workspace(dev, L.simsd_moe_workspace_size(T, k, E, H, I, code))
+            rc = L.simsd_moe_dispatch_shared_last(
+                x.data_ptr(), x.stride(0), ids.data_ptr(), wts.data_ptr(),
+                w_gate.data_ptr(), w_up.data_ptr(), w_gate.stride(0), w_gate.stride(1),
+                w_down.data_ptr(), w_down.stride(0), w_down.stride(1), out.data_ptr(), out.stride(0),
+                T, k, E, H, I, code, ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
+        _lib.check(rc, "moe_dispatch")
+        return out
     with _lib.device_guard(dev):
         nbytes = L.simsd_moe_workspace_size(T, k, E, H, I, code)
         ws = _lib.workspace(dev, nbytes)
@@ -181,8 +200,17 @@ def moe_dispatch(x, topk_ids, topk_weight, w_gate, w_up, w_down, add=None):
     return out
 
 
+def stack_shared_expert(w_gate, w_up, w_down, shared: tuple):
+    """The routed experts' stacked weights with the shared expert (w_gate_s,
+    w_up_s, w_down_s) appended as expert E (a copy, made once at install time),
+    for moe_layer(..., shared_stacked=True)."""
+    sg, su, sd = shared
+    return (torch.cat([w_gate, sg[None]]), torch.cat([w_up, su[None]]), torch.cat([w_down, sd[None]]))
+
+
 def moe_layer(x, w_router, router_bias, k, w_gate, w_up, w_down,
-              shared: tuple | None = None, renorm: bool = True, scale: float = 1.0):
+              shared: tuple | None = None, renorm: bool = True, scale: float = 1.0,
+              shared_stacked: bool = False):
     """Router + routed experts + optional shared expert (w_gate_s, w_up_s, w_down_s).
 
     The shared expert is the dense SwiGLU `down(silu(gate(x)) * up(x))`, run as
@@ -193,6 +221,15 @@ def moe_layer(x, w_router, router_bias, k, w_gate, w_up, w_down,
     for it before the dispatch.  Both orders of work are graph-capturable.
     """
     from .thin_linear_fused import thin_linear, thin_linear_silu_mul
+    if shared_stacked:
+        # the shared expert is expert E of the stacked weights (stack_shared_expert):
+        # the router adds it as an always-on last column and it runs in the
+        # dispatch's grouped GEMMs with the routed experts
+        E = w_router.shape[0]
+        if w_gate.shape[0] != E + 1:
+            raise ValueError(f"shared_stacked: {E} routed experts + 1 shared expected, got {w_gate.shape[0]}")
+        ids, wts = moe_route(x, w_router, router_bias, k=k, renorm=renorm, scale=scale, extra_expert=E)
+        return moe_dispatch(x, ids, wts, w_gate, w_up, w_down, shared_last=True)
     add = None
     if shared is not None:
         sg, su, sd = shared

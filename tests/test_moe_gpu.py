@@ -396,3 +396,43 @@ def test_programmatic_dependent_launch_moe_chain_is_exact():
 
 def test_no_device_errors_recorded():
     assert _lib.device_error(torch.device(DEV, torch.cuda.current_device())) == 0
+
+
+# ------------------------------------------------------------------ stacked shared expert
+def test_route_extra_column_for_the_shared_expert():
+    T, H, E, k = 100, 512, 64, 6
+    g = torch.Generator(device=DEV).manual_seed(71)
+    x = torch.randn(T, H, device=DEV, generator=g).to(torch.bfloat16)
+    wr = (torch.randn(E, H, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+    b = torch.randn(E, device=DEV, generator=g) * 0.1
+    with torch.inference_mode():
+        ids, w = moe_route(x, wr, b, k=k)
+        ids2, w2 = moe_route(x, wr, b, k=k, extra_expert=E)
+    assert ids2.shape == (T, k + 1)
+    assert torch.equal(ids2[:, :k], ids) and torch.equal(w2[:, :k], w)
+    assert bool((ids2[:, k] == E).all()) and bool((w2[:, k] == 1.0).all())
+
+
+@pytest.mark.parametrize("T", [16, 256, 1024])
+def test_moe_layer_with_stacked_shared_expert(T):
+    """The shared expert stacked as expert E (one set of grouped GEMMs) against
+    the separate shared-expert launches: the same layer to within the bf16
+    rounding of the shared expert's own output."""
+    from kernels.moe_dispatch_fused import moe_layer, stack_shared_expert
+    H, E, k, I = 2048, 256, 8, 512
+    g = torch.Generator(device=DEV).manual_seed(T + 81)
+    bf = torch.bfloat16
+    x = torch.randn(T, H, device=DEV, generator=g).to(bf)
+    wr = (torch.randn(E, H, device=DEV, generator=g) * 0.02).to(bf)
+    b = torch.randn(E, device=DEV, generator=g) * 0.1
+    wg, wu, wd = experts(E, H, I, bf, seed=T + 82)
+    shared = tuple((torch.randn(*sh, device=DEV, generator=g) * 0.02).to(bf) for sh in ((I, H), (I, H), (H, I)))
+    with torch.inference_mode():
+        ref = moe_layer(x, wr, b, k, wg, wu, wd, shared=shared)
+        st = stack_shared_expert(wg, wu, wd, shared)
+        got = moe_layer(x, wr, b, k, *st, shared_stacked=True)
+        got2 = moe_layer(x, wr, b, k, *st, shared_stacked=True)
+    torch.cuda.synchronize()
+    assert torch.equal(got, got2)
+    err = float((got.float() - ref.float()).abs().max())
+    assert err <= 2 ** -7 * float(ref.float().abs().max()) + 1e-3, err
