@@ -377,6 +377,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
         for (int r = 0; r < p.world; ++r) store_f(p.peer_out[r], t * p.ld_out + p.col_offset + col, v, odt);
       }
     };
+    // Owner sums (step 5): thread `row` takes the owned unit (row, or gate/up
+    // pair) ep_l for activation-row groups ep_g0, ep_g0 + ep_P, ... (4 rows a
+    // group); fixed for the launch, so no division per tile.
+    constexpr int EP_JMAX = BMAX / 8;   // groups per thread: BMAX / 4 groups, >= 2 threads per unit
+    constexpr int EP_JC = EP_JMAX < 4 ? EP_JMAX : 4;   // groups summed at once (registers)
+    const int ep_units = S > 1 ? (p.silu ? ro.rows_of(q) / 2 : ro.rows_of(q)) : 0;
+    const int ep_P = ep_units > 0 ? 128 / ep_units : 0;
+    const int ep_l = ep_units > 0 ? row % ep_units : 0;
+    const int ep_g0 = ep_units > 0 ? row / ep_units : 0;
+    const int ep_groups = (nrows_all + 3) >> 2;
+    const bool ep_active = ep_units > 0 && ep_g0 < ep_P;
+    const bool ep_fast = p.amax_keys == nullptr && p.world <= 1;   // plain stores into y
+    const long long ep_ld = p.ld_out;
+    const int ep_silu = p.silu;
+    const int ep_rows_out = p.rows_out;
     int done = 0;
     for (int i = 0; i < n_tiles; ++i) {
       const int rtile = tile_of(i);
@@ -464,6 +479,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
       }
       tc_fence_before();
       mbar_arrive(smem_u32(&acce_bar[a]));
+      const int ep_col = out_col0 + q * ro.per + ep_l;
+      const float ep_bias =
+          (ep_active && !ep_silu && p.bias && ep_col < ep_rows_out) ? load_f(p.bias, ep_col, odt) : 0.0f;
       // -- 4. every peer's rows for this CTA have landed
       if (!named_bar_and(1, 128, mbar_wait_cluster(red_full_u32, i & 1, abort_flag, p.err))) break;
       // -- 5. park this CTA's own rows in its (otherwise unused) slot, then all
@@ -482,43 +500,58 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
       }
       named_bar_sync(1, 128);
       {
-        // owned rows (plain) or pairs (silu), in the slot's local order; each
-        // thread takes one unit and 4 consecutive activation rows (one 16-byte
-        // group of every slot), consecutive threads consecutive columns
-        const int units = p.silu ? ro.rows_of(q) / 2 : ro.rows_of(q);
-        const int first = q * ro.per;   // first owned row (plain) or pair (silu)
-        const int groups = (nrows_all + 3) >> 2;
-        auto slot4 = [&](int r, int l, int g) -> float4 {
-          return reinterpret_cast<const float4*>(red + ((r * slot_rows) + l) * BMAX)[swz(l, g)];
-        };
-        for (int e = row; e < units * groups; e += 128) {
-          const int g = e / units;
-          const int l = e - g * units;
-          const int col = (p.silu ? rtile * 64 : rtile * 128) + first + l;
-          if (col >= p.rows_out) continue;
-          float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f), b = a;
-          for (int r = 0; r < S; ++r) {
-            const float4 f = slot4(r, l, g);
-            a.x = __fadd_rn(a.x, f.x);
-            a.y = __fadd_rn(a.y, f.y);
-            a.z = __fadd_rn(a.z, f.z);
-            a.w = __fadd_rn(a.w, f.w);
-            if (p.silu) {
-              const float4 h = slot4(r, ro.per + l, g);
-              b.x = __fadd_rn(b.x, h.x);
-              b.y = __fadd_rn(b.y, h.y);
-              b.z = __fadd_rn(b.z, h.z);
-              b.w = __fadd_rn(b.w, h.w);
-            }
-          }
-          const float va[4] = {a.x, a.y, a.z, a.w};
-          const float vb[4] = {b.x, b.y, b.z, b.w};
-          const float bv = (!p.silu && p.bias) ? load_f(p.bias, col, odt) : 0.0f;
+        // Each thread sums its unit's outputs for up to EP_JMAX groups over the
+        // S slots in rank (= K) order.  Group indices are clamped so every slot
+        // load is in range and none waits on a branch (all loads of a slot are
+        // independent); only the stores are predicated.
+        if (ep_active && ep_col < ep_rows_out) {
+          auto slot4 = [&](int r, int l, int g) -> float4 {
+            return reinterpret_cast<const float4*>(red + ((r * slot_rows) + l) * BMAX)[swz(l, g)];
+          };
+          uint16_t* const yc = reinterpret_cast<uint16_t*>(outp) + ep_col;
+#pragma unroll 1
+          for (int jc = 0; jc < EP_JMAX; jc += EP_JC) {
+            if (ep_g0 + jc * ep_P >= ep_groups) break;
+            float4 a[EP_JC], b[EP_JC];
 #pragma unroll
-          for (int k4 = 0; k4 < 4; ++k4) {
-            const int t = 4 * g + k4;
-            if (t < nrows_all)
-              put(t, col, p.silu ? silu_mul(va[k4], vb[k4]) : __fadd_rn(va[k4], bv));
+            for (int j = 0; j < EP_JC; ++j) a[j] = b[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+            for (int r = 0; r < TC_CL_MAX; ++r) {
+              if (r >= S) break;
+#pragma unroll
+              for (int j = 0; j < EP_JC; ++j) {
+                const int g = min(ep_g0 + (jc + j) * ep_P, ep_groups - 1);
+                const float4 f = slot4(r, ep_l, g);
+                a[j].x = __fadd_rn(a[j].x, f.x);
+                a[j].y = __fadd_rn(a[j].y, f.y);
+                a[j].z = __fadd_rn(a[j].z, f.z);
+                a[j].w = __fadd_rn(a[j].w, f.w);
+                if (ep_silu) {
+                  const float4 h = slot4(r, ro.per + ep_l, g);
+                  b[j].x = __fadd_rn(b[j].x, h.x);
+                  b[j].y = __fadd_rn(b[j].y, h.y);
+                  b[j].z = __fadd_rn(b[j].z, h.z);
+                  b[j].w = __fadd_rn(b[j].w, h.w);
+                }
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < EP_JC; ++j) {
+              const int g = ep_g0 + (jc + j) * ep_P;
+              if (g < ep_groups) {
+                const float va[4] = {a[j].x, a[j].y, a[j].z, a[j].w};
+                const float vb[4] = {b[j].x, b[j].y, b[j].z, b[j].w};
+#pragma unroll
+                for (int k4 = 0; k4 < 4; ++k4) {
+                  const int t = 4 * g + k4;
+                  if (t < nrows_all) {
+                    const float v = ep_silu ? silu_mul(va[k4], vb[k4]) : __fadd_rn(va[k4], ep_bias);
+                    if (ep_fast) yc[(long long)t * ep_ld] = f32_to_16bit(v, odt);
+                    else put(t, ep_col, v);
+                  }
+                }
+              }
+            }
           }
         }
       }
