@@ -263,6 +263,21 @@ def test_silu_mul_epilogue():
     assert_oracle(x, wg, got, silu_up=wu)
 
 
+@pytest.mark.parametrize("M", [4, 16, 64])
+def test_silu_mul_single_k_block(M):
+    """K = 64 is one K block, so every cluster is a single CTA (whole tiles) and
+    the gate and up rows meet through the staging rows of the epilogue; N = 1000
+    leaves a ragged last tile."""
+    x = rnd(M, 64, seed=60 + M)
+    wg, wu = rnd(1000, 64, scale=0.02, seed=61), rnd(1000, 64, scale=0.02, seed=62)
+    with torch.inference_mode():
+        got = thin_linear_silu_mul(x, wg, wu)
+        ref32 = F.silu(F.linear(x.float(), wg.float())) * F.linear(x.float(), wu.float())
+    assert got.shape == (M, 1000)
+    assert float((got.float() - ref32).abs().max()) <= 2 ** -7 * float(ref32.abs().max()) + 1e-3
+    assert_oracle(x, wg, got, silu_up=wu)
+
+
 @pytest.mark.parametrize("M", [4, 32, 64])
 def test_silu_mul_sdar8b(M):
     x = rnd(M, 4096, seed=50 + M)
