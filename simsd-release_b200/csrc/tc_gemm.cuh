@@ -575,14 +575,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
 #pragma unroll
             for (int j = 0; j < 16; ++j) sb[j * 128 + row] = f32_to_16bit(__fadd_rn(v[j], bv), odt);
           } else {
-            if (row >= 64) {
+            // gate row i (thread i) and up row i (thread 64 + i) meet through
+            // xbuf; thread i computes activation rows 0-7 of pair i and thread
+            // 64 + i rows 8-15, so all four warps share the SiLU*mul work
+            float* xg = xbuf;            // [8][64] gate values of rows 8-15
+            float* xu = xbuf + 8 * 64;   // [8][64] up values of rows 0-7
+            const int pr = row & 63;
+            if (row < 64) {
 #pragma unroll
-              for (int j = 0; j < 16; ++j) xbuf[j * 64 + (row - 64)] = v[j];
+              for (int j = 0; j < 8; ++j) xg[j * 64 + pr] = v[8 + j];
+            } else {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) xu[j * 64 + pr] = v[j];
             }
             named_bar_sync(1, 128);
             if (row < 64) {
 #pragma unroll
-              for (int j = 0; j < 16; ++j) sb[j * 64 + row] = f32_to_16bit(silu_mul(v[j], xbuf[j * 64 + row]), odt);
+              for (int j = 0; j < 8; ++j) sb[j * 64 + pr] = f32_to_16bit(silu_mul(v[j], xu[j * 64 + pr]), odt);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                sb[(8 + j) * 64 + pr] = f32_to_16bit(silu_mul(xg[j * 64 + pr], v[8 + j]), odt);
             }
           }
           named_bar_sync(1, 128);
