@@ -379,16 +379,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
   const int c = blockIdx.x;
   const SkSplit sk(iters, G > 0 ? G : 1);
   int it_begin = 0, it_end = 0;
+  int tstride = 1;   // tiles between one tile of this CTA and its next
   if (tc_whole_tiles(p.group_counts != nullptr, (int)total_tiles, (int)gridDim.x)) {
-    // grouped GEMM with at least two tiles per CTA: whole tiles, balanced by
-    // count — no split tile, so no partials and nothing for the fixup
-    const SkSplit ts((int)total_tiles, (int)gridDim.x);
-    it_begin = ts.start(c) * kb;
-    it_end = ts.start(c + 1) * kb;
+    // grouped GEMM with at least two tiles per CTA: whole tiles dealt round
+    // robin (tile c, c + grid, ...) — no split tile, so no partials and nothing
+    // for the fixup.  Dealing rather than cutting contiguous runs spreads the
+    // tall row chunks of a busy group (the shared expert is the last group) over
+    // all CTAs, and the row chunks that share a weight tile run at the same time
+    // on neighbouring CTAs, so the weight tile still streams from HBM once.
+    it_begin = c * kb;
+    it_end = (int)total_tiles * kb;
+    tstride = (int)gridDim.x;
   } else if (c < G) {
     it_begin = sk.start(c);
     it_end = sk.start(c + 1);
   }
+  // the iteration after tile `tile` whose K blocks end at kb1: the rest of a
+  // split range, or the first K block of this CTA's next tile
+  auto next_it = [&](int tile, int kb1) -> int {
+    if (kb1 < kb) return tile * kb + kb1;
+    const long long nx = (long long)(tile + tstride) * kb;
+    return nx < it_end ? (int)nx : it_end;
+  };
 
   if (warp == 4) {
     // ================= TMA producer
@@ -466,7 +478,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
-        it = tile * kb + kb1;
+        it = next_it(tile, kb1);
       }
       // fewer iterations than ring stages, or aborting with weight-only stages
       // armed: their activation boxes still have to land
@@ -518,7 +530,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         if (!ok) break;
         tc_commit(smem_u32(&accf_bar[a]));
         ++acc_iter;
-        it = tile * kb + kb1;
+        it = next_it(tile, kb1);
       }
       if (p.trace) p.trace[blockIdx.x * 8 + 5] = globaltimer_ns();
       if (!ok && issued_any) {
@@ -655,7 +667,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         }
       }
       ++acc_iter;
-      it = tile * kb + kb1;
+      it = next_it(tile, kb1);
     }
   }
 
