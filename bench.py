@@ -798,7 +798,8 @@ def profile_sweep(args):
 
 
 def profile_moe(args):
-    """A few MoE layers at T = --profile-moe (for ncu captures on a small case)."""
+    """A few MoE layers at T = --profile-moe, shared expert stacked as expert E
+    (for ncu captures on a small case)."""
     from kernels.moe_dispatch_fused import moe_layer
     dev = torch.device("cuda", 0)
     H, E, k, I = MOE["H"], MOE["E"], MOE["k"], MOE["I"]
@@ -806,11 +807,13 @@ def profile_moe(args):
     bf = torch.bfloat16
     wr = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(bf)
     bias = torch.randn(E, generator=g, device=dev) * MOE["bias_std"]
-    ws = tuple((torch.randn(*sh, generator=g, device=dev) * 0.02).to(bf) for sh in ((E, I, H), (E, I, H), (E, H, I)))
+    # the routed experts and the shared expert stacked as expert E, as the bench's MoE leg runs them
+    ws = tuple((torch.randn(*sh, generator=g, device=dev) * 0.02).to(bf)
+               for sh in ((E + 1, I, H), (E + 1, I, H), (E + 1, H, I)))
     x = torch.randn(args.profile_moe, H, generator=g, device=dev).to(bf)
     with torch.inference_mode():
         for _ in range(args.profile_launches + 1):
-            y = moe_layer(x, wr, bias, k, *ws)
+            y = moe_layer(x, wr, bias, k, *ws, shared_stacked=True)
         torch.cuda.synchronize()
     print(f"profile MoE layer T={args.profile_moe}: out {tuple(y.shape)}")
 
