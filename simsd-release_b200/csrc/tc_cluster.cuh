@@ -460,25 +460,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
       // 16-byte column group j of a received row sits at group swz(j): the XOR
       // spreads the rows that one quarter-warp touches over all 32 banks
       const uint32_t dst_bar = mapa_shared(red_full_u32, (uint32_t)own);
-      // every chunk into registers with one wait, the TMEM buffer back to the
-      // MMA warp, then the rows this CTA does not own to their owners
 #pragma unroll
-      for (int ch = 0; ch < BMAX / 16; ++ch)
-        if (ch < nb) tmem_ld16(t_base + ch * 16, *reinterpret_cast<float(*)[16]>(&mine[ch * 16]));
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(smem_u32(&acce_bar[a]));
-      if (own != q) {
+      for (int ch = 0; ch < BMAX / 16; ++ch) {
+        if (ch < nb) {
+          float v[16];
+          tmem_ld16(t_base + ch * 16, v);
+          tmem_wait_ld();
+          if (own == q) {
 #pragma unroll
-        for (int ch = 0; ch < BMAX / 16; ++ch) {
-          if (ch < nb) {
+            for (int j = 0; j < 16; ++j) mine[ch * 16 + j] = v[j];
+          } else {
 #pragma unroll
             for (int u = 0; u < 4; ++u)
-              st_async_v4(dst_row + (uint32_t)(swz(lr, ch * 4 + u) * 16), mine[ch * 16 + 4 * u],
-                          mine[ch * 16 + 4 * u + 1], mine[ch * 16 + 4 * u + 2], mine[ch * 16 + 4 * u + 3], dst_bar);
+              st_async_v4(dst_row + (uint32_t)(swz(lr, ch * 4 + u) * 16), v[4 * u], v[4 * u + 1], v[4 * u + 2],
+                          v[4 * u + 3], dst_bar);
           }
         }
       }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&acce_bar[a]));
       const int ep_col = out_col0 + q * ro.per + ep_l;
       const float ep_bias =
           (ep_active && !ep_silu && p.bias && ep_col < ep_rows_out) ? load_f(p.bias, ep_col, odt) : 0.0f;
