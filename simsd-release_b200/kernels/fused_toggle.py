@@ -32,27 +32,28 @@ import torch.nn as nn
 from ._lib import reset_workspace
 from .thin_linear_fused import ThinLinear, should_fuse, thin_linear_cat, thin_linear_silu_mul
 
-DEFAULT_TARGETS = (
-    "q_proj", "k_proj", "v_proj", "o_proj",
-    "gate_proj", "up_proj", "down_proj",
-)
-ALL_TARGETS = DEFAULT_TARGETS + ("lm_head",)
+# Projection names swapped by default: every linear of an SDAR/LLaDA2 decoder
+# layer.  The vocabulary projection is opt-in (ALL_TARGETS): with ~150 k output
+# rows cuBLAS already fills the GPU there.
+_LAYER_PROJECTIONS = ("q", "k", "v", "o", "gate", "up", "down")
+DEFAULT_TARGETS = tuple(f"{p}_proj" for p in _LAYER_PROJECTIONS)
+ALL_TARGETS = (*DEFAULT_TARGETS, "lm_head")
 
-_ORIGINALS: dict[int, dict[str, nn.Module]] = {}
+# id(model) -> {dotted path: (owning module, attribute, original nn.Linear)}
+_ORIGINALS: dict[int, dict[str, tuple[nn.Module, str, nn.Linear]]] = {}
 _MLP_PATCHED: dict[int, list[nn.Module]] = {}
 
 
-def _iter_targets(model: nn.Module, targets):
-    for name, mod in model.named_modules():
-        leaf = name.rsplit(".", 1)[-1]
-        if leaf in targets and isinstance(mod, nn.Linear):
-            yield name, mod
-
-
-def _set_submodule(model: nn.Module, qualified: str, new: nn.Module) -> None:
-    parent_path, _, leaf = qualified.rpartition(".")
-    parent = model.get_submodule(parent_path) if parent_path else model
-    setattr(parent, leaf, new)
+def _linear_slots(root: nn.Module, wanted, prefix: str = ""):
+    """Depth-first (path, owner, attribute, linear) for every nn.Linear child
+    whose attribute name is in `wanted`; the swap replaces owner.attribute."""
+    for attr, child in root.named_children():
+        path = f"{prefix}.{attr}" if prefix else attr
+        if isinstance(child, nn.Linear):
+            if attr in wanted:
+                yield path, root, attr, child
+        else:
+            yield from _linear_slots(child, wanted, path)
 
 
 def _is_silu(act) -> bool:
@@ -129,7 +130,7 @@ def _merge_qkv(model: nn.Module, saved: dict[str, nn.Module], config) -> None:
             continue
         share = _QKVShare()
         for i, (attr, path) in enumerate(zip(("q_proj", "k_proj", "v_proj"), paths)):
-            new = _QKVPart(saved[path], share, i, config=config)
+            new = _QKVPart(saved[path][2], share, i, config=config)
             share.parts.append(new)
             setattr(mod, attr, new)
 
@@ -150,17 +151,17 @@ def apply_to_model(model: nn.Module, enable: bool = True,
             mod.__dict__.pop("forward", None)
         if not saved:
             return 0
-        for path, orig in saved.items():
-            _set_submodule(model, path, orig)
+        for owner, attr, orig in saved.values():
+            setattr(owner, attr, orig)
         reset_workspace()
         return len(saved)
 
     if key in _ORIGINALS:
         return 0
-    saved: dict[str, nn.Module] = {}
-    for path, mod in list(_iter_targets(model, targets)):
-        saved[path] = mod
-        _set_submodule(model, path, ThinLinear(mod, config=config))
+    wanted = frozenset(targets)
+    saved = {path: (owner, attr, lin) for path, owner, attr, lin in _linear_slots(model, wanted)}
+    for owner, attr, lin in saved.values():
+        setattr(owner, attr, ThinLinear(lin, config=config))
     if saved:
         _ORIGINALS[key] = saved
         if fuse_gate_up:

@@ -266,13 +266,15 @@ def stack_expert_weights(experts, free_originals: bool = True):
 
 
 class FusedMoEDispatch(torch.nn.Module):
-    """nn.Module form of `moe_dispatch` holding the stacked expert weights."""
+    """Holds one layer's stacked expert weights (non-persistent buffers, so
+    checkpoints are unaffected) and applies `moe_dispatch` with them to the
+    routing it is given."""
 
     def __init__(self, w_gate, w_up, w_down):
         super().__init__()
-        self.register_buffer("w_gate", w_gate, persistent=False)
-        self.register_buffer("w_up", w_up, persistent=False)
-        self.register_buffer("w_down", w_down, persistent=False)
+        for name, t in (("w_gate", w_gate), ("w_up", w_up), ("w_down", w_down)):
+            self.register_buffer(name, t, persistent=False)
 
     def forward(self, x, topk_ids, topk_weight):
-        return moe_dispatch(x, topk_ids, topk_weight, self.w_gate, self.w_up, self.w_down)
+        packed = (self.w_gate, self.w_up, self.w_down)
+        return moe_dispatch(x, topk_ids, topk_weight, *packed)

@@ -299,29 +299,32 @@ def should_fuse(M: int, N: int, K: int) -> bool:
 
 
 class ThinLinear(torch.nn.Module):
-    """`nn.Linear` drop-in that routes the forward through `thin_linear`.
+    """Replacement for one `nn.Linear` whose forward runs on libsimsd_b200.
 
-    Holds a *reference* to the original module's parameters (no copy), so
-    swapping it in costs no memory and `state_dict()` round-trips unchanged.
-    Falls back to `F.linear` outside `should_fuse` unless `config` or
-    `always_fuse` is given.
+    The module registers the *same* Parameter objects as the linear it
+    replaces, so the swap allocates nothing, the optimiser-free inference
+    model keeps one copy of every weight, and `state_dict()` has the same keys
+    and tensors before and after.  Calls with an activation height inside
+    `should_fuse` (or any height when `config` pins a split or `always_fuse`
+    is set) take the thin-M kernel; the rest take cuBLAS through `F.linear`.
     """
 
     def __init__(self, linear: torch.nn.Linear,
                  config: tuple[int, int, int, int] | None = None,
                  always_fuse: bool = False):
         super().__init__()
-        self.in_features = linear.in_features
-        self.out_features = linear.out_features
-        self.weight = linear.weight
-        self.bias = linear.bias
-        self.config = config
-        self.always_fuse = always_fuse
+        self.in_features, self.out_features = linear.in_features, linear.out_features
+        self.weight, self.bias = linear.weight, linear.bias
+        self.config, self.always_fuse = config, always_fuse
+
+    def _thin(self, x: torch.Tensor) -> bool:
+        if self.config is not None or self.always_fuse:
+            return True
+        rows = x.numel() // x.shape[-1] if x.shape[-1] else 0
+        return should_fuse(rows, self.out_features, self.in_features)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        M = x.numel() // x.shape[-1] if x.shape[-1] else 0
-        if (self.config is not None or self.always_fuse
-                or should_fuse(M, self.out_features, self.in_features)):
+        if self._thin(x):
             return thin_linear(x, self.weight, self.bias, config=self.config)
         return torch.nn.functional.linear(x, self.weight, self.bias)
 
@@ -332,5 +335,9 @@ class ThinLinear(torch.nn.Module):
 
 
 def make_bench_fn(x, pool, sh):
-    """Bench hook with the reference's signature: call i reads weight pool[i]."""
-    return lambda i: thin_linear(x, pool[i])
+    """Timing hook taking (activations, weight pool, shape); the returned
+    callable's i-th call multiplies by pool[i], so a pool larger than L2 makes
+    every call stream its weight from HBM.  `sh` is unused here."""
+    def call(i):
+        return thin_linear(x, pool[i])
+    return call

@@ -1,10 +1,10 @@
 #!/usr/bin/env python3
 """Generate the golden fixtures in tests/golden/ from the reference's own code.
 
-Run in a container where the reference checkout exists (default
-/root/reference, override with SIMSD_REFERENCE); the GPU box never runs this.
+Run where a checkout of the reference exists, naming it with the required
+SIMSD_REFERENCE environment variable; the GPU box never runs this.
 
-    python tests/golden/make_golden.py
+    SIMSD_REFERENCE=<path to the SimSD-release checkout> python tests/golden/make_golden.py
 
 Writes (inputs and the reference's outputs, bf16 as uint16 bit patterns):
   align.npz          kernels/moe_dispatch_fused.py:93-132 `_align` (and :135 `_num_tiles`)
@@ -36,7 +36,9 @@ import numpy as np
 import torch
 import torch.nn.functional as F
 
-REF = Path(os.environ.get("SIMSD_REFERENCE", "/root/reference"))
+if not os.environ.get("SIMSD_REFERENCE"):
+    sys.exit("make_golden.py: set SIMSD_REFERENCE to the reference checkout (SimSD-release)")
+REF = Path(os.environ["SIMSD_REFERENCE"]).resolve()
 OUT = Path(__file__).resolve().parent
 sys.path.insert(0, str(REF))
 
