@@ -141,8 +141,12 @@ size_t simsd_thin_linear_workspace_size(int M, int N, int K, int dtype, int epil
  *   w_up [N, K]  same strides as w; SIMSD_EPI_SILU_MUL only (w is then the gate weight)
  *   bias [N]     or NULL (same dtype as x; SIMSD_EPI_NONE only)
  *   y    [M, N]  element (m, n) at y + m*ldy_m + n
- *   dtype        SIMSD_BF16 | SIMSD_F16 | SIMSD_F32 (x, w, bias and y share it;
- *                fp32 is accumulated in IEEE fp32, never TF32)
+ *   dtype        SIMSD_BF16 | SIMSD_F16 | SIMSD_F32 (x, w, bias and y share it).
+ *                fp32 with M <= 64 and split 0 runs on the tensor cores with each
+ *                operand split on chip into two tf32 parts (hi*hi + hi*lo + lo*hi,
+ *                about 2^-21 relative per product, fp32 accumulation - never a
+ *                one-pass TF32 product); other fp32 calls, and SIMSD_PATH_SIMT,
+ *                use IEEE fp32 FMA on the CUDA cores.
  *   split        0: balance the K reduction over all SMs (deterministic stream-K);
  *                s > 0: exactly s K-segments per output tile (the reference's
  *                config SPLIT_K); the sum order is fixed either way, so repeated
@@ -171,14 +175,29 @@ int simsd_thin_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w
  * for every N and K; layouts that take the CUDA-core path need no partials).
  * The first call on each device looks up the array's device address
  * (cudaGetSymbolAddress) with that device current: make that first call before
- * any stream capture.  All calls share the one array: calls that may overlap on
+ * any stream capture.  The address is kept for the life of the device's primary
+ * context; do not call this entry point again after cudaDeviceReset.  All calls share the one array: calls that may overlap on
  * the GPU (different streams, or different host threads) race and must be
- * serialised by the caller.  Each call clears the array's error word first.
+ * serialised by the caller.  A launch that gives up (a bounded wait ran out)
+ * sets a bit in the array's error word, which keeps it across calls until
+ * simsd_thin_linear_noalloc_error reads and clears it.
  */
 int simsd_thin_linear_noalloc(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w,
                               int64_t ldw_n, int64_t ldw_k, const void* w_up, const void* bias,
                               void* y, int64_t ldy_m, int M, int N, int K, int dtype,
                               int epilogue, void* stream);
+
+/*
+ * The device error word of simsd_thin_linear_noalloc's static array on the
+ * current device (SIMSD_DEV_ERR_* bits; 0 = every call since the last non-zero
+ * read completed), read after the work queued on `stream` finishes (this call waits
+ * for that stream).  A non-zero word means a launch gave up (a bounded wait ran
+ * out) and its output is incomplete; this call then zeroes the array's whole
+ * header - the error word and the per-tile arrival counters an aborted launch
+ * may leave raised - so later calls start clean.  No counterpart in the
+ * reference.  Same serialisation rule as simsd_thin_linear_noalloc.
+ */
+int simsd_thin_linear_noalloc_error(void* stream, int* out);
 
 /*
  * MoE router: logits = x wr^T (fp32, fixed summation order), score = sigmoid(logits),

@@ -101,7 +101,7 @@ int ensure_encode() {
   return SIMSD_OK;
 }
 
-// 128-byte-swizzled tiled map: box = {64 elements, box_rows[, 1]}.
+// 128-byte-swizzled tiled map: box = {one 128-byte row (64 16-bit or 32 fp32 elements), box_rows[, 1]}.
 int encode_map(CUtensorMap* m, const void* base, int dtype, int rank, const uint64_t* dims,
                const uint64_t* stride_bytes, uint32_t box_rows) {
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return SIMSD_ERR_ALIGN;
@@ -109,12 +109,13 @@ int encode_map(CUtensorMap* m, const void* base, int dtype, int rank, const uint
     if ((stride_bytes[i] & 15) != 0 || stride_bytes[i] == 0) return SIMSD_ERR_ALIGN;
   cuuint64_t gdim[3];
   cuuint64_t gstride[2];
-  cuuint32_t box[3] = {64, box_rows, 1};
+  cuuint32_t box[3] = {dtype == SIMSD_F32 ? 32u : 64u, box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   for (int i = 0; i < rank; ++i) gdim[i] = dims[i];
   for (int i = 0; i + 1 < rank; ++i) gstride[i] = stride_bytes[i];
-  const CUtensorMapDataType dt =
-      dtype == SIMSD_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUtensorMapDataType dt = dtype == SIMSD_BF16  ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                 : dtype == SIMSD_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   const CUresult r = g_encode(m, dt, rank, const_cast<void*>(base), gdim, gstride, box, estr,
                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -330,16 +331,17 @@ ThinPlan plan_thin(int M, int N, int K, int epilogue, int split, int sms) {
 // ---------------------------------------------------------------- cluster path
 // K atoms per ring stage of tc_cluster_kernel (its ring shares shared memory
 // with the cluster receive buffer, so 64-row tiles use single-atom stages).
-constexpr int cluster_ks(int bmax) { return bmax <= 32 ? 2 : 1; }
+// fp32 operands (F32) hold every atom twice (tf32 hi and lo parts): one atom a stage.
+constexpr int cluster_ks(int bmax, bool f32 = false) { return f32 ? 1 : (bmax <= 32 ? 2 : 1); }
 
-template <int BMAX>
+template <int BMAX, bool F32 = false>
 int cluster_prepare(int dev) {
-  constexpr int KS = cluster_ks(BMAX);
-  constexpr int smem = TcClusterConfig<BMAX, KS>::SMEM_BYTES;
+  constexpr int KS = cluster_ks(BMAX, F32);
+  constexpr int smem = TcClusterConfig<BMAX, KS, F32>::SMEM_BYTES;
   static bool done[kMaxDev];
   std::lock_guard<std::mutex> lk(g_mu);
   if (!done[dev]) {
-    if (cudaFuncSetAttribute(tc_cluster_kernel<BMAX, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+    if (cudaFuncSetAttribute(tc_cluster_kernel<BMAX, KS, F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
         cudaSuccess)
       return SIMSD_ERR_LAUNCH;
     done[dev] = true;
@@ -349,19 +351,19 @@ int cluster_prepare(int dev) {
 
 // Clusters of S CTAs of tc_cluster_kernel<BMAX> that fit on the device at once
 // (the occupancy calculator knows how clusters pack into GPCs); 0 if none.
-template <int BMAX>
+template <int BMAX, bool F32 = false>
 int max_clusters_b(int S, int dev) {
-  constexpr int KS = cluster_ks(BMAX);
+  constexpr int KS = cluster_ks(BMAX, F32);
   static int cache[kMaxDev][TC_CL_MAX + 1];
   {
     std::lock_guard<std::mutex> lk(g_mu);
     if (cache[dev][S] != 0) return cache[dev][S] > 0 ? cache[dev][S] : 0;
   }
-  if (cluster_prepare<BMAX>(dev) != SIMSD_OK) return 0;
+  if (cluster_prepare<BMAX, F32>(dev) != SIMSD_OK) return 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)S);
   cfg.blockDim = dim3(TC_THREADS);
-  cfg.dynamicSmemBytes = TcClusterConfig<BMAX, KS>::SMEM_BYTES;
+  cfg.dynamicSmemBytes = TcClusterConfig<BMAX, KS, F32>::SMEM_BYTES;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeClusterDimension;
   at[0].val.clusterDim.x = (unsigned)S;
@@ -370,7 +372,7 @@ int max_clusters_b(int S, int dev) {
   cfg.attrs = at;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, tc_cluster_kernel<BMAX, KS>, &cfg) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveClusters(&n, tc_cluster_kernel<BMAX, KS, F32>, &cfg) != cudaSuccess) {
     (void)cudaGetLastError();
     n = 0;
   }
@@ -379,19 +381,19 @@ int max_clusters_b(int S, int dev) {
   return n > 0 ? n : 0;
 }
 
-int max_clusters(int bmax, int S, int dev) {
+int max_clusters(int bmax, int S, int dev, bool f32 = false) {
   switch (bmax) {
-    case 16: return max_clusters_b<16>(S, dev);
-    case 32: return max_clusters_b<32>(S, dev);
-    case 64: return max_clusters_b<64>(S, dev);
+    case 16: return f32 ? max_clusters_b<16, true>(S, dev) : max_clusters_b<16>(S, dev);
+    case 32: return f32 ? max_clusters_b<32, true>(S, dev) : max_clusters_b<32>(S, dev);
+    case 64: return f32 ? max_clusters_b<64, true>(S, dev) : max_clusters_b<64>(S, dev);
   }
   return 0;
 }
 
-template <int BMAX>
+template <int BMAX, bool F32 = false>
 int launch_cluster_b(const TcClusterArgs& a, int S, int C, cudaStream_t s, int dev) {
-  constexpr int KS = cluster_ks(BMAX);
-  if (cluster_prepare<BMAX>(dev) != SIMSD_OK) return SIMSD_ERR_LAUNCH;
+  constexpr int KS = cluster_ks(BMAX, F32);
+  if (cluster_prepare<BMAX, F32>(dev) != SIMSD_OK) return SIMSD_ERR_LAUNCH;
   TcClusterArgs args = a;
   args.pdl = pdl_on() ? 1 : 0;
   args.prefetch = prefetch_stages();
@@ -400,7 +402,7 @@ int launch_cluster_b(const TcClusterArgs& a, int S, int C, cudaStream_t s, int d
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(C * S));
   cfg.blockDim = dim3(TC_THREADS);
-  cfg.dynamicSmemBytes = TcClusterConfig<BMAX, KS>::SMEM_BYTES;
+  cfg.dynamicSmemBytes = TcClusterConfig<BMAX, KS, F32>::SMEM_BYTES;
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
   int n = 0;
@@ -416,15 +418,15 @@ int launch_cluster_b(const TcClusterArgs& a, int S, int C, cudaStream_t s, int d
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  if (cudaLaunchKernelEx(&cfg, tc_cluster_kernel<BMAX, KS>, args) != cudaSuccess) return SIMSD_ERR_LAUNCH;
+  if (cudaLaunchKernelEx(&cfg, tc_cluster_kernel<BMAX, KS, F32>, args) != cudaSuccess) return SIMSD_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? SIMSD_OK : SIMSD_ERR_LAUNCH;
 }
 
-int launch_cluster(int bmax, const TcClusterArgs& a, int S, int C, cudaStream_t s, int dev) {
+int launch_cluster(int bmax, const TcClusterArgs& a, int S, int C, cudaStream_t s, int dev, bool f32 = false) {
   switch (bmax) {
-    case 16: return launch_cluster_b<16>(a, S, C, s, dev);
-    case 32: return launch_cluster_b<32>(a, S, C, s, dev);
-    case 64: return launch_cluster_b<64>(a, S, C, s, dev);
+    case 16: return f32 ? launch_cluster_b<16, true>(a, S, C, s, dev) : launch_cluster_b<16>(a, S, C, s, dev);
+    case 32: return f32 ? launch_cluster_b<32, true>(a, S, C, s, dev) : launch_cluster_b<32>(a, S, C, s, dev);
+    case 64: return f32 ? launch_cluster_b<64, true>(a, S, C, s, dev) : launch_cluster_b<64>(a, S, C, s, dev);
   }
   return SIMSD_ERR_UNSUPPORTED;
 }
@@ -451,11 +453,11 @@ int cluster_cta_cap() {
 // CTAs).  Whole tiles per cluster leave the SMs that no cluster fills free for
 // the next launch's CTAs, which fetch their first weight stages there while
 // this launch drains (programmatic dependent launch).
-ClusterPlan plan_cluster(int bmax, long long tiles, int kb, int dev) {
+ClusterPlan plan_cluster(int bmax, long long tiles, int kb, int dev, bool f32 = false) {
   ClusterPlan best;
   long long best_cost = -1, best_ctas = 0;
   for (int S = 1; S <= TC_CL_MAX && S <= kb; ++S) {
-    const long long cmax = std::min<long long>(max_clusters(bmax, S, dev), cluster_cta_cap() / S);
+    const long long cmax = std::min<long long>(max_clusters(bmax, S, dev, f32), cluster_cta_cap() / S);
     if (cmax <= 0) continue;
     const long long c0 = std::min(cmax, tiles);
     const long long w = cdiv(tiles, c0);
@@ -495,24 +497,28 @@ int thin_cluster(const void* x, long long ldx_m, const void* w, long long ldw_n,
                  int col_offset, int world, int rank, void* const* peer_sig, cudaStream_t s, int dev,
                  unsigned long long* amax_keys = nullptr, long long* amax_idx = nullptr, int* amax_count = nullptr,
                  const CatSpec* cat = nullptr) {
+  const bool f32 = dtype == SIMSD_F32;   // fp32 operands: 32-element K blocks, tf32 split on chip
+  const long long esz = f32 ? 4 : 2;
   const int bmax = pick_bmax_rows(M);
   const long long row_tiles = silu ? cdiv(N, 64) : cdiv(N, 128);
-  const int kb = (int)cdiv(K, 64);
-  const ClusterPlan cp = plan_cluster(bmax, row_tiles, kb, dev);
+  const int kb = (int)cdiv(K, f32 ? 32 : 64);
+  const ClusterPlan cp = plan_cluster(bmax, row_tiles, kb, dev, f32);
   if (cp.S <= 0) return SIMSD_ERR_UNSUPPORTED;
   if (ensure_encode() != SIMSD_OK) return SIMSD_ERR_DEVICE;
   TcClusterArgs a;
   memset(&a, 0, sizeof(a));
-  const long long lx = (M > 1) ? ldx_m : ((K * 2 + 15) / 16) * 8;
-  const long long lw = (N > 1) ? ldw_n : ((K * 2 + 15) / 16) * 8;
-  const uint64_t xd[2] = {(uint64_t)K, (uint64_t)M}, xs[1] = {(uint64_t)lx * 2};
-  const uint64_t wd[2] = {(uint64_t)K, (uint64_t)N}, wsb[1] = {(uint64_t)lw * 2};
+  // a one-row operand's stride is never used; give the map any legal one
+  const long long pad_ld = ((K * esz + 15) / 16) * 16 / esz;
+  const long long lx = (M > 1) ? ldx_m : pad_ld;
+  const long long lw = (N > 1) ? ldw_n : pad_ld;
+  const uint64_t xd[2] = {(uint64_t)K, (uint64_t)M}, xs[1] = {(uint64_t)(lx * esz)};
+  const uint64_t wd[2] = {(uint64_t)K, (uint64_t)N}, wsb[1] = {(uint64_t)(lw * esz)};
   int rc = encode_map(&a.tmB, x, dtype, 2, xd, xs, (uint32_t)bmax);
   if (cat != nullptr && cat->parts > 1) {
     CUtensorMap* maps[3] = {&a.tmA0, &a.tmA1, &a.tmA2};
     for (int i = 0; i < cat->parts && rc == SIMSD_OK; ++i) {
-      const long long li = cat->n[i] > 1 ? cat->ldw[i] : ((K * 2 + 15) / 16) * 8;
-      const uint64_t di[2] = {(uint64_t)K, (uint64_t)cat->n[i]}, si[1] = {(uint64_t)li * 2};
+      const long long li = cat->n[i] > 1 ? cat->ldw[i] : pad_ld;
+      const uint64_t di[2] = {(uint64_t)K, (uint64_t)cat->n[i]}, si[1] = {(uint64_t)(li * esz)};
       rc = encode_map(maps[i], cat->w[i], dtype, 2, di, si, 128);
     }
     a.cat_t1 = cat->n[0] / 128;
@@ -542,7 +548,19 @@ int thin_cluster(const void* x, long long ldx_m, const void* w, long long ldw_n,
     a.peer_out[r] = peer_y[r];
     a.peer_sig[r] = static_cast<int*>(peer_sig[r]);
   }
-  return launch_cluster(bmax, a, cp.S, cp.C, s, dev);
+  return launch_cluster(bmax, a, cp.S, cp.C, s, dev, f32);
+}
+
+// fp32 thin linear on the cluster kernel (tf32 hi/lo split, M <= 64): layouts
+// TMA can read with 32-element (128-byte) K blocks.
+int f32_tc_possible(const void* x, long long ldx_m, long long ldx_k, const void* w, long long ldw_n,
+                    long long ldw_k, const void* w_up, int M, int N, int K) {
+  if (M > 64 || K < 32 || ldx_k != 1 || ldw_k != 1) return 0;
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!al(x) || !al(w) || (w_up && !al(w_up))) return 0;
+  if (M > 1 && (ldx_m < K || ((ldx_m * 4) & 15) != 0)) return 0;
+  if (N > 1 && (ldw_n < K || ((ldw_n * 4) & 15) != 0)) return 0;
+  return 1;
 }
 
 int thin_tc_possible(const void* x, long long ldx_m, long long ldx_k, const void* w, long long ldw_n,
@@ -681,6 +699,14 @@ int simsd_thin_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w
   cudaStream_t s = (cudaStream_t)stream;
   int* err = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + WS_ERR_OFFSET);
 
+  if (dtype == SIMSD_F32 && path != SIMSD_PATH_SIMT && split == 0 && cluster_enabled() &&
+      f32_tc_possible(x, ldx_m, ldx_k, w, ldw_n, ldw_k, w_up, M, N, K)) {
+    // fp32, M <= 64: the same cluster kernel on tf32 hi/lo parts (three
+    // products per K step, fp32 accumulate)
+    const int rc = thin_cluster(x, ldx_m, w, ldw_n, w_up, bias, y, ldy_m, M, N, K, dtype, silu, err, nullptr, 0, 1,
+                                0, nullptr, s, dev);
+    if (rc != SIMSD_ERR_UNSUPPORTED) return rc;
+  }
   const bool tc_ok = thin_tc_possible(x, ldx_m, ldx_k, w, ldw_n, ldw_k, w_up, M, N, K, dtype) != 0;
   bool use_tc;
   if (path == SIMSD_PATH_TC) {
@@ -775,9 +801,10 @@ int simsd_thin_linear_noalloc(const void* x, int64_t ldx_m, int64_t ldx_k, const
   char* scratch = reinterpret_cast<char*>(noalloc_scratch(dev));
   if (scratch == nullptr) return SIMSD_ERR_DEVICE;
   cudaStream_t s = (cudaStream_t)stream;
+  // the error word is zero from module load and after every
+  // simsd_thin_linear_noalloc_error that finds it set; kernels only OR bits into
+  // it, so it keeps any failure until the caller reads it
   int* err = reinterpret_cast<int*>(scratch);
-  // the error word is the only scratch that must start at zero for each call
-  if (cudaMemsetAsync(err, 0, sizeof(int), s) != cudaSuccess) return SIMSD_ERR_LAUNCH;
 
   const bool tc_ok = thin_tc_possible(x, ldx_m, ldx_k, w, ldw_n, ldw_k, w_up, M, N, K, dtype) != 0;
   if (tc_ok && K >= 64) {
@@ -840,6 +867,27 @@ int simsd_thin_linear_noalloc(const void* x, int64_t ldx_m, int64_t ldx_k, const
   const long long gy = cdiv(M, SIMT_ROWS);
   if (gy > 65535) return SIMSD_ERR_UNSUPPORTED;
   return launch(simt_gemm_kernel, dim3((unsigned)cdiv(N, SIMT_WARPS), (unsigned)gy), dim3(SIMT_WARPS * 32), 0, s, a);
+}
+
+int simsd_thin_linear_noalloc_error(void* stream, int* out) {
+  if (out == nullptr) return SIMSD_ERR_SHAPE;
+  const int dev = current_device();
+  if (dev < 0) return SIMSD_ERR_DEVICE;
+  char* scratch = reinterpret_cast<char*>(noalloc_scratch(dev));
+  if (scratch == nullptr) return SIMSD_ERR_DEVICE;
+  cudaStream_t s = (cudaStream_t)stream;
+  int v = 0;
+  if (cudaMemcpyAsync(&v, scratch, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) return SIMSD_ERR_LAUNCH;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return SIMSD_ERR_LAUNCH;
+  if (v != 0) {
+    // a launch that gave up part-way may have left per-tile arrival counters
+    // raised; zero the whole header (error word and counters) so the next call
+    // starts from the state every completed launch leaves behind
+    if (cudaMemsetAsync(scratch, 0, kNoAllocHeader, s) != cudaSuccess) return SIMSD_ERR_LAUNCH;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return SIMSD_ERR_LAUNCH;
+  }
+  *out = v;
+  return SIMSD_OK;
 }
 
 // ---------------------------------------------------------------- MoE

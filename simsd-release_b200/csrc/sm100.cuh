@@ -166,6 +166,38 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D (+)= A B^T with A, B tf32 operands read as 32-bit words from shared memory
+// (K = 8 per instruction); the fp32 tensor-core path splits every operand so
+// that each word it hands in is exactly representable in tf32.
+__device__ __forceinline__ void tc_mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Split the four fp32 words hi[v] into tf32 parts: hi[v] keeps the sign,
+// exponent and top 10 mantissa bits of each word (exact in tf32), lo[v] gets
+// the rest, x - hi (exact in fp32), cut to tf32 the same way.  hi + lo matches
+// x to 2^-21 of |x|, so hi*hi' + hi*lo' + lo*hi' matches x*x' to about
+// 3 * 2^-21 relative.  Infinities and NaNs keep hi = x and lo = 0.
+__device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
+__device__ __forceinline__ float tf32_lo(float x, float h) {
+  return (__float_as_uint(x) & 0x7f800000u) == 0x7f800000u ? 0.0f : tf32_hi(__fsub_rn(x, h));
+}
+__device__ __forceinline__ void split_tf32(float4* hi, float4* lo, int v) {
+  const float4 x = hi[v];
+  const float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
+  lo[v] = make_float4(tf32_lo(x.x, h.x), tf32_lo(x.y, h.y), tf32_lo(x.z, h.z), tf32_lo(x.w, h.w));
+  hi[v] = h;
+}
+// Shared-memory writes of this thread (generic proxy) become visible to the
+// tensor cores and TMA (async proxy) that are ordered after this fence.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 // Arrive (once) on `bar` when every tcgen05 op this thread issued so far is done.
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -211,6 +243,18 @@ __host__ __device__ __forceinline__ uint32_t make_idesc_f16(int is_bf16, int M, 
   d |= 1u << 4;                                 // D format: f32
   d |= (uint32_t)(is_bf16 ? 1 : 0) << 7;        // A format
   d |= (uint32_t)(is_bf16 ? 1 : 0) << 10;       // B format
+  d |= (uint32_t)(N >> 3) << 17;                // N / 8
+  d |= (uint32_t)(M >> 4) << 24;                // M / 16
+  return d;
+}
+
+// Instruction descriptor, kind::tf32: fp32 accumulate, A and B tf32 (format 2),
+// both K-major, shape M x N.
+__host__ __device__ __forceinline__ uint32_t make_idesc_tf32(int M, int N) {
+  uint32_t d = 0;
+  d |= 1u << 4;                                 // D format: f32
+  d |= 2u << 7;                                 // A format: tf32
+  d |= 2u << 10;                                // B format: tf32
   d |= (uint32_t)(N >> 3) << 17;                // N / 8
   d |= (uint32_t)(M >> 4) << 24;                // M / 16
   return d;

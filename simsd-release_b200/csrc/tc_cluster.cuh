@@ -74,18 +74,34 @@ struct TcClusterArgs {
   int* peer_sig[TC_AG_MAX_WORLD];
 };
 
-template <int BMAX, int KS>
+// F32: fp32 operands on the tensor cores.  A K block is then 32 elements (one
+// 128-byte row, as 64 bf16 are), and each stage holds every atom twice: the
+// raw fp32 words as loaded (turned in place into their tf32 "hi" parts) and the
+// "lo" remainders, so the MMA can form hi*hi + hi*lo + lo*hi.
+template <int BMAX, int KS, bool F32 = false>
 struct TcClusterConfig {
+  static constexpr int SPLIT = F32 ? 2 : 1;
+  static constexpr int KW = F32 ? 32 : 64;   // K elements per block
   static constexpr int A_ATOM = TC_A_BYTES;
   static constexpr int B_ATOM = BMAX * 128;
-  static constexpr int A_STAGE = KS * A_ATOM;
-  static constexpr int B_STAGE = KS * B_ATOM;
+  static constexpr int A_STAGE = SPLIT * KS * A_ATOM;
+  static constexpr int B_STAGE = SPLIT * KS * B_ATOM;
   static constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
   static constexpr int RED_BYTES = TC_CL_RED_ROWS * BMAX * 4;
   static constexpr int TAIL_BYTES = 2 * 10 * 8 + 8 * 8 + 64 + 64 * 16 * 4 + 64 * 8;
   static constexpr int STAGES_RAW = (227 * 1024 - 1024 - RED_BYTES - TAIL_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 10 ? 10 : STAGES_RAW;
-  static constexpr int TMEM_COLS = (2 * BMAX) < 32 ? 32 : 2 * BMAX;
+  // TMEM per accumulator buffer (two buffers).  F32: the tensor cores' fp32
+  // accumulation loses a little with every MMA added into one accumulator, so
+  // the hi*hi products of a CTA's K range go to NACC accumulators (consecutive
+  // runs of K blocks) and the small hi*lo + lo*hi terms to one more; the
+  // epilogue adds them with IEEE fp32 adds in a fixed order.
+  static constexpr int NACC = F32 ? (BMAX >= 64 ? 3 : 7) : 1;
+  static constexpr int ACC_STRIDE = F32 ? (NACC + 1) * BMAX : BMAX;
+  static constexpr int TMEM_RAW = 2 * ACC_STRIDE;
+  static constexpr int TMEM_COLS = TMEM_RAW <= 32 ? 32 : TMEM_RAW <= 64 ? 64 : TMEM_RAW <= 128 ? 128
+                                   : TMEM_RAW <= 256 ? 256 : 512;
+  static_assert(TMEM_RAW <= 512, "TMEM columns");
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + RED_BYTES + TAIL_BYTES;
   static_assert(STAGES >= 2, "ring needs two stages");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
@@ -135,17 +151,19 @@ __device__ __forceinline__ const CUtensorMap* weight_map(const TcClusterArgs& p,
 // two zeros equal), then 0xffffffff - col so that equal values keep the lowest
 // column under a max.
 __device__ __forceinline__ unsigned long long amax_key(float v, int col, int odt) {
-  float r = odt == 0 ? __bfloat162float(__float2bfloat16_rn(v)) : __half2float(__float2half_rn(v));
+  float r = odt == 0 ? __bfloat162float(__float2bfloat16_rn(v))
+                     : (odt == 1 ? __half2float(__float2half_rn(v)) : v);
   if (r == 0.0f) r = 0.0f;
   const uint32_t b = __float_as_uint(r);
   const uint32_t k = (r != r) ? 0xffffffffu : ((b & 0x80000000u) ? ~b : (b | 0x80000000u));
   return ((unsigned long long)k << 32) | (unsigned long long)(0xffffffffu - (uint32_t)col);
 }
 
-template <int BMAX, int KS>
+template <int BMAX, int KS, bool F32 = false>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_constant__ TcClusterArgs p) {
-  using Cfg = TcClusterConfig<BMAX, KS>;
+  using Cfg = TcClusterConfig<BMAX, KS, F32>;
   constexpr int STAGES = Cfg::STAGES;
+  constexpr int KW = Cfg::KW;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -217,6 +235,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
   const int n_tiles = cid < tiles ? (tiles - 1 - cid) / C + 1 : 0;
   auto tile_of = [&](int i) { return cid + i * C; };
   const int nrows_all = p.rows < BMAX ? p.rows : BMAX;   // rows <= BMAX: one row block
+  // F32: K blocks of this CTA and the hi*hi accumulator runs they are cut into
+  const int f32_nblk = k_hi - k_lo;
+  const int f32_nch = f32_nblk < Cfg::NACC ? f32_nblk : Cfg::NACC;
   const int nb = (nrows_all + TC_BOX_ROWS - 1) / TC_BOX_ROWS;
 
   if (warp == 4) {
@@ -241,7 +262,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
         dep_ready = true;
         for (int s2 = 0; s2 < npend; ++s2)
           for (int at = 0; at < pend_na[s2]; ++at)
-            tma_load_2d(pend_dst[s2] + at * Cfg::B_ATOM, &p.tmB, pend_bar[s2], pend_k0[s2] + at * 64, 0, pol_x);
+            tma_load_2d(pend_dst[s2] + at * Cfg::B_ATOM, &p.tmB, pend_bar[s2], pend_k0[s2] + at * KW, 0, pol_x);
         npend = 0;
       };
       // L2 prefetch cursor over the (tile, stage) sequence: DRAM requests for the
@@ -260,12 +281,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
             const int prt = tile_of(pi);
             for (int at = 0; at < KS && pk + at < k_hi; ++at) {
               if (p.silu) {
-                tma_prefetch_l2_2d(&p.tmA0, (pk + at) * 64, prt * 64, pol_w);
-                tma_prefetch_l2_2d(&p.tmA1, (pk + at) * 64, prt * 64, pol_w);
+                tma_prefetch_l2_2d(&p.tmA0, (pk + at) * KW, prt * 64, pol_w);
+                tma_prefetch_l2_2d(&p.tmA1, (pk + at) * KW, prt * 64, pol_w);
               } else {
                 int pr0;
                 const CUtensorMap* pm = weight_map(p, prt, pr0);
-                tma_prefetch_l2_2d(pm, (pk + at) * 64, pr0, pol_w);
+                tma_prefetch_l2_2d(pm, (pk + at) * KW, pr0, pol_w);
               }
             }
           }
@@ -278,7 +299,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
           const uint32_t b_dst = smem_u32(sB + stage * Cfg::B_STAGE);
           for (int at = 0; at < na; ++at) {
             const uint32_t a_dst = smem_u32(sA + stage * Cfg::A_STAGE + at * Cfg::A_ATOM);
-            const int k0 = (k + at) * 64;
+            const int k0 = (k + at) * KW;
             if (p.silu) {
               tma_load_2d(a_dst, &p.tmA0, fb, k0, rtile * 64, pol_w);
               tma_load_2d(a_dst + 8192, &p.tmA1, fb, k0, rtile * 64, pol_w);
@@ -293,7 +314,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
           if (!dep_ready) {
             pend_dst[npend] = b_dst;
             pend_bar[npend] = fb;
-            pend_k0[npend] = k * 64;
+            pend_k0[npend] = k * KW;
             pend_na[npend] = na;
             ++npend;
           }
@@ -312,7 +333,82 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
     cluster_wait_acquire();   // pairs this warp's set-up arrive
   } else if (warp == 5) {
     // ================= MMA issuer
-    if (lane == 0) {
+    if constexpr (F32) {
+      // fp32 operands: the whole warp turns each landed stage into tf32 parts
+      // (hi in place, lo beside it), then lane 0 issues hi*hi + hi*lo + lo*hi
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      bool issued_any = false;
+      const uint32_t idesc = make_idesc_tf32(128, nb * TC_BOX_ROWS);
+      const int b_vec = nb * TC_BOX_ROWS * 8;   // float4s of the activation rows the MMA reads
+      for (int i = 0; ok && i < n_tiles; ++i) {
+        const int a = i & 1;
+        const uint32_t aphase = (i >> 1) & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&acce_bar[a]), aphase ^ 1, abort_flag, p.err))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_base = tmem_base + a * Cfg::ACC_STRIDE;
+        const uint32_t d_small = d_base + Cfg::NACC * BMAX;
+        for (int k = k_lo; k < k_hi; k += KS) {
+          const int na = min(KS, k_hi - k);
+          // KS == 1: one K block per stage; its run j of the NACC hi*hi accumulators
+          const int jrun = (k - k_lo) * f32_nch / f32_nblk;
+          const bool run_start = k == k_lo || (k - 1 - k_lo) * f32_nch / f32_nblk != jrun;
+          if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&full_bar[stage]), phase, abort_flag, p.err))) {
+            ok = false;
+            break;
+          }
+          uint8_t* const a_st = sA + stage * Cfg::A_STAGE;
+          uint8_t* const b_st = sB + stage * Cfg::B_STAGE;
+          for (int at = 0; at < na; ++at) {
+            float4* ah = reinterpret_cast<float4*>(a_st + at * Cfg::A_ATOM);
+            float4* al = reinterpret_cast<float4*>(a_st + (KS + at) * Cfg::A_ATOM);
+#pragma unroll 4
+            for (int v = lane; v < Cfg::A_ATOM / 16; v += 32) split_tf32(ah, al, v);
+            float4* bh = reinterpret_cast<float4*>(b_st + at * Cfg::B_ATOM);
+            float4* bl = reinterpret_cast<float4*>(b_st + (KS + at) * Cfg::B_ATOM);
+            for (int v = lane; v < b_vec; v += 32) split_tf32(bh, bl, v);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tc_fence_after();
+            if (p.trace && !issued_any) p.trace[blockIdx.x * 8 + 3] = globaltimer_ns();
+            for (int at = 0; at < na; ++at) {
+              const uint64_t ahd = make_sw128_desc(smem_u32(a_st + at * Cfg::A_ATOM));
+              const uint64_t ald = make_sw128_desc(smem_u32(a_st + (KS + at) * Cfg::A_ATOM));
+              const uint64_t bhd = make_sw128_desc(smem_u32(b_st + at * Cfg::B_ATOM));
+              const uint64_t bld = make_sw128_desc(smem_u32(b_st + (KS + at) * Cfg::B_ATOM));
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) {
+                const uint32_t acc_main = (run_start && at == 0 && kk == 0) ? 0u : 1u;
+                const uint32_t acc_small = (k > k_lo || at > 0 || kk > 0) ? 1u : 0u;
+                tc_mma_tf32(d_base + jrun * BMAX, ahd + 2 * kk, bhd + 2 * kk, idesc, acc_main);
+                tc_mma_tf32(d_small, ahd + 2 * kk, bld + 2 * kk, idesc, acc_small);
+                tc_mma_tf32(d_small, ald + 2 * kk, bhd + 2 * kk, idesc, 1u);
+              }
+            }
+            tc_commit(smem_u32(&empty_bar[stage]));
+          }
+          __syncwarp();
+          issued_any = true;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        if (lane == 0) tc_commit(smem_u32(&accf_bar[a]));
+        __syncwarp();
+      }
+      if (lane == 0) {
+        if (p.trace) p.trace[blockIdx.x * 8 + 5] = globaltimer_ns();
+        if (!ok && issued_any) {
+          tc_commit(smem_u32(drain_bar));
+          mbar_wait_drain(smem_u32(drain_bar), 0, 100000000ull);
+        }
+      }
+    } else if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -358,7 +454,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
     const int own = ro.owner(row);
     const int lr = ro.local(row);
     const int slot_rows = ro.slot_rows();
-    const int odt = p.is_bf16 ? 0 : 1;
+    const int odt = F32 ? 2 : (p.is_bf16 ? 0 : 1);
     char* outp = reinterpret_cast<char*>(p.out);
     const uint32_t red_u32 = smem_u32(red);
     const uint32_t red_full_u32 = smem_u32(red_full);
@@ -392,6 +488,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
     const long long ep_ld = p.ld_out;
     const int ep_silu = p.silu;
     const int ep_rows_out = p.rows_out;
+    // 16 accumulator columns (activation rows ch*16 ..) of this thread's row;
+    // F32: the hi*hi runs in order, then the small terms, with IEEE fp32 adds
+    auto acc_ld16 = [&](uint32_t tb, int ch, float (&v)[16]) {
+      tmem_ld16(tb + ch * 16, v);
+      if constexpr (F32) {
+        tmem_wait_ld();
+#pragma unroll 1
+        for (int j = 1; j <= f32_nch; ++j) {
+          float w[16];
+          tmem_ld16(tb + (j < f32_nch ? j : Cfg::NACC) * BMAX + ch * 16, w);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) v[e] = __fadd_rn(v[e], w[e]);
+        }
+      }
+    };
     int done = 0;
     for (int i = 0; i < n_tiles; ++i) {
       const int rtile = tile_of(i);
@@ -399,14 +511,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
       const uint32_t aphase = (i >> 1) & 1;
       if (!named_bar_and(1, 128, mbar_wait(smem_u32(&accf_bar[a]), aphase, abort_flag, p.err))) break;
       tc_fence_after();
-      const uint32_t t_base = tmem_base + ((uint32_t)(warp * 32) << 16) + a * BMAX;
+      const uint32_t t_base = tmem_base + ((uint32_t)(warp * 32) << 16) + a * Cfg::ACC_STRIDE;
       const int out_col0 = p.silu ? rtile * 64 : rtile * 128;
 
       if (S == 1) {
         // whole K range here: straight to y (as tc_gemm_kernel's whole tiles)
         for (int ch = 0; ch < nb; ++ch) {
           float v[16];
-          tmem_ld16(t_base + ch * 16, v);
+          acc_ld16(t_base, ch, v);
           tmem_wait_ld();
           if (ch == nb - 1) {
             tc_fence_before();
@@ -464,7 +576,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
       for (int ch = 0; ch < BMAX / 16; ++ch) {
         if (ch < nb) {
           float v[16];
-          tmem_ld16(t_base + ch * 16, v);
+          acc_ld16(t_base, ch, v);
           tmem_wait_ld();
           if (own == q) {
 #pragma unroll
@@ -546,8 +658,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
                   const int t = 4 * g + k4;
                   if (t < nrows_all) {
                     const float v = ep_silu ? silu_mul(va[k4], vb[k4]) : __fadd_rn(va[k4], ep_bias);
-                    if (ep_fast) yc[(long long)t * ep_ld] = f32_to_16bit(v, odt);
-                    else put(t, ep_col, v);
+                    if (!ep_fast) put(t, ep_col, v);
+                    else if constexpr (F32) reinterpret_cast<float*>(outp)[(long long)t * ep_ld + ep_col] = v;
+                    else yc[(long long)t * ep_ld] = f32_to_16bit(v, odt);
                   }
                 }
               }

@@ -59,6 +59,7 @@ SIGNATURES: dict[str, tuple] = {
     "simsd_thin_linear": (_I, [_P, _L, _L, _P, _L, _L, _P, _P, _P, _L, _I, _I, _I, _I, _I, _I, _I,
                                _P, _S, _P]),
     "simsd_thin_linear_noalloc": (_I, [_P, _L, _L, _P, _L, _L, _P, _P, _P, _L, _I, _I, _I, _I, _I, _P]),
+    "simsd_thin_linear_noalloc_error": (_I, [_P, ctypes.POINTER(_I)]),
     "simsd_moe_route_ex": (_I, [_P, _L, _I, _P, _L, _I, _P, _I, _I, _I, _I, _I, _F, _P, _P, _L, _I, _P, _P]),
     "simsd_moe_route": (_I, [_P, _L, _I, _P, _L, _I, _P, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P]),
     "simsd_moe_align": (_I, [_P, _I, _I, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P]),

@@ -5,14 +5,20 @@ Mirrors the interface of the reference module kernels/thin_linear_fused.py
 `should_fuse` :348-377, `ThinLinear` :380-412, `reset_workspace` :193-195,
 `make_bench_fn` :418) with the computation moved to libsimsd_b200.so:
 
-* bf16/fp16 with TMA-describable layouts run the tcgen05 kernel
-  (csrc/tc_gemm.cuh): the weight rows stream through a TMA ring into the
-  tensor cores (128 weight rows = MMA M, the activation rows = MMA N), fp32
-  accumulation in TMEM, and the K reduction is spread over every SM with a
-  deterministic fixed-order fixup (stream-K);
-* fp32 (IEEE, never TF32) and layouts TMA cannot describe (transposed views,
-  rows that are not 16-byte aligned) run the CUDA-core kernel
-  (csrc/simt_gemm.cuh).
+* bf16/fp16 with TMA-describable layouts run the tcgen05 kernels: the weight
+  rows stream through a TMA ring into the tensor cores (128 weight rows = MMA
+  M, the activation rows = MMA N) with fp32 accumulation in TMEM; for M <= 64
+  the K range of each output tile is split over the CTAs of a thread-block
+  cluster and summed in fixed order over distributed shared memory
+  (csrc/tc_cluster.cuh), above that a deterministic stream-K split with a
+  fixed-order fixup (csrc/tc_gemm.cuh);
+* fp32 with M <= 64 runs the same cluster kernel on the tensor cores with
+  every operand split into two tf32 parts on chip (hi*hi + hi*lo + lo*hi,
+  about 2^-21 relative per product, fp32 accumulation: far inside the
+  reference's 1e-5 fp32 tolerance, never plain one-pass TF32);
+* larger fp32, `config`-forced CUDA cores and layouts TMA cannot describe
+  (transposed views, rows that are not 16-byte aligned) run the CUDA-core
+  kernel (csrc/simt_gemm.cuh), IEEE fp32 FMA.
 
 There is no CPU path: CUDA tensors only, and a missing library raises.
 """

@@ -13,6 +13,8 @@ every other test before this one.
 """
 from __future__ import annotations
 
+import ctypes
+
 import pytest
 import torch
 import torch.nn.functional as F
@@ -49,17 +51,54 @@ def noalloc(x, w, w_up=None, bias=None):
     return rc, y
 
 
+def noalloc_error():
+    """The static array's error word (read and, if set, cleared by the library)."""
+    v = ctypes.c_int(-1)
+    rc = _lib.lib().simsd_thin_linear_noalloc_error(torch.cuda.current_stream().cuda_stream, ctypes.byref(v))
+    assert rc == _lib.SIMSD_OK
+    return v.value
+
+
+@pytest.mark.parametrize("inkernel", [False, True], ids=["fixup-kernel", "in-kernel-reduce"])
 @pytest.mark.parametrize("M,N,K", [(4, 2048, 2048), (16, 6144, 4096), (32, 4096, 12288), (1, 300, 72)])
-def test_noalloc_matches_workspace_entry_point_twice(M, N, K):
+def test_noalloc_matches_workspace_entry_point_twice(M, N, K, inkernel):
+    """Two calls in a row against the workspace entry point, with split tiles
+    summed by the separate kernel or by their last contributor (the only mode
+    that uses the array's per-tile counters, which every launch leaves zero)."""
     x, w = rnd(M, K, seed=M), rnd(N, K, scale=0.02, seed=N + K)
+    prev = _lib.set_inkernel_reduce(inkernel)
+    try:
+        with torch.inference_mode():
+            ref = thin_linear(x, w)
+            for _ in range(2):
+                rc, y = noalloc(x, w)
+                torch.cuda.synchronize()
+                assert rc == _lib.SIMSD_OK
+                assert float((y.float() - ref.float()).abs().max()) <= tol(ref)
+                assert float((y.float() - F.linear(x, w).float()).abs().max()) <= tol(ref)
+    finally:
+        _lib.set_inkernel_reduce(prev)
+    assert noalloc_error() == 0
+
+
+def test_noalloc_strided_activations_twice():
+    """A bf16 activation view with a padded row stride (the tensor-core path) and
+    a transposed one (the CUDA-core path)."""
+    big = rnd(8, 4096 + 64, seed=12)
+    x = big[:, :4096]
+    xt = rnd(2048, 8, seed=13).t()              # [8, 2048], column-major
+    w = rnd(3072, 4096, scale=0.02, seed=14)
+    w2 = rnd(1024, 2048, scale=0.02, seed=15)
     with torch.inference_mode():
-        ref = thin_linear(x, w)
+        ref, ref2 = F.linear(x, w), F.linear(xt, w2)
         for _ in range(2):
             rc, y = noalloc(x, w)
+            rc2, y2 = noalloc(xt, w2)
             torch.cuda.synchronize()
-            assert rc == _lib.SIMSD_OK
+            assert rc == _lib.SIMSD_OK and rc2 == _lib.SIMSD_OK
             assert float((y.float() - ref.float()).abs().max()) <= tol(ref)
-            assert float((y.float() - F.linear(x, w).float()).abs().max()) <= tol(ref)
+            assert float((y2.float() - ref2.float()).abs().max()) <= tol(ref2)
+    assert noalloc_error() == 0
 
 
 def test_noalloc_silu_mul_and_fp32_twice():
@@ -76,11 +115,24 @@ def test_noalloc_silu_mul_and_fp32_twice():
             assert rc == _lib.SIMSD_OK and rcf == _lib.SIMSD_OK
             assert float((y.float() - ref.float()).abs().max()) <= tol(ref)
             assert float((yf - reff).abs().max()) <= tol(reff)
+    assert noalloc_error() == 0
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch():
+    """M = 64, K = N = 4096 runs one CTA per SM, each with two 64 x 128 fp32
+    partial slots (64 KiB); the array holds 8 MiB less a 64 KiB header, so the
+    call fits on a GPU with at most 127 SMs and is refused above that (a
+    148-SM B200 refuses it)."""
     x, w = rnd(64, 4096, seed=8), rnd(4096, 4096, scale=0.02, seed=9)
+    sms = _lib.lib().simsd_device_sm_count()
+    fits = sms * 2 * 64 * 128 * 4 <= (8 << 20) - (64 << 10)
     with torch.inference_mode():
-        rc, _ = noalloc(x, w)
-    assert rc == _lib.SIMSD_ERR_SCRATCH_LIMIT
-    assert b"static" in _lib.lib().simsd_status_string(rc)
+        rc, y = noalloc(x, w)
+        torch.cuda.synchronize()
+    if fits:
+        assert rc == _lib.SIMSD_OK
+        assert float((y.float() - F.linear(x, w).float()).abs().max()) <= tol(y)
+    else:
+        assert rc == _lib.SIMSD_ERR_SCRATCH_LIMIT
+        assert b"static" in _lib.lib().simsd_status_string(rc)
+    assert noalloc_error() == 0
