@@ -425,9 +425,10 @@ def gpu_arm(args):
     clk_summary = clk.summary()
     line["clocks"] = clk_summary
     if world == 1 and "verify" in args.workload:
-        line["verify"] = verify_bench(dev, args.steps)
+        line["verify"] = verify_bench(dev, args.steps, None if args.no_cpu_baseline else min(10.0, args.cpu_seconds))
     if "ep" in args.workload.split(","):
-        line["ep_moe"] = ep_moe_bench(dev, rank, world, dist, args.steps)
+        line["ep_moe"] = ep_moe_bench(dev, rank, world, dist, args.steps,
+                                      None if (args.no_cpu_baseline or rank != 0) else min(5.0, args.cpu_seconds))
     if world == 1 and "moe" in args.workload:
         line["moe"] = moe_bench(dev, args.steps, None if args.no_cpu_baseline else min(5.0, args.cpu_seconds))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -452,10 +453,21 @@ def moe_bytes_flops(T: int, n_active: int) -> tuple[int, int]:
 
 
 # ------------------------------------------------------------------ EP MoE
-EP = dict(H=4096, E=256, k=8, I=1536, bias_std=0.5, Ts=(256, 1024, 4096))
+EP = dict(H=4096, E=256, k=8, I=1536, bias_std=0.5, Ts=(64, 256, 1024, 4096))
 
 
-def ep_moe_bench(dev, rank: int, world: int, dist, steps: int) -> dict:
+def tc_peaks() -> dict:
+    """Dense bf16 tensor-core denominators: the burst figure (a kernel timed
+    alone) and the sustained one (inside a long run under the power cap)."""
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"burst": float(d["bf16_tflops"]) * 1e12,
+                "sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])) * 1e12, "src": "measured"}
+    return {"burst": 1.59e15, "sustained": 1.4e15, "src": "fallback"}
+
+
+def ep_moe_bench(dev, rank: int, world: int, dist, steps: int, cpu_seconds: float | None = None) -> dict:
     """Expert-parallel MoE layer: E/world experts per rank, T/world tokens per
     rank, all-to-all exchange (NCCL); at world 1 the single-GPU layer."""
     from kernels.moe_dispatch_fused import moe_layer, moe_route
@@ -471,11 +483,14 @@ def ep_moe_bench(dev, rank: int, world: int, dist, steps: int) -> dict:
     wg, wu = [(torch.randn(hi - lo, I, H, generator=g, device=dev) * 0.02).to(bf) for _ in range(2)]
     wd = (torch.randn(hi - lo, H, I, generator=g, device=dev) * 0.02).to(bf)
     pk = peaks()
+    tcp = tc_peaks()
     out = {}
+    xs = {}
     with torch.inference_mode():
         for T in EP["Ts"]:
             Tr = T // world
             x = torch.randn(Tr, H, generator=g, device=dev).to(bf)
+            xs[T] = x
             ids, _ = moe_route(x, wr, bias, k=k)
             active = torch.zeros(E, dtype=torch.int32, device=dev)
             active[ids.reshape(-1)] = 1
@@ -506,15 +521,57 @@ def ep_moe_bench(dev, rank: int, world: int, dist, steps: int) -> dict:
                 dist.all_reduce(t, op=dist.ReduceOp.MAX)
                 ms = float(t.item())
             b = n_active * 3 * H * I * 2 + world * (3 * H * I * 2 + E * H * 2) + 2 * T * H * 2 + T * k * 12
+            f = 2 * T * (k + 1) * 3 * H * I + 2 * T * E * H
             a2a = 2 * T * k * H * 2 * (world - 1) // world if world > 1 else 0
-            out[f"T{T}"] = {"ms": round(ms, 4), "gbs": round(b / ms / 1e6, 1), "n_active_experts": n_active,
+            # roofline: the slower of streaming the bytes and doing the flops on
+            # `world` GPUs (sustained bf16 peak: the layer runs back to back)
+            roof_ms = max(b / (world * pk["hbm_gbs"] * 1e9), f / (world * tcp["sustained"])) * 1e3
+            out[f"T{T}"] = {"ms": round(ms, 4), "gbs": round(b / ms / 1e6, 1), "tflops": round(f / ms / 1e9, 1),
+                            "n_active_experts": n_active,
+                            "bound": "tensor" if f / tcp["sustained"] > b / (pk["hbm_gbs"] * 1e9) else "hbm",
+                            "frac_roofline": round(roof_ms / ms, 4),
                             "frac_hbm_peak_per_gpu": round(b / ms / 1e6 / world / pk["hbm_gbs"], 4),
+                            "frac_tc_sustained_per_gpu": round(f / (ms * 1e-3) / world / tcp["sustained"], 4),
                             "a2a_bytes_expected": a2a}
-    return {"workload": "EP MoE layer, BASELINE configs[4]: H=4096, E=256 (E/N per GPU), top-8 sigmoid+bias(N(0,0.5)), "
+    res_cpu = None
+    if world == 1 and cpu_seconds:
+        res_cpu = ep_cpu_baseline(xs[64], wr, bias, k, (wg, wu, wd), shared, cpu_seconds)
+    return {"cpu_baseline": res_cpu,
+            "workload": "EP MoE layer, BASELINE configs[4]: H=4096, E=256 (E/N per GPU), top-8 sigmoid+bias(N(0,0.5)), "
                         "I=1536 SiLU*mul experts + 1 shared expert, bf16, T tokens split over N GPUs, "
                         "all-to-all in fixed-capacity buckets (eager launches)",
-            "metric": "MoE layer HBM GB/s, all GPUs (algorithmic bytes: active experts + per-GPU shared/router + activations)",
+            "metric": "MoE layer HBM GB/s, all GPUs (algorithmic bytes: active experts + per-GPU shared/router + "
+                      "activations); frac_roofline = max(bytes / HBM peak, flops / sustained bf16 peak) / time",
             "n_gpus": world, "per_T": out}
+
+
+def ep_cpu_baseline(x, wr, bias, k, routed, shared, seconds: float) -> dict:
+    """configs[4] at T=64 on the host cores: the stock moe_infer restatement
+    (oracle/torch_eager.py, torch eager bf16) on host copies of the GPU's weights."""
+    from oracle.torch_eager import moe_layer as moe_layer_ref
+    from oracle.torch_eager import route
+    torch.set_num_threads(os.cpu_count() or 1)
+    H, E, I = EP["H"], EP["E"], EP["I"]
+    xc, wrc, bc = x.cpu(), wr.cpu(), bias.cpu()
+    rc = tuple(t.cpu() for t in routed)
+    sc = tuple(t.cpu() for t in shared)
+    with torch.inference_mode():
+        moe_layer_ref(xc, wrc, bc, k, *rc, shared=sc)
+        n = 0
+        t0 = time.perf_counter()
+        while n < 2 or time.perf_counter() - t0 < seconds:
+            moe_layer_ref(xc, wrc, bc, k, *rc, shared=sc)
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        ids, _ = route(xc, wrc, bc, k)
+    T = x.shape[0]
+    n_active = int(torch.unique(ids).numel())
+    b = n_active * 3 * H * I * 2 + 3 * H * I * 2 + E * H * 2 + 2 * T * H * 2 + T * k * 12
+    del rc, sc
+    return {"value": round(b / dt / 1e9, 2), "unit": "GB/s", "ms": round(dt * 1e3, 2),
+            "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"configs[4] T={T} MoE layer (router + {n_active} active experts + shared), stock moe_infer "
+                      f"restatement in torch eager bf16, {n} runs"}
 
 
 def moe_bench(dev, steps: int, cpu_seconds: float | None) -> dict:
@@ -529,8 +586,7 @@ def moe_bench(dev, steps: int, cpu_seconds: float | None) -> dict:
     pools = [tuple((torch.randn(*sh, generator=g, device=dev) * 0.02).to(bf)
                    for sh in ((E + 1, I, H), (E + 1, I, H), (E + 1, H, I))) for _ in range(POOL)]
     pk = peaks()
-    tc_peak = float(json.loads((REPO / "MEASURED_PEAKS.json").read_text())["bf16_tflops"]) * 1e12 \
-        if (REPO / "MEASURED_PEAKS.json").exists() else 1.59e15
+    tc_peak = tc_peaks()["sustained"]
     out = {}
     tot_b = tot_t = 0.0
     with torch.inference_mode():
@@ -607,16 +663,119 @@ def moe_cpu_baseline(seconds: float) -> dict:
 
 
 # ------------------------------------------------------------------ verify
-def verify_bench(dev, steps: int) -> dict:
+VERIFY_PERTURB = ((0, 2), (1, 0), (2, 3), (3, 1))
+
+
+def _greedy_chain_sets(h, K: int, BL: int, vocab: int):
+    """Draft sets for acceptance: the target's own greedy chain (drafts equal to
+    the argmax at every mask row after a few refinements, so most are
+    accepted), then copies with one token changed in different blocks."""
+    drafts = [[0] * BL for _ in range(K)]
+    with torch.inference_mode():
+        for _ in range(4):
+            h.set_drafts(drafts, h.smaps)
+            lg = h.window_logits()
+            drafts = [lg[h.mask_rows(k)].float().argmax(-1).tolist() for k in range(K)]
+    sets = [[list(d) for d in drafts]]
+    for blk, pos in VERIFY_PERTURB:
+        d = [list(x) for x in drafts]
+        d[blk][pos] = (d[blk][pos] + 1) % vocab
+        sets.append(d)
+    return sets
+
+
+def _accept_lists(h, sets, fn):
+    """(accept lengths per set, logits per set) with the current forward `fn`."""
+    out, logits = [], []
+    with torch.inference_mode():
+        for d in sets:
+            h.set_drafts(d, h.smaps)
+            lg = fn()
+            torch.cuda.synchronize()
+            if lg.ndim == 2:
+                logits.append(lg.float())
+                out.append([a[1] for a in h.accept(lg, d)])
+            else:
+                out.append([a[1] for a in h.accept_ids(lg, d)])
+    return out, logits
+
+
+def _verify_fp32_greedy(dev, K: int, BL: int, P: int) -> dict:
+    """fp32 gate (the reference's own end-to-end gate is fp32): the same
+    random-init model in fp32, accept lists of cuBLAS against the thin-M
+    kernels, which take fp32 on the tensor cores (tf32 hi/lo split)."""
+    from kernels import fused_toggle
+    from kernels.sdar_verify import SDAR_8B, SDARVerifyModel, VerifyHarness
+    s = SDAR_8B
+    model = SDARVerifyModel.random_init(s, dev, dtype=torch.float32, seed=0)
+    g = torch.Generator().manual_seed(1)
+    prompt = torch.randint(0, s.vocab, (P,), generator=g).tolist()
+    d0 = [torch.randint(0, s.vocab, (BL,), generator=g).tolist() for _ in range(K)]
+    smaps = [torch.randperm(BL, generator=g).tolist() for _ in range(K)]
+    h = VerifyHarness(model, prompt, d0, smaps, BL)
+    h.smaps = smaps
+    sets = _greedy_chain_sets(h, K, BL, s.vocab)
+    ref, lr = _accept_lists(h, sets, h.window_logits)
+    fused_toggle.apply_to_model(model, True)
+    ours, lo = _accept_lists(h, sets, h.window_logits)
+    fused_toggle.apply_to_model(model, False)
+    res = {"accepted_cublas": ref, "accepted_ours_tcgen05": ours, "identical_accepted_tokens": ref == ours,
+           "max_abs_logit_diff": round(max(float((a - b).abs().max()) for a, b in zip(lr, lo)), 6)}
+    del h, model
+    torch.cuda.empty_cache()
+    return res
+
+
+def _verify_cpu_baseline(h, model, seconds: float) -> dict:
+    """The K = 4 verify forward on the host cores (torch eager bf16, the
+    reference's CPU path), over the prefix KV the GPU computed (
+    a CPU prefill of 2048 tokens would be ~33 TFLOP)."""
+    from kernels.sdar_verify import SDARVerifyModel, VerifyHarness
+    torch.set_num_threads(os.cpu_count() or 1)
+    with torch.device("meta"):
+        mc = SDARVerifyModel(model.s)
+    mc = mc.to_empty(device="cpu").to(next(model.parameters()).dtype)
+    with torch.no_grad():
+        for (name, pc), pg in zip(mc.named_parameters(), model.parameters()):
+            pc.copy_(pg.detach().cpu())
+    hc = object.__new__(VerifyHarness)
+    hc.__dict__.update(h.__dict__)
+    hc.model, hc.fused = mc, False
+    hc.caches = [(k.cpu(), v.cpu()) for k, v in h.caches]
+    hc.win_ids, hc.win_pos, hc.window_mask = h.win_ids.cpu(), h.win_pos.cpu(), h.window_mask.cpu()
+    n = 0
+    with torch.inference_mode():
+        hc.window_logits()
+        t0 = time.perf_counter()
+        while n < 2 or time.perf_counter() - t0 < seconds:
+            hc.window_logits()
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+    del hc, mc
+    K, BL = h.K, h.bl
+    return {"ms_per_forward": round(dt * 1e3, 1), "tok_s": round(K * BL / dt, 2), "unit": "tok/s",
+            "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n} K=4 verify forwards (32 query rows x 36 layers + lm_head, bf16 torch eager on the host) "
+                      f"over the GPU-computed 2048-token KV prefix"}
+
+
+def verify_bench(dev, steps: int, cpu_seconds: float | None = None) -> dict:
     """Synthetic SDAR-8B verify forward: K=4 blocks x bl=4 over a 2048-token prefix.
 
     tok/s = K*bl / forward latency (CUDA-graph replay of the 32-row window
     forward through all 36 layers + lm_head).  Measured twice on the same
     weights: the reference path (stock nn.Linear = cuBLAS) and ours
     (fused_toggle with the fused gate/up and merged q/k/v, PDL, and the fused
-    layer ops: RMSNorm + residual, q/k norm + rotary + cache write).  Both use a
-    static KV cache.  Algorithmic bytes per forward:
+    layer ops: RMSNorm + residual, q/k norm + rotary + cache write, verify
+    attention).  Both use a static KV cache.  Algorithmic bytes per forward:
     every linear weight + lm_head + the embedding rows + the KV prefix.
+
+    Acceptance is measured on draft sets built from the target's own greedy
+    chain (plus single-token changes), so drafts are accepted and the accept
+    lengths differ between sets; in bf16 the two arms' greedy tokens differ at
+    near-ties (a random-init 36-layer model amplifies any rounding difference,
+    cuBLAS against itself included), so the identity gate runs in fp32, where
+    the thin-M kernels also run on the tensor cores.
     """
     from kernels import fused_toggle
     from kernels.sdar_verify import SDAR_8B, SDARVerifyModel, VerifyHarness
@@ -625,25 +784,33 @@ def verify_bench(dev, steps: int) -> dict:
     model = SDARVerifyModel.random_init(s, dev, seed=0)
     g = torch.Generator().manual_seed(1)
     prompt = torch.randint(0, s.vocab, (P,), generator=g).tolist()
-    drafts = [torch.randint(0, s.vocab, (BL,), generator=g).tolist() for _ in range(K)]
+    drafts0 = [torch.randint(0, s.vocab, (BL,), generator=g).tolist() for _ in range(K)]
     smaps = [torch.randperm(BL, generator=g).tolist() for _ in range(K)]
-    h = VerifyHarness(model, prompt, drafts, smaps, BL)
+    h = VerifyHarness(model, prompt, drafts0, smaps, BL)
+    h.smaps = smaps
+    sets = _greedy_chain_sets(h, K, BL, s.vocab)
+    h.set_drafts(sets[0], smaps)
     kv_bytes = s.layers * 2 * P * s.kv_heads * s.head_dim * 2
     fwd_bytes = s.linear_params * 2 + s.vocab * s.hidden * 2 + kv_bytes
     res = {"workload": "random-init SDAR-8B-shaped target (36 layers, H=4096, 32q/8kv x 128, MLP 12288, "
                        "vocab 151936, bf16 N(0,0.02)), K=4 draft blocks x bl=4 (32 query rows) over a "
-                       "2048-token KV prefix of uniform random ids; CUDA-graph replay",
+                       "2048-token KV prefix of uniform random ids; CUDA-graph replay; acceptance over "
+                       f"{len(sets)} draft sets (the target's greedy chain + single-token changes)",
            "unit": "tok/s", "bytes_per_forward": fwd_bytes}
+    if cpu_seconds:
+        res["cpu_baseline"] = _verify_cpu_baseline(h, model, cpu_seconds)
+    logits = {}
 
     def timed(label, fn=None):
         fn = fn or h.window_logits
+        h.set_drafts(sets[0], smaps)
         with torch.inference_mode():
             for _ in range(3):
                 fn()
             torch.cuda.synchronize()
             gr = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gr):
-                out = fn()
+                fn()
             for _ in range(3):
                 gr.replay()
             torch.cuda.synchronize()
@@ -655,11 +822,12 @@ def verify_bench(dev, steps: int) -> dict:
             e1.record()
             torch.cuda.synchronize()
             ms = e0.elapsed_time(e1) / n
-            acc = h.accept(out, drafts) if out.ndim == 2 else h.accept_ids(out, drafts)
         del gr
+        acc, lg = _accept_lists(h, sets, fn)
+        if lg:
+            logits[label] = lg
         res[label] = {"ms_per_forward": round(ms, 3), "tok_s": round(K * BL / (ms * 1e-3), 1),
-                      "weight_stream_gbs": round(fwd_bytes / ms / 1e6, 1),
-                      "accepted": [a[1] for a in acc]}
+                      "weight_stream_gbs": round(fwd_bytes / ms / 1e6, 1), "accepted": acc}
 
     timed("reference_cublas")
     # the whole greedy step: forward, lm_head and the argmax of every row
@@ -675,10 +843,20 @@ def verify_bench(dev, steps: int) -> dict:
     res["speedup_vs_cublas"] = round(res["reference_cublas"]["ms_per_forward"] / res["ours"]["ms_per_forward"], 3)
     res["greedy_step_speedup_vs_cublas"] = round(res["reference_cublas_greedy"]["ms_per_forward"]
                                                  / res["ours_greedy_fused_head"]["ms_per_forward"], 3)
-    res["identical_accepted_tokens"] = (res["ours"]["accepted"] == res["reference_cublas"]["accepted"]
-                                        == res["ours_greedy_fused_head"]["accepted"])
-    del h, model
+    rows = torch.cat([torch.arange(h.mask_rows(k).start, h.mask_rows(k).stop) for k in range(K)])
+    ref_l, our_l = logits["reference_cublas"], logits["ours"]
+    flips = sum(int((a[rows].argmax(-1) != b[rows].argmax(-1)).sum()) for a, b in zip(ref_l, our_l))
+    res["bf16_vs_cublas"] = {
+        "identical_accepted_tokens": res["ours"]["accepted"] == res["reference_cublas"]["accepted"],
+        "verified_positions": len(rows) * len(sets), "argmax_differs": flips,
+        "logits_bit_identical_frac": round(sum(float((a[rows] == b[rows]).float().mean())
+                                               for a, b in zip(ref_l, our_l)) / len(sets), 4),
+        "note": "bf16 greedy tokens of a random-init 36-layer model differ between any two GEMM "
+                "implementations at near-ties (cuBLAS against a transposed cuBLAS formulation flips as "
+                "many rows); the identity gate is fp32_tensor_core_greedy"}
+    del h, model, logits
     torch.cuda.empty_cache()
+    res["fp32_tensor_core_greedy"] = _verify_fp32_greedy(dev, K, BL, P)
     return res
 
 

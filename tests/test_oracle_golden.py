@@ -75,6 +75,51 @@ def test_moe_dispatch_oracle_matches_reference():
         assert err <= _moe_tol(ref, dt), f"{c}: {err} > {_moe_tol(ref, dt)}"
 
 
+@pytest.mark.parametrize("via", ["c", "grouped"])
+def test_moe_dispatch_grouped_oracle_matches_reference(via):
+    """The grouped numpy restatement against the same golden outputs as the C loop."""
+    z = _load("moe_dispatch")
+    for c in _cases(z):
+        dt = str(z[f"{c}.dtype"])
+        if "float16" in dt and "bfloat16" not in dt:
+            cast = lambda a: a.view(np.float16)  # noqa: E731
+        else:
+            cast = lambda a: a  # noqa: E731
+        args = [cast(z[f"{c}.{k}"]) for k in ("x", "ids", "w", "wg", "wu", "wd")]
+        args[1] = z[f"{c}.ids"]
+        args[2] = z[f"{c}.w"]
+        fn = O.moe_dispatch if via == "c" else O.moe_dispatch_grouped
+        _, out = fn(*args, mode=0)
+        ref = _f32(z[f"{c}.ref"], dt) if "float16" not in dt or "bfloat16" in dt else z[f"{c}.ref"].view(np.float16).astype(np.float32)
+        got = _f32(out, dt) if out.dtype != np.float16 else out.astype(np.float32)
+        err = float(np.abs(got - ref).max())
+        assert err <= _moe_tol(ref, dt), f"{c}: {err} > {_moe_tol(ref, dt)}"
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_moe_dispatch_grouped_oracle_matches_c_loop(mode):
+    """Same rounding points, different summation order inside each dot product:
+    the fp32 combines agree to a few fp32 ulps of the scale and almost every
+    bf16 output has the same bits (a rounding boundary crossed by the order
+    change moves one output by one bf16 ulp)."""
+    rng = np.random.default_rng(7)
+    T, k, E, H, I = 48, 4, 12, 256, 192
+    x = O.f32_to_bf16_bits(rng.standard_normal((T, H)).astype(np.float32))
+    wg, wu = (O.f32_to_bf16_bits((rng.standard_normal((E, I, H)) * 0.02).astype(np.float32)) for _ in range(2))
+    wd = O.f32_to_bf16_bits((rng.standard_normal((E, H, I)) * 0.02).astype(np.float32))
+    ids = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int64)
+    ids[3, 1] = -1                         # an empty slot (expert-parallel buckets) contributes nothing
+    w = rng.random((T, k)).astype(np.float32)
+    add = O.f32_to_bf16_bits(rng.standard_normal((T, H)).astype(np.float32))
+    a_c, o_c = O.moe_dispatch(x, ids, w, wg, wu, wd, add=add, mode=mode)
+    a_g, o_g = O.moe_dispatch_grouped(x, ids, w, wg, wu, wd, add=add, mode=mode)
+    scale = float(np.abs(a_c).max())
+    assert float(np.abs(a_c - a_g).max()) <= 2 ** -8 * scale       # bf16 rounding of h may differ
+    assert float((o_c == o_g).mean()) >= 0.98
+    assert float(np.abs(O.bf16_bits_to_f32(o_c) - O.bf16_bits_to_f32(o_g)).max()) <= 2 ** -7 * float(
+        np.abs(O.bf16_bits_to_f32(o_c)).max())
+
+
 def _lin_tol(ref, dtype_str):
     m = float(np.abs(ref).max())
     if "float32" in dtype_str:
