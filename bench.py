@@ -167,18 +167,26 @@ def run_step(ws, xs, world, dist, ag=None, on_result=None):
     from kernels.parallel import gather_columns
     from kernels.thin_linear_fused import thin_linear, thin_linear_silu_mul
     res = []
+    fused = world > 1 and ag is not None
     for M in MS:
         for name, K, N, silu in SHAPES:
             x = xs[M][K]
-            if world > 1 and ag is not None:
-                y = ag.linear(x, *ws[name]) if silu else ag.linear(x, ws[name])
+            if fused:
+                # the 20 linears of a step are independent: their gathers
+                # complete together at the one wait below
+                y = ag.linear(x, *ws[name], wait=False) if silu else ag.linear(x, ws[name], wait=False)
             else:
                 y = thin_linear_silu_mul(x, *ws[name]) if silu else thin_linear(x, ws[name])
                 if world > 1:
                     y = gather_columns(y)
-            if on_result is not None:
-                on_result(len(res), y)
+                if on_result is not None:
+                    on_result(len(res), y)
             res.append(y)
+    if fused:
+        ag.wait()
+        if on_result is not None:
+            for j, y in enumerate(res):
+                on_result(j, y)
     return res
 
 
@@ -332,6 +340,11 @@ def gpu_arm(args):
                     houts[j].copy_(y, non_blocking=True)     # into pinned host buffers
 
             main.wait_event(ready[MS[0]])
+            if ag is not None:
+                # the fused gathers hand results over after the step's one wait,
+                # so every input is in place before the first launch
+                for M in MS[1:]:
+                    main.wait_event(ready[M])
             run_step(pool[p], sx, world, dist, ag, on_result=out)
             main.wait_stream(cs)
             main.wait_stream(hs)
@@ -426,6 +439,8 @@ def gpu_arm(args):
     line["clocks"] = clk_summary
     if world == 1 and "verify" in args.workload:
         line["verify"] = verify_bench(dev, args.steps, None if args.no_cpu_baseline else min(10.0, args.cpu_seconds))
+    elif world > 1 and "verify" in args.workload:
+        line["verify"] = verify_tp_bench(dev, rank, world, dist, args.steps)
     if "ep" in args.workload.split(","):
         line["ep_moe"] = ep_moe_bench(dev, rank, world, dist, args.steps,
                                       None if (args.no_cpu_baseline or rank != 0) else min(5.0, args.cpu_seconds))
@@ -860,6 +875,85 @@ def verify_bench(dev, steps: int, cpu_seconds: float | None = None) -> dict:
     return res
 
 
+def verify_tp_bench(dev, rank: int, world: int, dist, steps: int) -> dict:
+    """configs[3] with every linear column-split over the N GPUs (fused
+    all-gather, K split pinned to the single-GPU plan) and attention / norms
+    replicated.  Each rank also runs the single-GPU fused forward on its own
+    copy of the model: the sharded hidden states and greedy tokens must equal
+    it bit for bit.  tok/s = K*bl / max-over-ranks latency of the graph-replayed
+    greedy step (forward + lm_head + argmax)."""
+    from kernels import fused_toggle
+    from kernels.sdar_verify import SDAR_8B, SDARVerifyModel, VerifyHarness
+    from kernels.sdar_verify_tp import ShardedVerify
+    s = SDAR_8B
+    K, BL, P = 4, 4, 2048
+    model = SDARVerifyModel.random_init(s, dev, seed=0)
+    g = torch.Generator().manual_seed(1)
+    prompt = torch.randint(0, s.vocab, (P,), generator=g).tolist()
+    drafts0 = [torch.randint(0, s.vocab, (BL,), generator=g).tolist() for _ in range(K)]
+    smaps = [torch.randperm(BL, generator=g).tolist() for _ in range(K)]
+    h = VerifyHarness(model, prompt, drafts0, smaps, BL)
+    h.smaps = smaps
+    sets = _greedy_chain_sets(h, K, BL, s.vocab)
+    sv = ShardedVerify(model)
+    fused_toggle.apply_to_model(model, True, fuse_gate_up=True, fuse_qkv=True)
+    fused_toggle.warmup(model, BL, extra_M=(2 * BL * K,))
+    res = {"workload": f"BASELINE configs[3] target, every linear column-split over {world} GPUs (all-gather fused "
+                       "into the GEMM, K split pinned to the single-GPU plan), attention and norms replicated; "
+                       "CUDA-graph replay of the greedy step (forward + lm_head + argmax)",
+           "unit": "tok/s", "n_gpus": world}
+    same_hidden, same_ids, acc1, accg = True, True, [], []
+    with torch.inference_mode():
+        for d in sets:
+            h.set_drafts(d, smaps)
+            h.fused = True
+            h1 = h.window_hidden().clone()
+            id1 = h.window_argmax().clone()
+            h.fused = False
+            hg = sv.window_hidden(h).clone()
+            idg = sv.window_argmax(h).clone()
+            torch.cuda.synchronize()
+            same_hidden &= bool(torch.equal(h1, hg))
+            same_ids &= bool(torch.equal(id1, idg))
+            acc1.append([a[1] for a in h.accept_ids(id1, d)])
+            accg.append([a[1] for a in h.accept_ids(idg, d)])
+        h.set_drafts(sets[0], smaps)
+        for _ in range(3):
+            sv.window_argmax(h)
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            sv.window_argmax(h)
+        for _ in range(3):
+            gr.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        n = max(10, min(steps, 50))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / n
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        del gr
+        torch.cuda.synchronize()
+    ok = torch.tensor([int(same_hidden and same_ids)], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    fused_toggle.apply_to_model(model, False)
+    dist.barrier()
+    sv.close()
+    res.update({"ms_per_forward": round(ms, 3), "tok_s": round(K * BL / (ms * 1e-3), 1), "value": round(K * BL / (ms * 1e-3), 1),
+                "bit_identical_to_single_gpu": bool(ok.item()), "accepted_single_gpu": acc1,
+                "accepted_sharded": accg, "identical_accepted_tokens": acc1 == accg})
+    del h, model, sv
+    torch.cuda.empty_cache()
+    return res
+
+
 def _traffic_summary() -> dict | None:
     p = REPO / "profiles" / "tc_gemm_traffic.json"
     if p.exists():
@@ -996,6 +1090,29 @@ def profile_moe(args):
     print(f"profile MoE layer T={args.profile_moe}: out {tuple(y.shape)}")
 
 
+def profile_ep(args):
+    """A few configs[4] MoE layers on one GPU at T = --profile-ep (for ncu
+    captures of the grouped GEMMs' tensor-pipe use)."""
+    from kernels.moe_dispatch_fused import moe_layer
+    dev = torch.device("cuda", 0)
+    H, k, I = EP["H"], EP["k"], EP["I"]
+    E = args.profile_ep_experts     # fewer experts than configs[4]'s 256 keep an ncu capture to a few GB
+    bf = torch.bfloat16
+    g0 = torch.Generator(device=dev).manual_seed(77)
+    wr = (torch.randn(E, H, generator=g0, device=dev) * 0.02).to(bf)
+    bias = torch.randn(E, generator=g0, device=dev) * EP["bias_std"]
+    shared = tuple((torch.randn(*sh, generator=g0, device=dev) * 0.02).to(bf) for sh in ((I, H), (I, H), (H, I)))
+    g = torch.Generator(device=dev).manual_seed(1000)
+    wg, wu = [(torch.randn(E, I, H, generator=g, device=dev) * 0.02).to(bf) for _ in range(2)]
+    wd = (torch.randn(E, H, I, generator=g, device=dev) * 0.02).to(bf)
+    x = torch.randn(args.profile_ep, H, generator=g, device=dev).to(bf)
+    with torch.inference_mode():
+        for _ in range(args.profile_launches + 1):
+            y = moe_layer(x, wr, bias, k, wg, wu, wd, shared=shared)
+        torch.cuda.synchronize()
+    print(f"profile EP MoE layer (configs[4] shapes, {E} experts, one GPU) T={args.profile_ep}: out {tuple(y.shape)}")
+
+
 def profile_verify(args):
     """A few eager verify forwards (for an ncu launch list)."""
     from kernels import fused_toggle
@@ -1028,6 +1145,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--profile-verify", default=None, choices=["ours", "cublas"])
     ap.add_argument("--profile-moe", type=int, default=0)
+    ap.add_argument("--profile-ep", type=int, default=0)
+    ap.add_argument("--profile-ep-experts", type=int, default=256)
     ap.add_argument("--profile-case", default=None, choices=[s[0] for s in SHAPES])
     ap.add_argument("--profile-sweep", action="store_true")
     ap.add_argument("--profile-m", type=int, default=16)
@@ -1052,6 +1171,8 @@ def main():
         profile_sweep(args)
     elif args.profile_moe:
         profile_moe(args)
+    elif args.profile_ep:
+        profile_ep(args)
     elif args.profile_verify:
         profile_verify(args)
     elif args.impl == "reference":

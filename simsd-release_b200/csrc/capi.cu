@@ -334,14 +334,14 @@ ThinPlan plan_thin(int M, int N, int K, int epilogue, int split, int sms) {
 // fp32 operands (F32) hold every atom twice (tf32 hi and lo parts): one atom a stage.
 constexpr int cluster_ks(int bmax, bool f32 = false) { return f32 ? 1 : (bmax <= 32 ? 2 : 1); }
 
-template <int BMAX, bool F32 = false>
+template <int BMAX, bool F32 = false, bool AG = false>
 int cluster_prepare(int dev) {
   constexpr int KS = cluster_ks(BMAX, F32);
   constexpr int smem = TcClusterConfig<BMAX, KS, F32>::SMEM_BYTES;
   static bool done[kMaxDev];
   std::lock_guard<std::mutex> lk(g_mu);
   if (!done[dev]) {
-    if (cudaFuncSetAttribute(tc_cluster_kernel<BMAX, KS, F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+    if (cudaFuncSetAttribute(tc_cluster_kernel<BMAX, KS, F32, AG>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
         cudaSuccess)
       return SIMSD_ERR_LAUNCH;
     done[dev] = true;
@@ -390,10 +390,10 @@ int max_clusters(int bmax, int S, int dev, bool f32 = false) {
   return 0;
 }
 
-template <int BMAX, bool F32 = false>
+template <int BMAX, bool F32 = false, bool AG = false>
 int launch_cluster_b(const TcClusterArgs& a, int S, int C, cudaStream_t s, int dev) {
   constexpr int KS = cluster_ks(BMAX, F32);
-  if (cluster_prepare<BMAX, F32>(dev) != SIMSD_OK) return SIMSD_ERR_LAUNCH;
+  if (cluster_prepare<BMAX, F32, AG>(dev) != SIMSD_OK) return SIMSD_ERR_LAUNCH;
   TcClusterArgs args = a;
   args.pdl = pdl_on() ? 1 : 0;
   args.prefetch = prefetch_stages();
@@ -418,11 +418,21 @@ int launch_cluster_b(const TcClusterArgs& a, int S, int C, cudaStream_t s, int d
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  if (cudaLaunchKernelEx(&cfg, tc_cluster_kernel<BMAX, KS, F32>, args) != cudaSuccess) return SIMSD_ERR_LAUNCH;
+  if (cudaLaunchKernelEx(&cfg, tc_cluster_kernel<BMAX, KS, F32, AG>, args) != cudaSuccess) return SIMSD_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? SIMSD_OK : SIMSD_ERR_LAUNCH;
 }
 
 int launch_cluster(int bmax, const TcClusterArgs& a, int S, int C, cudaStream_t s, int dev, bool f32 = false) {
+  if (a.world > 1) {
+    // fused all-gather: the instantiation with the peer-store epilogue (16-bit only)
+    if (f32) return SIMSD_ERR_UNSUPPORTED;
+    switch (bmax) {
+      case 16: return launch_cluster_b<16, false, true>(a, S, C, s, dev);
+      case 32: return launch_cluster_b<32, false, true>(a, S, C, s, dev);
+      case 64: return launch_cluster_b<64, false, true>(a, S, C, s, dev);
+    }
+    return SIMSD_ERR_UNSUPPORTED;
+  }
   switch (bmax) {
     case 16: return f32 ? launch_cluster_b<16, true>(a, S, C, s, dev) : launch_cluster_b<16>(a, S, C, s, dev);
     case 32: return f32 ? launch_cluster_b<32, true>(a, S, C, s, dev) : launch_cluster_b<32>(a, S, C, s, dev);
@@ -474,6 +484,19 @@ ClusterPlan plan_cluster(int bmax, long long tiles, int kb, int dev, bool f32 = 
   return best;
 }
 
+// The plan for `tiles` output tiles with the cluster size pinned to `S` (the
+// K split of each tile fixed): as many clusters as fit, tiles dealt evenly.
+ClusterPlan plan_cluster_with_s(int bmax, long long tiles, int S, int dev, bool f32 = false) {
+  ClusterPlan cp;
+  const long long cmax = std::min<long long>(max_clusters(bmax, S, dev, f32), cluster_cta_cap() / S);
+  if (cmax <= 0 || tiles <= 0) return cp;
+  const long long c0 = std::min(cmax, tiles);
+  const long long w = cdiv(tiles, c0);
+  cp.S = S;
+  cp.C = (int)cdiv(tiles, w);
+  return cp;
+}
+
 bool cluster_enabled() {
   static const bool v = env_choice("SIMSD_TC_CLUSTER", {0, 1}, 1) == 1;
   return v;
@@ -496,13 +519,20 @@ int thin_cluster(const void* x, long long ldx_m, const void* w, long long ldw_n,
                  void* y, long long ldy, int M, int N, int K, int dtype, bool silu, int* err, void* const* peer_y,
                  int col_offset, int world, int rank, void* const* peer_sig, cudaStream_t s, int dev,
                  unsigned long long* amax_keys = nullptr, long long* amax_idx = nullptr, int* amax_count = nullptr,
-                 const CatSpec* cat = nullptr) {
+                 const CatSpec* cat = nullptr, int plan_n = 0) {
   const bool f32 = dtype == SIMSD_F32;   // fp32 operands: 32-element K blocks, tf32 split on chip
   const long long esz = f32 ? 4 : 2;
   const int bmax = pick_bmax_rows(M);
   const long long row_tiles = silu ? cdiv(N, 64) : cdiv(N, 128);
   const int kb = (int)cdiv(K, f32 ? 32 : 64);
-  const ClusterPlan cp = plan_cluster(bmax, row_tiles, kb, dev, f32);
+  ClusterPlan cp = plan_cluster(bmax, row_tiles, kb, dev, f32);
+  if (plan_n > 0) {
+    // the K split a single-GPU call with plan_n output columns would use, so
+    // every output element is summed exactly as it would be there
+    const ClusterPlan full = plan_cluster(bmax, silu ? cdiv(plan_n, 64) : cdiv(plan_n, 128), kb, dev, f32);
+    if (full.S <= 0) return SIMSD_ERR_UNSUPPORTED;
+    cp = plan_cluster_with_s(bmax, row_tiles, full.S, dev, f32);
+  }
   if (cp.S <= 0) return SIMSD_ERR_UNSUPPORTED;
   if (ensure_encode() != SIMSD_OK) return SIMSD_ERR_DEVICE;
   TcClusterArgs a;
@@ -1380,8 +1410,9 @@ int simsd_ipc_close(void* dev_ptr) {
 int simsd_thin_linear_allgather(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w, int64_t ldw_n,
                                 int64_t ldw_k, const void* w_up, const void* bias, void* const* peer_y, int64_t ldy,
                                 int col_offset, int M, int N, int K, int dtype, int epilogue, int rank, int world,
-                                void* const* peer_signal, void* workspace, size_t workspace_bytes, void* stream) {
-  if (M < 1 || N < 1 || K < 1 || col_offset < 0) return SIMSD_ERR_SHAPE;
+                                void* const* peer_signal, int plan_n, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+  if (M < 1 || N < 1 || K < 1 || col_offset < 0 || plan_n < 0) return SIMSD_ERR_SHAPE;
   if (world < 2 || world > TC_AG_MAX_WORLD || rank < 0 || rank >= world) return SIMSD_ERR_UNSUPPORTED;
   if (dtype != SIMSD_BF16 && dtype != SIMSD_F16) return SIMSD_ERR_UNSUPPORTED;
   if (epilogue != SIMSD_EPI_NONE && epilogue != SIMSD_EPI_SILU_MUL) return SIMSD_ERR_UNSUPPORTED;
@@ -1399,7 +1430,17 @@ int simsd_thin_linear_allgather(const void* x, int64_t ldx_m, int64_t ldx_k, con
   if (dev < 0) return SIMSD_ERR_DEVICE;
   int* err = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + WS_ERR_OFFSET);
   return thin_cluster(x, ldx_m, w, ldw_n, w_up, bias, peer_y[rank], ldy, M, N, K, dtype, silu, err, peer_y,
-                      col_offset, world, rank, peer_signal, (cudaStream_t)stream, dev);
+                      col_offset, world, rank, peer_signal, (cudaStream_t)stream, dev, nullptr, nullptr, nullptr,
+                      nullptr, plan_n);
+}
+
+int simsd_allgather_wait(void* own_signal, int world, void* workspace, size_t workspace_bytes, void* stream) {
+  if (own_signal == nullptr || world < 2 || world > TC_AG_MAX_WORLD) return SIMSD_ERR_SHAPE;
+  if (workspace == nullptr || workspace_bytes < (size_t)WS_COUNTER_BYTES) return SIMSD_ERR_WORKSPACE;
+  if (current_device() < 0) return SIMSD_ERR_DEVICE;
+  int* err = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + WS_ERR_OFFSET);
+  return launch(ag_wait_kernel, dim3(1), dim3(32), 0, (cudaStream_t)stream, static_cast<int*>(own_signal), world,
+                err);
 }
 
 int simsd_thin_linear_argmax(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w, int64_t ldw_n,
@@ -1471,6 +1512,19 @@ int simsd_rmsnorm(const void* x, int64_t ldx, const void* res, int64_t ldres, vo
   a.n = n;
   a.dtype = dtype;
   a.eps = eps;
+  auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  const bool vec = (n & 7) == 0 && (ldx & 7) == 0 && (ldy & 7) == 0 && (!res || (ldres & 7) == 0) &&
+                   (!h_out || (ldh & 7) == 0) && al16(x) && al16(w) && al16(y) && (!res || al16(res)) &&
+                   (!h_out || al16(h_out));
+  if (vec) {
+    // 16-byte vectors, the row in registers (<= 8 vectors a thread)
+    const int vpt = (int)cdiv(n / 8, NORM_THREADS);
+    const dim3 g((unsigned)rows), b(NORM_THREADS);
+    if (vpt <= 1) return launch(rmsnorm_vec_kernel<1>, g, b, 0, (cudaStream_t)stream, a);
+    if (vpt <= 2) return launch(rmsnorm_vec_kernel<2>, g, b, 0, (cudaStream_t)stream, a);
+    if (vpt <= 4) return launch(rmsnorm_vec_kernel<4>, g, b, 0, (cudaStream_t)stream, a);
+    return launch(rmsnorm_vec_kernel<8>, g, b, 0, (cudaStream_t)stream, a);
+  }
   const int smem = (n + NORM_THREADS / 32) * (int)sizeof(float);
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)

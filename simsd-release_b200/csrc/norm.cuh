@@ -15,6 +15,7 @@
 // multiplied by 1/n as torch's mean does.
 #pragma once
 #include "sm100.cuh"
+#include "moe.cuh"   // unpack8
 
 namespace simsd {
 
@@ -70,6 +71,80 @@ __global__ void __launch_bounds__(NORM_THREADS) rmsnorm_kernel(const RmsNormArgs
     if (hr) store_f(hr, i, v, p.dtype);
     const float nv = round16(__fmul_rn(v, inv), p.dtype);
     store_f(yr, i, __fmul_rn(load_f(p.w, i, p.dtype), nv), p.dtype);
+  }
+}
+
+// The same RMSNorm for rows whose length is a multiple of 8 with 16-byte
+// aligned rows: thread t holds the 8-element vectors t, t + 256, ... of its row
+// in registers (VPT of them), so the row is read once with 16-byte loads, all
+// issued before the first use, and never staged in shared memory.  Mean-square
+// order: each thread sums its vectors' squares in element order, then the
+// warp's xor butterfly, then the warps in order.
+__device__ __forceinline__ uint4 pack8(const float (&f)[8], int dtype) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    w[i] = (uint32_t)f32_to_16bit(f[2 * i], dtype) | ((uint32_t)f32_to_16bit(f[2 * i + 1], dtype) << 16);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <int VPT>
+__global__ void __launch_bounds__(NORM_THREADS) rmsnorm_vec_kernel(const RmsNormArgs p) {
+  griddep_launch_dependents();
+  griddep_wait();
+  __shared__ float part[NORM_THREADS / 32];
+  const int r = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int nvec = p.n >> 3;
+  const uint4* xr = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(p.x) + (long long)r * p.ldx * 2);
+  const uint4* rr =
+      p.res ? reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(p.res) + (long long)r * p.ldres * 2)
+            : nullptr;
+  uint4 xa[VPT], ra[VPT];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int vi = tid + j * NORM_THREADS;
+    xa[j] = vi < nvec ? xr[vi] : make_uint4(0, 0, 0, 0);
+    ra[j] = (rr && vi < nvec) ? rr[vi] : make_uint4(0, 0, 0, 0);
+  }
+  float h[VPT][8];
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    unpack8(xa[j], p.dtype, h[j]);
+    if (rr) {
+      float b[8];
+      unpack8(ra[j], p.dtype, b);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) h[j][e] = round16(__fadd_rn(h[j][e], b[e]), p.dtype);
+    }
+    if (tid + j * NORM_THREADS < nvec) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = __fadd_rn(ss, __fmul_rn(h[j][e], h[j][e]));
+    }
+  }
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, m));
+  if ((tid & 31) == 0) part[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+#pragma unroll
+  for (int j = 0; j < NORM_THREADS / 32; ++j) tot = __fadd_rn(tot, part[j]);
+  const float inv = rsqrtf(__fadd_rn(__fmul_rn(tot, 1.0f / (float)p.n), p.eps));
+  uint4* yr = reinterpret_cast<uint4*>(reinterpret_cast<char*>(p.y) + (long long)r * p.ldy * 2);
+  uint4* hr = p.h_out ? reinterpret_cast<uint4*>(reinterpret_cast<char*>(p.h_out) + (long long)r * p.ldh * 2)
+                      : nullptr;
+  const uint4* wv = reinterpret_cast<const uint4*>(p.w);
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int vi = tid + j * NORM_THREADS;
+    if (vi >= nvec) break;
+    if (hr) hr[vi] = pack8(h[j], p.dtype);
+    float wf[8], o[8];
+    unpack8(wv[vi], p.dtype, wf);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = __fmul_rn(wf[e], round16(__fmul_rn(h[j][e], inv), p.dtype));
+    yr[vi] = pack8(o, p.dtype);
   }
 }
 

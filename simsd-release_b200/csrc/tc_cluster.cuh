@@ -34,7 +34,12 @@ namespace simsd {
 
 constexpr int TC_CL_MAX = 8;          // largest cluster (portable)
 constexpr int TC_AG_MAX_WORLD = 8;    // ranks of a fused column-parallel all-gather
-constexpr int TC_SIG_SLOTS = 16;      // launch slots of a rank's signal block, used round robin
+// A rank's signal block (ints): arrivals of every rank's finished fused
+// all-gather launches (each rank adds 1 per launch, cumulative), this rank's
+// CTAs finished in the current launch, and this rank's launch count.
+constexpr int AG_SIG_ARRIVED = 0;
+constexpr int AG_SIG_CTAS = 1;
+constexpr int AG_SIG_LAUNCHES = 2;
 constexpr int TC_CL_RED_ROWS = 144;   // >= S * rows one owner holds, for every S <= 8
 
 struct TcClusterArgs {
@@ -64,13 +69,13 @@ struct TcClusterArgs {
   long long* amax_idx;
   int* amax_count;
   unsigned long long* trace; // optional: 8 %globaltimer stamps per CTA (diagnostics)
-  // column-parallel all-gather (world > 1): every output element is stored at
-  // column col_offset + col of each rank's y (peer_out[r], NVLink mappings),
-  // then the ranks' CTAs meet on counters in peer_sig (see the kernel's end)
+  // column-parallel all-gather (world > 1, the AG instantiation): every output
+  // element is stored at column col_offset + col of each rank's y (peer_out[r],
+  // NVLink mappings); the launch's last CTA then counts the launch on every
+  // rank's signal block (peer_sig, AG_SIG_*) and nobody waits here: a reader
+  // of y waits first (ag_wait_kernel)
   int world, rank, col_offset;
   void* peer_out[TC_AG_MAX_WORLD];
-  // each rank's signal block (ints): [0, SLOTS) ranks arrived, [SLOTS, 2 SLOTS)
-  // this rank's CTAs arrived, [2 SLOTS] this rank's launch count
   int* peer_sig[TC_AG_MAX_WORLD];
 };
 
@@ -159,7 +164,7 @@ __device__ __forceinline__ unsigned long long amax_key(float v, int col, int odt
   return ((unsigned long long)k << 32) | (unsigned long long)(0xffffffffu - (uint32_t)col);
 }
 
-template <int BMAX, int KS, bool F32 = false>
+template <int BMAX, int KS, bool F32 = false, bool AG = false>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_constant__ TcClusterArgs p) {
   using Cfg = TcClusterConfig<BMAX, KS, F32>;
   constexpr int STAGES = Cfg::STAGES;
@@ -484,7 +489,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
     const int ep_g0 = ep_units > 0 ? row / ep_units : 0;
     const int ep_groups = (nrows_all + 3) >> 2;
     const bool ep_active = ep_units > 0 && ep_g0 < ep_P;
-    const bool ep_fast = p.amax_keys == nullptr && p.world <= 1;   // plain stores into y
+    // plain stores into y (AG: into every rank's y)
+    const bool ep_fast = p.amax_keys == nullptr && (AG || p.world <= 1);
     const long long ep_ld = p.ld_out;
     const int ep_silu = p.silu;
     const int ep_rows_out = p.rows_out;
@@ -658,9 +664,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
                   const int t = 4 * g + k4;
                   if (t < nrows_all) {
                     const float v = ep_silu ? silu_mul(va[k4], vb[k4]) : __fadd_rn(va[k4], ep_bias);
-                    if (!ep_fast) put(t, ep_col, v);
-                    else if constexpr (F32) reinterpret_cast<float*>(outp)[(long long)t * ep_ld + ep_col] = v;
-                    else yc[(long long)t * ep_ld] = f32_to_16bit(v, odt);
+                    if (!ep_fast) {
+                      put(t, ep_col, v);
+                    } else if constexpr (F32) {
+                      reinterpret_cast<float*>(outp)[(long long)t * ep_ld + ep_col] = v;
+                    } else if constexpr (AG) {
+                      const uint16_t bits = f32_to_16bit(v, odt);
+                      const long long at = (long long)t * ep_ld + p.col_offset + ep_col;
+                      for (int r = 0; r < p.world; ++r) reinterpret_cast<uint16_t*>(p.peer_out[r])[at] = bits;
+                    } else {
+                      yc[(long long)t * ep_ld] = f32_to_16bit(v, odt);
+                    }
                   }
                 }
               }
@@ -704,36 +718,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
       // aborting: give peers that may still be sending to this CTA time to land
       mbar_wait_cluster_drain(red_full_u32, done & 1, 100000000ull);
     }
-    if (p.world > 1) {
-      // Fused all-gather: the launch completes only when this rank's y is
-      // whole.  Each CTA counts itself on its own rank with a system-scope
-      // acquire-release add (after a CTA barrier, so it covers every epilogue
-      // thread's stores, local and remote); the rank's last CTA then adds 1,
-      // with release, to the rank counter of every rank; CTA 0 of each rank
-      // waits (bounded) until all ranks have added.  Slots follow this rank's
-      // launch count, kept on the device (graph replays advance it); every
-      // rank launches the same sequence, so the slots agree.
-      griddep_wait();   // the previous launch's count update is visible (no-op without PDL)
+    if constexpr (AG) {
+      // Fused all-gather: count this launch as done on every rank once all of
+      // this rank's CTAs have stored.  Each CTA counts itself with a
+      // system-scope acquire-release add (after a CTA barrier, so it covers
+      // every epilogue thread's stores, local and remote); the last one resets
+      // the CTA count, advances this rank's launch count and adds 1, with
+      // release, to the arrival counter of every rank.  Nothing waits here: a
+      // reader of y first runs ag_wait_kernel, which waits until its arrival
+      // counter reaches world x its launch count.
+      griddep_wait();   // the previous launch's counter updates are visible (no-op without PDL)
       named_bar_sync(1, 128);
       if (row == 0) {
         int* my_sig = p.peer_sig[p.rank];
-        const int seq = *reinterpret_cast<volatile int*>(my_sig + 2 * TC_SIG_SLOTS);
-        const int slot = seq & (TC_SIG_SLOTS - 1);
-        if (atom_add_acq_rel_sys(my_sig + TC_SIG_SLOTS + slot, 1) == (int)gridDim.x - 1) {
-          my_sig[TC_SIG_SLOTS + slot] = 0;   // every CTA of this launch has counted
-          for (int r = 0; r < p.world; ++r) red_add_release_sys(p.peer_sig[r] + slot, 1);
-        }
-        if (blockIdx.x == 0) {
-          const uint64_t t0 = globaltimer_ns();
-          while (ld_acquire_sys(my_sig + slot) < p.world) {
-            if (globaltimer_ns() - t0 > SIMSD_WAIT_LIMIT_NS) {
-              atomicOr(p.err, SIMSD_DEV_ERR_TIMEOUT);
-              break;
-            }
-          }
-          my_sig[slot] = 0;   // no rank adds to this slot again before this launch count comes round
-          __threadfence_system();
-          *reinterpret_cast<volatile int*>(my_sig + 2 * TC_SIG_SLOTS) = seq + 1;
+        if (atom_add_acq_rel_sys(my_sig + AG_SIG_CTAS, 1) == (int)gridDim.x - 1) {
+          my_sig[AG_SIG_CTAS] = 0;
+          volatile int* launches = my_sig + AG_SIG_LAUNCHES;
+          *launches = *launches + 1;
+          for (int r = 0; r < p.world; ++r) red_add_release_sys(p.peer_sig[r] + AG_SIG_ARRIVED, 1);
         }
       }
     }
@@ -750,6 +752,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
     tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
   if (p.trace && tid == 0) p.trace[blockIdx.x * 8 + 7] = globaltimer_ns();
+}
+
+// Reader side of the fused all-gather: one thread waits (bounded) until this
+// rank's arrival counter reaches world x its launch count, i.e. every rank has
+// stored its columns of every fused launch issued so far on this signal block
+// (counters are cumulative and compared modulo 2^32).  Launched on the stream
+// of those launches, before the kernels that read their outputs.
+__global__ void ag_wait_kernel(int* my_sig, int world, int* err) {
+  if (threadIdx.x != 0) return;
+  griddep_wait();
+  const unsigned target = (unsigned)*reinterpret_cast<volatile int*>(my_sig + AG_SIG_LAUNCHES) * (unsigned)world;
+  const uint64_t t0 = globaltimer_ns();
+  while ((int)((unsigned)ld_acquire_sys(my_sig + AG_SIG_ARRIVED) - target) < 0) {
+    if (globaltimer_ns() - t0 > SIMSD_WAIT_LIMIT_NS) {
+      atomicOr(err, SIMSD_DEV_ERR_TIMEOUT);
+      break;
+    }
+  }
+  __threadfence_system();
 }
 
 }  // namespace simsd

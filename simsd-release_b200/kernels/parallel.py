@@ -157,17 +157,22 @@ class SymmetricBlock:
 class FusedAllGather:
     """Column-parallel thin linears whose all-gather is fused into the GEMM
     (simsd_thin_linear_allgather): each rank stores its columns straight into
-    every rank's output over NVLink, then the ranks meet on device counters.
+    every rank's output over NVLink and counts the launch on every rank's
+    signal block; a reader waits for the counts (simsd_allgather_wait) before
+    it reads.  No rank waits for the others at the end of a launch, so ranks
+    only meet where an output is actually read.
 
-    `linear(x, w_local, w_up_local=None, bias_local=None)` returns the full
-    [M, world * n] output.  It lives in buffers this object owns, two per
-    output shape used in turn, so a result stays valid until the second-next
-    call with the same shape.  Peers write into them, and every launch ends
-    with all ranks meeting, so a peer runs at most one fused launch ahead:
-    consume each result before issuing the next fused call (as a model's next
-    op does).  Calls are collective: every rank makes the same sequence of
-    calls with the same shapes.  Shapes the fused kernel does not take (M > 64,
-    fp32, odd layouts) fall back to thin_linear and gather_columns (NCCL).
+    `linear(x, w_local, w_up_local=None, bias_local=None, wait=True)` returns
+    the full [M, world * n] output; with `wait=False` the output is complete
+    only after a later `wait()` on the same stream (several launches may share
+    one wait).  Outputs live in buffers this object owns, two per output shape
+    used in turn, so a result stays valid until the second-next call with the
+    same shape.  Peers write into them: consume each result before issuing the
+    call after next with the same shape, and keep at most one unwaited call
+    per shape in flight.  Calls are collective: every rank makes the same
+    sequence of calls with the same shapes.  Shapes the fused kernel does not
+    take (M > 64, fp32, odd layouts) fall back to thin_linear and
+    gather_columns (NCCL), which are complete on return.
     """
 
     def __init__(self, group=None):
@@ -191,7 +196,10 @@ class FusedAllGather:
         return blk.tensor.view(dtype).view(M, N), self._out_arrs[key]
 
     def linear(self, x: torch.Tensor, w: torch.Tensor, w_up: torch.Tensor | None = None,
-               bias: torch.Tensor | None = None) -> torch.Tensor:
+               bias: torch.Tensor | None = None, wait: bool = True, plan_n: int = 0) -> torch.Tensor:
+        """`plan_n` > 0 (the unsharded output width): split K exactly as one GPU
+        would for that width, so the gathered output is bit-identical to the
+        single-GPU thin linear."""
         M, K = x.shape
         n = w.shape[0]
         N = n * self.world
@@ -203,12 +211,22 @@ class FusedAllGather:
             x.data_ptr(), x.stride(0), x.stride(1), w.data_ptr(), w.stride(0), w.stride(1),
             w_up.data_ptr() if w_up is not None else None, bias.data_ptr() if bias is not None else None,
             peers, N, self.rank * n, M, n, K, code, _lib.EPI_SILU_MUL if w_up is not None else _lib.EPI_NONE,
-            self.rank, self.world, self._sig_arr, ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
+            self.rank, self.world, self._sig_arr, plan_n, ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
         if rc == _lib.SIMSD_ERR_UNSUPPORTED:
             local = thin_linear_silu_mul(x, w, w_up) if w_up is not None else thin_linear(x, w, bias)
             return gather_columns(local, self.group)
         _lib.check(rc, "thin_linear_allgather")
+        if wait:
+            self.wait(dev)
         return y
+
+    def wait(self, dev: torch.device | None = None) -> None:
+        """Make every fused output issued so far on the current stream complete
+        on this rank (one bounded device-side wait; no host synchronisation)."""
+        dev = dev or torch.device("cuda", torch.cuda.current_device())
+        ws = _lib.workspace(dev, _lib.lib().simsd_workspace_header_bytes())
+        _lib.check(_lib.lib().simsd_allgather_wait(self.sig.own, self.world, ws.data_ptr(), ws.numel(),
+                                                   _lib.stream_ptr(dev)), "allgather_wait")
 
     def close(self) -> None:
         for blk in self.outs.values():

@@ -79,18 +79,26 @@ def case_fused(dev):
             ref_h = thin_linear_silu_mul(x, wg, wu)
             ref_d = thin_linear(x64, wd)
             wl, wgl, wul, wdl = (column_shard(t, rank, world) for t in (w, wg, wu, wd))
-            for _ in range(40):          # more launches than counter slots
+            for _ in range(40):          # many launches on the cumulative counters
                 y = ag.linear(x, wl)
                 h = ag.linear(x, wgl, wul)
                 d = ag.linear(x64, wdl)
+                assert _close(y, ref) and _close(h, ref_h) and _close(d, ref_d)
+            # deferred: three launches, one wait
+            for _ in range(5):
+                y = ag.linear(x, wl, wait=False)
+                h = ag.linear(x, wgl, wul, wait=False)
+                d = ag.linear(x64, wdl, wait=False)
+                ag.wait()
                 assert _close(y, ref) and _close(h, ref_h) and _close(d, ref_d)
             torch.cuda.synchronize()
             first = ag.linear(x, wl).clone()
             assert torch.equal(first, ag.linear(x, wl))          # bit-identical across calls
             gr = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gr):
-                yg = ag.linear(x, wl)
-                hg = ag.linear(x, wgl, wul)
+                yg = ag.linear(x, wl, wait=False)
+                hg = ag.linear(x, wgl, wul, wait=False)
+                ag.wait()
             for _ in range(5):
                 gr.replay()
             torch.cuda.synchronize()
@@ -104,7 +112,44 @@ def case_fused(dev):
         ag.close()
 
 
-CASES = {"column": case_column, "ep": case_ep, "fused": case_fused}
+def case_verify_tp(dev):
+    """The verify forward with every linear column-split (fused all-gather, K
+    split pinned to the single-GPU plan): hidden states and greedy tokens equal
+    to the single-GPU fused forward bit for bit, on 3 SDAR-8B-wide layers."""
+    from kernels import fused_toggle
+    from kernels.sdar_verify import SDARShape, SDARVerifyModel, VerifyHarness
+    from kernels.sdar_verify_tp import ShardedVerify
+    s = SDARShape(layers=3)
+    K, BL, P = 4, 4, 128
+    model = SDARVerifyModel.random_init(s, dev, seed=5)
+    g = torch.Generator().manual_seed(6)
+    prompt = torch.randint(0, s.vocab, (P,), generator=g).tolist()
+    drafts = [torch.randint(0, s.vocab, (BL,), generator=g).tolist() for _ in range(K)]
+    smaps = [torch.randperm(BL, generator=g).tolist() for _ in range(K)]
+    h = VerifyHarness(model, prompt, drafts, smaps, BL)
+    sv = ShardedVerify(model)
+    try:
+        fused_toggle.apply_to_model(model, True, fuse_gate_up=True, fuse_qkv=True)
+        with torch.inference_mode():
+            for trial in range(3):
+                d = [[(t * 7 + trial) % s.vocab for t in blk] for blk in drafts]
+                h.set_drafts(d, smaps)
+                h.fused = True
+                h1, id1 = h.window_hidden().clone(), h.window_argmax().clone()
+                h.fused = False
+                hg, idg = sv.window_hidden(h).clone(), sv.window_argmax(h).clone()
+                torch.cuda.synchronize()
+                assert torch.equal(h1, hg), ("hidden", trial, float((h1.float() - hg.float()).abs().max()))
+                assert torch.equal(id1, idg), ("argmax", trial)
+        fused_toggle.apply_to_model(model, False)
+        dist.barrier()
+        from kernels import _lib
+        assert _lib.device_error(dev) == 0
+    finally:
+        sv.close()
+
+
+CASES = {"column": case_column, "ep": case_ep, "fused": case_fused, "verify_tp": case_verify_tp}
 
 
 def main():
