@@ -14,6 +14,7 @@
 #include "moe.cuh"
 #include "norm.cuh"
 #include "attn.cuh"
+#include "attn_tc.cuh"
 #include "simsd_b200.h"
 #include "simt_gemm.cuh"
 #include "tc_cluster.cuh"
@@ -495,6 +496,46 @@ ClusterPlan plan_cluster_with_s(int bmax, long long tiles, int S, int dev, bool 
   cp.S = S;
   cp.C = (int)cdiv(tiles, w);
   return cp;
+}
+
+// Clusters of S CTAs of attn_tc_kernel that fit on the device at once (0: S does
+// not run here).  Sets the kernel's shared-memory and cluster-size attributes.
+int attn_max_clusters(int S, int dev) {
+  static int cache[kMaxDev][ATC_CL_MAX_NP + 1];
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (cache[dev][S] != 0) return cache[dev][S] > 0 ? cache[dev][S] : 0;
+  }
+  if (cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ATC_SMEM) != cudaSuccess ||
+      cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)S);
+  cfg.blockDim = dim3(ATC_THREADS);
+  cfg.dynamicSmemBytes = ATC_SMEM;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = (unsigned)S;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, attn_tc_kernel, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    n = 0;
+  }
+  std::lock_guard<std::mutex> lk(g_mu);
+  cache[dev][S] = n > 0 ? n : -1;
+  return n > 0 ? n : 0;
+}
+
+// SIMSD_ATTN_TC=0 keeps verify attention on the mma.sync split kernel + combine.
+bool attn_tc_enabled() {
+  static const bool v = env_choice("SIMSD_ATTN_TC", {0, 1}, 1) == 1;
+  return v;
 }
 
 bool cluster_enabled() {
@@ -1580,6 +1621,75 @@ int simsd_verify_attention(const void* q, const void* k_cache, const void* v_cac
   const int nch = (int)cdiv(Lk, ATT_KC);
   if (workspace == nullptr || workspace_bytes < simsd_verify_attention_workspace_size(Hq, Hk, L, Lk))
     return SIMSD_ERR_WORKSPACE;
+  const int dev = current_device();
+  if (dev < 0) return SIMSD_ERR_DEVICE;
+  cudaStream_t st = (cudaStream_t)stream;
+  // tensor cores (tcgen05), one cluster of up to 8 CTAs per KV head: needs at
+  // most 3 key tiles per CTA and TMA-describable q / caches
+  const int ntiles = (int)cdiv(Lk, ATC_TILE);
+  if (attn_tc_enabled() && scale > 0.0f && ntiles <= ATC_CL_MAX * ATC_NT_MAX && (long long)Hk * cache_cap < (1LL << 31) &&
+      (long long)Hq * L < (1LL << 31) && ensure_encode() == SIMSD_OK) {
+    AttnTcArgs t;
+    memset(&t, 0, sizeof(t));
+    const uint64_t qd[2] = {128, (uint64_t)Hq * L}, kd[2] = {128, (uint64_t)(Hk * cache_cap)};
+    const uint64_t rs[1] = {256};
+    int rc = encode_map(&t.tmQ, q, SIMSD_BF16, 2, qd, rs, 128);
+    if (rc == SIMSD_OK) rc = encode_map(&t.tmK, k_cache, SIMSD_BF16, 2, kd, rs, 128);
+    if (rc == SIMSD_OK) rc = encode_map(&t.tmV, v_cache, SIMSD_BF16, 2, kd, rs, 128);
+    if (rc == SIMSD_OK) {
+      t.mask = mask;
+      t.o = o;
+      t.err = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + WS_ERR_OFFSET);
+      t.cap = cache_cap;
+      t.ldm = ldmask;
+      t.Hq = Hq;
+      t.Hk = Hk;
+      t.L = L;
+      t.Lk = Lk;
+      t.ntiles = ntiles;
+      t.mask_vec = ((ldmask & 15) == 0 && al16(mask)) ? 1 : 0;
+      t.scale_log2 = scale * 1.4426950408889634f;
+      // at most two key tiles per CTA where a cluster that large runs here
+      // (every tile's loads then issue at once), else up to three in 8
+      int S = std::min(ATC_CL_MAX, ntiles);
+      const int S2 = (int)cdiv(ntiles, 2);
+      if (S2 > ATC_CL_MAX && S2 <= ATC_CL_MAX_NP && attn_max_clusters(S2, dev) > 0) S = S2;
+      t.trace = trace_slot((long long)Hk * S);
+      {
+        static bool done_tc[kMaxDev];
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (!done_tc[dev]) {
+          if (cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ATC_SMEM) !=
+              cudaSuccess)
+            return SIMSD_ERR_LAUNCH;
+          (void)cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+          (void)cudaGetLastError();
+          done_tc[dev] = true;
+        }
+      }
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)(Hk * S));
+      cfg.blockDim = dim3(ATC_THREADS);
+      cfg.dynamicSmemBytes = ATC_SMEM;
+      cfg.stream = st;
+      cudaLaunchAttribute attr[2];
+      int na = 0;
+      attr[na].id = cudaLaunchAttributeClusterDimension;
+      attr[na].val.clusterDim.x = (unsigned)S;
+      attr[na].val.clusterDim.y = 1;
+      attr[na].val.clusterDim.z = 1;
+      ++na;
+      if (pdl_on()) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+      }
+      cfg.attrs = attr;
+      cfg.numAttrs = na;
+      if (cudaLaunchKernelEx(&cfg, attn_tc_kernel, t) != cudaSuccess) return SIMSD_ERR_LAUNCH;
+      return cudaGetLastError() == cudaSuccess ? SIMSD_OK : SIMSD_ERR_LAUNCH;
+    }
+  }
   AttnArgs a;
   a.q = q;
   a.k = k_cache;
@@ -1599,8 +1709,6 @@ int simsd_verify_attention(const void* q, const void* k_cache, const void* v_cac
   constexpr int smem = 3 * 32768;
   {
     static bool done[kMaxDev];
-    const int dev = current_device();
-    if (dev < 0) return SIMSD_ERR_DEVICE;
     std::lock_guard<std::mutex> lk(g_mu);
     if (!done[dev]) {
       if (cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
@@ -1608,7 +1716,6 @@ int simsd_verify_attention(const void* q, const void* k_cache, const void* v_cac
       done[dev] = true;
     }
   }
-  cudaStream_t st = (cudaStream_t)stream;
   int rc = launch(attn_split_kernel, dim3((unsigned)nch, (unsigned)Hk), dim3(ATT_THREADS), smem, st, a);
   if (rc != SIMSD_OK) return rc;
   const long long units = (long long)Hk * (Hq / Hk) * L;

@@ -98,16 +98,23 @@ def test_qk_norm_rope_matches_torch():
     assert bool((kc[:, :P] == 0).all()) and bool((vc[:, :P] == 0).all())   # other rows untouched
 
 
-@pytest.mark.parametrize("Hq,Hk,L,Lk,cap,pmask", [(32, 8, 32, 2080, 2080, 0.0), (32, 8, 32, 2080, 2100, 0.3),
-                                                  (16, 8, 8, 300, 320, 0.5), (32, 8, 4, 129, 129, 0.0),
-                                                  (8, 8, 16, 1000, 1000, 0.9)])
-def test_verify_attention_matches_fp32_reference(Hq, Hk, L, Lk, cap, pmask):
+# Lk up to 24 x 128 keys runs the tcgen05 cluster kernel (1-3 key tiles per
+# CTA, clusters of 2..8), longer contexts the mma.sync split kernel + combine;
+# mask rows of a 16-byte multiple take the vector mask loads
+@pytest.mark.parametrize("Hq,Hk,L,Lk,cap,pmask,mpad", [(32, 8, 32, 2080, 2080, 0.0, 5), (32, 8, 32, 2080, 2100, 0.3, 5),
+                                                       (16, 8, 8, 300, 320, 0.5, 5), (32, 8, 4, 129, 129, 0.0, 5),
+                                                       (8, 8, 16, 1000, 1000, 0.9, 5), (32, 8, 32, 2080, 2112, 0.2, 0),
+                                                       (32, 8, 32, 3072, 3072, 0.1, 0), (8, 8, 16, 4000, 4000, 0.2, 0),
+                                                       (32, 8, 32, 100, 100, 0.0, 12)])
+def test_verify_attention_matches_fp32_reference(Hq, Hk, L, Lk, cap, pmask, mpad):
     g = torch.Generator(device=DEV).manual_seed(Lk + L)
     bf = torch.bfloat16
     q = torch.randn(Hq, L, 128, generator=g, device=DEV).to(bf)
     kc = torch.randn(Hk, cap, 128, generator=g, device=DEV).to(bf)
     vc = torch.randn(Hk, cap, 128, generator=g, device=DEV).to(bf)
-    mask = torch.rand(L, Lk + 5, generator=g, device=DEV) >= pmask
+    if cap > Lk:
+        vc[:, Lk:] = float("nan")                       # rows past Lk never reach the output
+    mask = torch.rand(L, Lk + mpad, generator=g, device=DEV) >= pmask
     mask[:, 0] = True                                   # every row sees a key
     mask[0, 1:] = False                                 # row 0: one key only
     scale = 128 ** -0.5
