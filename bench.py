@@ -371,10 +371,21 @@ def gpu_arm(args):
         e3.record()
         torch.cuda.synchronize()
         e2e_ms = e2.elapsed_time(e3) / e2e_steps
+        # the same step issued eagerly, call by call from Python (no graph): the
+        # per-call host cost of the public API is inside this one
+        torch.cuda.synchronize()
         if dist:
-            t = torch.tensor([e2e_ms], device=dev)
+            dist.barrier()
+        e2.record()
+        for i in range(e2e_steps):
+            e2e_step(i % POOL)
+        e3.record()
+        torch.cuda.synchronize()
+        e2e_eager_ms = e2.elapsed_time(e3) / e2e_steps
+        if dist:
+            t = torch.tensor([e2e_ms, e2e_eager_ms], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e_ms = float(t.item())
+            e2e_ms, e2e_eager_ms = float(t[0].item()), float(t[1].item())
         del houts
         e2e_graphs.clear()
         del ge
@@ -412,7 +423,10 @@ def gpu_arm(args):
                 "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "path": "kernels.thin_linear_fused public API -> libsimsd_b200 C ABI, replayed from a CUDA graph "
                         "with the copies inside: pinned host inputs -> device per activation height and each "
-                        "result -> pinned host on side streams, overlapping the linears"},
+                        "result -> pinned host on side streams, overlapping the linears",
+                "eager": {"value": round(total_bytes / (e2e_eager_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                          "ms_per_step": round(e2e_eager_ms, 4),
+                          "note": "the same calls issued from Python each step, no CUDA graph"}},
         "gpu_launches": args.steps * launches_per_step,
     }
     if per is not None:

@@ -41,6 +41,7 @@ constexpr int ATC_NT_MAX = 3;      // key tiles per CTA (TMEM: S + 3 O accumulat
 constexpr int ATC_CL_MAX = 8;      // CTAs per cluster (portable)
 constexpr int ATC_CL_MAX_NP = 16;  // non-portable cluster size, where the device runs it
 constexpr int ATC_REC = 132;       // floats per merged row record: O[128], M, L, 2 pad
+constexpr int ATC_G4 = ATC_REC / 4;  // its 16-byte groups
 constexpr int ATC_Q_BYTES = 32768;            // 128 rows x 128 dims bf16, two 64-dim atoms
 constexpr int ATC_STAGE_BYTES = 65536;        // K tile + V tile
 constexpr int ATC_P_BYTES = 32768;            // 128 rows x 128 keys bf16, two 64-key atoms
@@ -427,14 +428,15 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attn_tc_kernel(const __grid_co
     const uint32_t bar_u32 = smem_u32(recv_full);
     const int own_rows = max(0, min(RP, R - q * RP));
     if (st_id == 0) mbar_arrive_expect_tx(bar_u32, (uint32_t)((S - 1) * own_rows * ATC_REC * 4));
+    // records are stored group-major, [sender][16-byte group][row of the owner's
+    // slice], so the 32 rows of a warp write contiguous runs
+    auto g4_off = [&](int sender, int g4, int r) { return ((sender * ATC_G4 + g4) * RP + r) * 4; };
     {
       // every lane runs the TMEM loads (tcgen05.ld is warp-collective); only
       // live rows send or park their half of the record
-      const uint32_t rec = (uint32_t)(((q * RP) + lr) * ATC_REC * 4);
       const int own_c = live ? own : q;
-      const uint32_t dst = mapa_shared(recv_u32 + rec, (uint32_t)own_c);
+      const uint32_t dst = mapa_shared(recv_u32, (uint32_t)own_c);
       const uint32_t dbar = mapa_shared(bar_u32, (uint32_t)own_c);
-      float* mine = recv + ((q * RP) + lr) * ATC_REC;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         const int col = 64 * hc + 16 * c;
@@ -454,20 +456,22 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attn_tc_kernel(const __grid_co
         if (live) {
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
+            const int off = g4_off(q, (col >> 2) + u, lr);
             if (own == q)
-              *reinterpret_cast<float4*>(mine + col + 4 * u) =
+              *reinterpret_cast<float4*>(recv + off) =
                   make_float4(acc[4 * u], acc[4 * u + 1], acc[4 * u + 2], acc[4 * u + 3]);
             else
-              st_async_v4(dst + (uint32_t)((col + 4 * u) * 4), acc[4 * u], acc[4 * u + 1], acc[4 * u + 2],
-                          acc[4 * u + 3], dbar);
+              st_async_v4(dst + (uint32_t)(off * 4), acc[4 * u], acc[4 * u + 1], acc[4 * u + 2], acc[4 * u + 3],
+                          dbar);
           }
         }
       }
       if (live && hc == 0) {
+        const int off = g4_off(q, ATC_G4 - 1, lr);
         if (own == q)
-          *reinterpret_cast<float4*>(mine + 128) = make_float4(M, Lsum, 0.0f, 0.0f);
+          *reinterpret_cast<float4*>(recv + off) = make_float4(M, Lsum, 0.0f, 0.0f);
         else
-          st_async_v4(dst + 128 * 4, M, Lsum, 0.0f, 0.0f, dbar);
+          st_async_v4(dst + (uint32_t)(off * 4), M, Lsum, 0.0f, 0.0f, dbar);
       }
     }
     if (tr && st_id == 0) tr[6] = globaltimer_ns();
@@ -478,16 +482,16 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) attn_tc_kernel(const __grid_co
       for (int item = st_id; item < own_rows * 32; item += ATC_SM_THREADS) {
         const int r = item >> 5, d4 = item & 31;
         float Mt = NEG;
-        for (int s2 = 0; s2 < S; ++s2) Mt = fmaxf(Mt, recv[((s2 * RP) + r) * ATC_REC + 128]);
+        for (int s2 = 0; s2 < S; ++s2) Mt = fmaxf(Mt, recv[g4_off(s2, ATC_G4 - 1, r)]);
         float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         float den = 0.0f;
         if (Mt != NEG) {
           for (int s2 = 0; s2 < S; ++s2) {
-            const float* rec = recv + ((s2 * RP) + r) * ATC_REC;
-            if (rec[128] == NEG) continue;
-            const float w = exp2f(rec[128] - Mt);
-            den = __fadd_rn(den, __fmul_rn(w, rec[129]));
-            const float4 ov = reinterpret_cast<const float4*>(rec)[d4];
+            const float2 ml = *reinterpret_cast<const float2*>(recv + g4_off(s2, ATC_G4 - 1, r));
+            if (ml.x == NEG) continue;
+            const float w = exp2f(ml.x - Mt);
+            den = __fadd_rn(den, __fmul_rn(w, ml.y));
+            const float4 ov = *reinterpret_cast<const float4*>(recv + g4_off(s2, d4, r));
             acc.x = __fadd_rn(acc.x, __fmul_rn(w, ov.x));
             acc.y = __fadd_rn(acc.y, __fmul_rn(w, ov.y));
             acc.z = __fadd_rn(acc.z, __fmul_rn(w, ov.z));

@@ -330,10 +330,12 @@ ThinPlan plan_thin(int M, int N, int K, int epilogue, int split, int sms) {
 }
 
 // ---------------------------------------------------------------- cluster path
-// K atoms per ring stage of tc_cluster_kernel (its ring shares shared memory
-// with the cluster receive buffer, so 64-row tiles use single-atom stages).
-// fp32 operands (F32) hold every atom twice (tf32 hi and lo parts): one atom a stage.
-constexpr int cluster_ks(int bmax, bool f32 = false) { return f32 ? 1 : (bmax <= 32 ? 2 : 1); }
+// K atoms per ring stage of tc_cluster_kernel: two (per-stage barrier and
+// issue overheads halve; at 64 activation rows that leaves three stages, 96 KB
+// of weights in flight, and still measured 12-14 % faster than seven
+// single-atom stages).  fp32 operands (F32) hold every atom twice (tf32 hi and
+// lo parts): one atom a stage.
+constexpr int cluster_ks(int bmax, bool f32 = false) { return f32 ? 1 : (bmax <= 64 ? 2 : 1); }
 
 template <int BMAX, bool F32 = false, bool AG = false>
 int cluster_prepare(int dev) {

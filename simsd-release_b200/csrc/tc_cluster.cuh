@@ -761,6 +761,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
 // of those launches, before the kernels that read their outputs.
 __global__ void ag_wait_kernel(int* my_sig, int world, int* err) {
   if (threadIdx.x != 0) return;
+  griddep_launch_dependents();   // the reader may launch and set up; its own wait covers this kernel
   griddep_wait();
   const unsigned target = (unsigned)*reinterpret_cast<volatile int*>(my_sig + AG_SIG_LAUNCHES) * (unsigned)world;
   const uint64_t t0 = globaltimer_ns();

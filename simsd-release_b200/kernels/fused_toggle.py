@@ -222,24 +222,50 @@ def warmup(model: nn.Module, block_length: int = 4, extra_M=()) -> None:
 _MOE_ATTR = "_simsd_fused_moe"
 
 
-def apply_moe_to_model(model: nn.Module, enable: bool = True) -> int:
+def _free_expert_weights(experts) -> None:
+    for e in experts:
+        for name in ("gate_proj", "up_proj", "down_proj"):
+            lin = getattr(e, name)
+            lin.weight.data = lin.weight.data.new_empty(0)
+
+
+def apply_moe_to_model(model: nn.Module, enable: bool = True, pack_dir=None) -> int:
     """Switch LLaDA2 MoE blocks to the fused dispatch.  Idempotent.
 
     Stacks each block's expert weights (releasing the per-expert copies) and
     patches the block class's `moe_infer` once.  Disabling is not supported
     (the per-expert weights are gone): it raises NotImplementedError, as the
     reference does.  Must run before any CUDA-graph capture.
+
+    `pack_dir` (a directory): each block's stacked weights are persisted there
+    as `<module path>.simsd-experts` (kernels/expert_pack.py) the first time
+    and read back from that file on later installs, on the device the block's
+    experts live on.
     """
     from .moe_dispatch_fused import moe_dispatch, stack_expert_weights
 
     n = 0
-    for mod in model.modules():
+    for name, mod in model.named_modules():
         if mod.__class__.__name__ != "LLaDA2MoeSparseMoeBlock":
             continue
         if enable:
             if getattr(mod, _MOE_ATTR, None) is not None:
                 continue
-            setattr(mod, _MOE_ATTR, stack_expert_weights(mod.experts))
+            if pack_dir is not None:
+                from pathlib import Path
+
+                from .expert_pack import load_packed, pack_stacked
+                path = Path(pack_dir) / f"{name or 'moe'}.simsd-experts"
+                dev = mod.experts[0].gate_proj.weight.device
+                if path.exists():
+                    stacked = load_packed(path, dev)
+                    _free_expert_weights(mod.experts)
+                else:
+                    stacked = stack_expert_weights(mod.experts)
+                    pack_stacked(path, *stacked)
+            else:
+                stacked = stack_expert_weights(mod.experts)
+            setattr(mod, _MOE_ATTR, stacked)
             n += 1
         elif getattr(mod, _MOE_ATTR, None) is not None:
             raise NotImplementedError(

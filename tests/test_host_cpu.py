@@ -195,3 +195,42 @@ def test_stack_expert_weights_keeps_originals_on_request():
     assert wg.is_contiguous() and wg.shape == (3, 4, 8) and wd.shape == (3, 8, 4)
     assert blk.experts[2].up_proj.weight.numel() == 32
     assert torch.equal(wu[2], blk.experts[2].up_proj.weight)
+
+
+# ------------------------------------------------------------------ packed experts on disk
+def test_expert_pack_round_trip_and_checks(tmp_path):
+    from kernels.expert_pack import load_packed, pack_experts, read_header
+    for dtype in (torch.bfloat16, torch.float16, torch.float32):
+        blk = LLaDA2MoeSparseMoeBlock(E=5, H=24, I=12).to(dtype)
+        ref = stack_expert_weights(blk.experts, free_originals=False)
+        path = pack_experts(tmp_path / f"l0_{dtype}.simsd-experts", blk.experts)
+        hdr = read_header(path)
+        assert (hdr["E"], hdr["I"], hdr["H"]) == (5, 12, 24)
+        assert all(a["offset"] % 4096 == 0 for a in hdr["arrays"])
+        got = load_packed(path, "cpu")
+        for a, b in zip(got, ref):
+            assert a.dtype == dtype and torch.equal(a, b)
+    # a flipped byte in the data fails the checksum; a wrong magic fails the header
+    raw = bytearray(path.read_bytes())
+    raw[hdr["arrays"][1]["offset"] + 3] ^= 0x40
+    bad = tmp_path / "bad.simsd-experts"
+    bad.write_bytes(bytes(raw))
+    with pytest.raises(ValueError, match="checksum"):
+        load_packed(bad, "cpu")
+    bad.write_bytes(b"NOTAPACK" + bytes(raw[8:]))
+    with pytest.raises(ValueError, match="not a simsd expert pack"):
+        load_packed(bad, "cpu")
+
+
+def test_moe_toggle_writes_then_reads_packs(tmp_path):
+    torch.manual_seed(0)
+    m1 = nn.Sequential(LLaDA2MoeSparseMoeBlock(), LLaDA2MoeSparseMoeBlock())
+    m2 = nn.Sequential(LLaDA2MoeSparseMoeBlock(), LLaDA2MoeSparseMoeBlock())
+    m2.load_state_dict(m1.state_dict())
+    assert fused_toggle.apply_moe_to_model(m1, pack_dir=tmp_path) == 2          # stacks and writes
+    assert sorted(p.name for p in tmp_path.iterdir()) == ["0.simsd-experts", "1.simsd-experts"]
+    assert fused_toggle.apply_moe_to_model(m2, pack_dir=tmp_path) == 2          # reads back
+    for b1, b2 in zip(m1, m2):
+        for a, b in zip(getattr(b1, "_simsd_fused_moe"), getattr(b2, "_simsd_fused_moe")):
+            assert torch.equal(a, b)
+    assert m2[1].experts[0].down_proj.weight.numel() == 0                      # originals released
