@@ -527,13 +527,25 @@ def ep_moe_bench(dev, rank: int, world: int, dist, steps: int, cpu_seconds: floa
                 dist.all_reduce(active, op=dist.ReduceOp.MAX)
             n_active = int(active.sum().item())
 
+            # the N(0, 0.5) router bias concentrates the tokens on a few dozen
+            # experts: the grouped GEMMs split the experts by size
             def layer():
                 if world == 1:
-                    return moe_layer(x, wr, bias, k, wg, wu, wd, shared=shared)
-                return ep_moe_layer(x, wr, bias, k, wg, wu, wd, E, shared=shared)
+                    return moe_layer(x, wr, bias, k, wg, wu, wd, shared=shared, size_classes=True)
+                return ep_moe_layer(x, wr, bias, k, wg, wu, wd, E, shared=shared, size_classes=True)
 
             for _ in range(3):
                 layer()
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            # replayed from a CUDA graph (routing, buckets and all-to-alls
+            # included: every size is fixed, nothing syncs with the host)
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                layer()
+            for _ in range(3):
+                gr.replay()
             torch.cuda.synchronize()
             if world > 1:
                 dist.barrier()
@@ -541,10 +553,12 @@ def ep_moe_bench(dev, rank: int, world: int, dist, steps: int, cpu_seconds: floa
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
             for _ in range(n):
-                layer()
+                gr.replay()
             e1.record()
             torch.cuda.synchronize()
             ms = e0.elapsed_time(e1) / n
+            del gr
+            torch.cuda.synchronize()
             if world > 1:
                 t = torch.tensor([ms], device=dev)
                 dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -568,7 +582,8 @@ def ep_moe_bench(dev, rank: int, world: int, dist, steps: int, cpu_seconds: floa
     return {"cpu_baseline": res_cpu,
             "workload": "EP MoE layer, BASELINE configs[4]: H=4096, E=256 (E/N per GPU), top-8 sigmoid+bias(N(0,0.5)), "
                         "I=1536 SiLU*mul experts + 1 shared expert, bf16, T tokens split over N GPUs, "
-                        "all-to-all in fixed-capacity buckets (eager launches)",
+                        "all-to-all in fixed-capacity buckets, CUDA-graph replay; grouped GEMMs split by "
+                        "expert size (size_classes, for the skewed routing)",
             "metric": "MoE layer HBM GB/s, all GPUs (algorithmic bytes: active experts + per-GPU shared/router + "
                       "activations); frac_roofline = max(bytes / HBM peak, flops / sustained bf16 peak) / time",
             "n_gpus": world, "per_T": out}

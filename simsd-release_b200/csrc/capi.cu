@@ -699,7 +699,8 @@ const char* simsd_status_string(int s) {
 }
 
 int simsd_set_launch_flags(int flags) {
-  return g_launch_flags.exchange(flags & (SIMSD_LAUNCH_PDL | SIMSD_LAUNCH_INKERNEL_REDUCE | SIMSD_LAUNCH_GROUPED_FIXUP));
+  return g_launch_flags.exchange(flags & (SIMSD_LAUNCH_PDL | SIMSD_LAUNCH_INKERNEL_REDUCE | SIMSD_LAUNCH_GROUPED_FIXUP |
+                                         SIMSD_LAUNCH_MOE_SIZE_CLASSES));
 }
 
 int simsd_get_launch_flags(void) { return g_launch_flags.load(); }
@@ -1117,7 +1118,7 @@ int simsd_moe_align(const int64_t* topk_ids, int S, int E, int32_t* counts, int3
 namespace {
 struct MoePlan {
   bool tc;
-  int bmax, grid;
+  int bmax, bmax_big, grid;
   size_t off_counts, off_offsets, off_sorted, off_s2r, off_xs, off_h, off_ys, off_tables, off_part, total;
   long long max_chunks;
 };
@@ -1135,6 +1136,13 @@ MoePlan plan_moe(int T, int k, int E, int H, int I, int dtype, int sms, bool tc)
   p.bmax = want <= 16 ? 16 : want <= 32 ? 32 : want <= 64 ? 64 : want <= 128 ? 128 : 256;
   // SIMSD_MOE_BMAX (16, 32, 64, 128, 256) overrides the choice (measurement knob)
   p.bmax = env_choice("SIMSD_MOE_BMAX", {16, 32, 64, 128, 256}, p.bmax);
+  // Skewed routing (SIMSD_LAUNCH_MOE_SIZE_CLASSES): groups with more rows than
+  // bmax go to a second launch of each grouped GEMM with 256-row tiles, the
+  // device choosing the class of every group from its count.  Off by default:
+  // with near-uniform routing the second class holds little work and its
+  // launches and 256-row split-K partials cost more than the chunks they save.
+  const bool two_class = (g_launch_flags.load(std::memory_order_relaxed) & SIMSD_LAUNCH_MOE_SIZE_CLASSES) != 0;
+  p.bmax_big = (tc && two_class && p.bmax < 256 && T > p.bmax) ? 256 : 0;
   p.grid = std::max(1, std::min(sms > 0 ? sms : 148, TC_MAX_GRID));
   size_t o = WS_COUNTER_BYTES;
   p.off_counts = o; o = align256(o + (size_t)E * 4);
@@ -1146,7 +1154,7 @@ MoePlan plan_moe(int T, int k, int E, int H, int I, int dtype, int sms, bool tc)
   p.off_ys = o; o = align256(o + (size_t)S * H * es);
   p.off_tables = o; o = align256(o + (size_t)TC_TABLE_INTS * 4);
   p.off_part = o;
-  if (tc) o = align256(o + (size_t)2 * p.grid * p.bmax * 128 * sizeof(float));
+  if (tc) o = align256(o + (size_t)2 * p.grid * std::max(p.bmax, p.bmax_big) * 128 * sizeof(float));
   p.total = o;
   p.max_chunks = std::min<long long>(E, S) + S / p.bmax + 1;
   return p;
@@ -1235,71 +1243,69 @@ static int moe_dispatch_impl(const void* x, int64_t ldx, const int64_t* topk_ids
 
   if (plan.tc) {
     if (ensure_encode() != SIMSD_OK) return SIMSD_ERR_DEVICE;
-    // gate/up: out[row, i] = silu(xs[row] . w_gate[e, i]) * (xs[row] . w_up[e, i])
-    TcGemmArgs a;
-    memset(&a, 0, sizeof(a));
-    {
-      const uint64_t gd[3] = {(uint64_t)H, (uint64_t)I, (uint64_t)E};
-      const uint64_t gs[2] = {(uint64_t)ldg_i * es, (uint64_t)ldg_e * es};
-      const uint64_t bd[2] = {(uint64_t)H, (uint64_t)S};
-      const uint64_t bs[1] = {(uint64_t)H * es};
-      rc = encode_map(&a.tmA0, w_gate, dtype, 3, gd, gs, 64);
-      if (rc == SIMSD_OK) rc = encode_map(&a.tmA1, w_up, dtype, 3, gd, gs, 64);
-      if (rc == SIMSD_OK) rc = encode_map(&a.tmB, xs, dtype, 2, bd, bs, (uint32_t)plan.bmax);
-      if (rc != SIMSD_OK) return rc;
-    }
-    a.out = hbuf;
-    a.ld_out = I;
-    a.partials = reinterpret_cast<float*>(ws + plan.off_part);
-    a.tables = reinterpret_cast<int*>(ws + plan.off_tables);
-    a.counters = use_counters_grouped() && plan.max_chunks * cdiv(I, 64) <= WS_MAX_COUNTERS ? reinterpret_cast<int*>(ws) : nullptr;
-    a.err = err;
-    a.group_counts = counts;
-    a.num_groups = E;
-    a.kb = (int)cdiv(H, 64);
-    a.rows_out = I;
-    a.row_tiles = (int)cdiv(I, 64);
-    a.silu = 1;
-    a.three_d = 1;
-    a.is_bf16 = dtype == SIMSD_BF16 ? 1 : 0;
-    // a grouped GEMM with at least two tiles per CTA splits no tile (tc_whole_tiles);
-    // there are at least ceil(S / bmax) row chunks, so often that is known here
-    const long long min_chunks = std::max<long long>(1, cdiv(S, plan.bmax));
-    rc = launch_tc(plan.bmax, a, plan.grid, s, dev);
-    if (rc == SIMSD_OK && a.counters == nullptr &&
-        !tc_whole_tiles(true, (int)std::min<long long>(min_chunks * a.row_tiles, 1 << 30), plan.grid))
-      rc = launch_fixup(plan.bmax, fixup_args(a, plan.grid), s);
-    if (rc != SIMSD_OK) return rc;
-    // down: ys[row, h] = hbuf[row] . w_down[e, h]
-    TcGemmArgs d;
-    memset(&d, 0, sizeof(d));
-    {
-      const uint64_t dd[3] = {(uint64_t)I, (uint64_t)H, (uint64_t)E};
-      const uint64_t ds[2] = {(uint64_t)ldd_h * es, (uint64_t)ldd_e * es};
-      const uint64_t bd[2] = {(uint64_t)I, (uint64_t)S};
-      const uint64_t bs[1] = {(uint64_t)I * es};
-      rc = encode_map(&d.tmA0, w_down, dtype, 3, dd, ds, 128);
-      if (rc == SIMSD_OK) rc = encode_map(&d.tmB, hbuf, dtype, 2, bd, bs, (uint32_t)plan.bmax);
-      if (rc != SIMSD_OK) return rc;
-    }
-    d.out = ys;
-    d.ld_out = H;
-    d.partials = a.partials;
-    d.tables = a.tables;
-    d.counters = use_counters_grouped() && plan.max_chunks * cdiv(H, 128) <= WS_MAX_COUNTERS ? reinterpret_cast<int*>(ws) : nullptr;
-    d.err = err;
-    d.group_counts = counts;
-    d.num_groups = E;
-    d.kb = (int)cdiv(I, 64);
-    d.rows_out = H;
-    d.row_tiles = (int)cdiv(H, 128);
-    d.silu = 0;
-    d.three_d = 1;
-    d.is_bf16 = a.is_bf16;
-    rc = launch_tc(plan.bmax, d, plan.grid, s, dev);
-    if (rc == SIMSD_OK && d.counters == nullptr &&
-        !tc_whole_tiles(true, (int)std::min<long long>(min_chunks * d.row_tiles, 1 << 30), plan.grid))
-      rc = launch_fixup(plan.bmax, fixup_args(d, plan.grid), s);
+    // One grouped GEMM over the groups of class (lo, hi] rows with bm-row tiles:
+    // gate/up (out[row, i] = silu(xs[row] . w_gate[e, i]) * (xs[row] . w_up[e, i]))
+    // or down (ys[row, h] = hbuf[row] . w_down[e, h]).
+    auto grouped = [&](bool up, int bm, int lo, int hi) -> int {
+      TcGemmArgs a;
+      memset(&a, 0, sizeof(a));
+      int r;
+      if (up) {
+        const uint64_t gd[3] = {(uint64_t)H, (uint64_t)I, (uint64_t)E};
+        const uint64_t gs[2] = {(uint64_t)ldg_i * es, (uint64_t)ldg_e * es};
+        const uint64_t bd[2] = {(uint64_t)H, (uint64_t)S};
+        const uint64_t bs[1] = {(uint64_t)H * es};
+        r = encode_map(&a.tmA0, w_gate, dtype, 3, gd, gs, 64);
+        if (r == SIMSD_OK) r = encode_map(&a.tmA1, w_up, dtype, 3, gd, gs, 64);
+        if (r == SIMSD_OK) r = encode_map(&a.tmB, xs, dtype, 2, bd, bs, (uint32_t)bm);
+        a.out = hbuf;
+        a.ld_out = I;
+        a.kb = (int)cdiv(H, 64);
+        a.rows_out = I;
+        a.row_tiles = (int)cdiv(I, 64);
+        a.silu = 1;
+      } else {
+        const uint64_t dd[3] = {(uint64_t)I, (uint64_t)H, (uint64_t)E};
+        const uint64_t ds[2] = {(uint64_t)ldd_h * es, (uint64_t)ldd_e * es};
+        const uint64_t bd[2] = {(uint64_t)I, (uint64_t)S};
+        const uint64_t bs[1] = {(uint64_t)I * es};
+        r = encode_map(&a.tmA0, w_down, dtype, 3, dd, ds, 128);
+        if (r == SIMSD_OK) r = encode_map(&a.tmB, hbuf, dtype, 2, bd, bs, (uint32_t)bm);
+        a.out = ys;
+        a.ld_out = H;
+        a.kb = (int)cdiv(I, 64);
+        a.rows_out = H;
+        a.row_tiles = (int)cdiv(H, 128);
+        a.silu = 0;
+      }
+      if (r != SIMSD_OK) return r;
+      a.partials = reinterpret_cast<float*>(ws + plan.off_part);
+      a.tables = reinterpret_cast<int*>(ws + plan.off_tables);
+      const long long max_chunks = std::min<long long>(E, S) + S / bm + 1;
+      a.counters = use_counters_grouped() && max_chunks * a.row_tiles <= WS_MAX_COUNTERS ? reinterpret_cast<int*>(ws)
+                                                                                         : nullptr;
+      a.err = err;
+      a.group_counts = counts;
+      a.num_groups = E;
+      a.cls_lo = lo;
+      a.cls_hi = hi;
+      a.three_d = 1;
+      a.is_bf16 = dtype == SIMSD_BF16 ? 1 : 0;
+      // a grouped GEMM with at least two tiles per CTA splits no tile
+      // (tc_whole_tiles); with the class filter the chunk count is only known
+      // on the device, so the fixup kernel runs unless the in-kernel reduction does
+      const long long min_chunks = hi == 0 && lo == 0 ? std::max<long long>(1, cdiv(S, bm)) : 0;
+      r = launch_tc(bm, a, plan.grid, s, dev);
+      if (r == SIMSD_OK && a.counters == nullptr &&
+          !tc_whole_tiles(true, (int)std::min<long long>(min_chunks * a.row_tiles, 1 << 30), plan.grid))
+        r = launch_fixup(bm, fixup_args(a, plan.grid), s);
+      return r;
+    };
+    const int bs_hi = plan.bmax_big > 0 ? plan.bmax : 0;   // small tiles take groups of <= bmax rows
+    rc = grouped(true, plan.bmax, 0, bs_hi);
+    if (rc == SIMSD_OK && plan.bmax_big > 0) rc = grouped(true, plan.bmax_big, plan.bmax, 0);
+    if (rc == SIMSD_OK) rc = grouped(false, plan.bmax, 0, bs_hi);
+    if (rc == SIMSD_OK && plan.bmax_big > 0) rc = grouped(false, plan.bmax_big, plan.bmax, 0);
     if (rc != SIMSD_OK) return rc;
   } else {
     const long long max_chunks = std::min<long long>(E, S) + S / SIMT_ROWS + 1;

@@ -64,6 +64,10 @@ struct alignas(64) TcGemmArgs {
   const int* group_counts;   // grouped mode: rows per group; nullptr = single mode
   long long ld_out;
   int num_groups;
+  // grouped mode: only groups with cls_lo < rows <= cls_hi take tiles here
+  // (cls_hi 0: no upper bound); the others keep their rows but get no chunks,
+  // so two launches with different tile heights can split the groups by size
+  int cls_lo, cls_hi;
   int single_rows;           // single mode: rows of B (M)
   int kb;                    // number of 64-wide K blocks
   int rows_out;              // valid output columns (N, or I in SiLU-mul mode)
@@ -333,7 +337,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
       for (int base = 0; base < G; base += 32) {
         const int g = base + lane;
         int c = (g < G) ? row_prefix[g + 1] : 0;
-        int ch = (c + BMAX - 1) / BMAX;
+        int ch = (c > p.cls_lo && (p.cls_hi == 0 || c <= p.cls_hi)) ? (c + BMAX - 1) / BMAX : 0;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
           const int c2 = __shfl_up_sync(0xffffffffu, c, o);

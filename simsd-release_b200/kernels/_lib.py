@@ -33,6 +33,7 @@ PATH_AUTO, PATH_TC, PATH_SIMT = 0, 1, 2
 LAUNCH_PDL = 1
 LAUNCH_INKERNEL_REDUCE = 2
 LAUNCH_GROUPED_FIXUP = 4
+LAUNCH_MOE_SIZE_CLASSES = 8
 IPC_HANDLE_BYTES = 64
 SIGNAL_BYTES = 256
 
@@ -246,6 +247,22 @@ def set_inkernel_reduce(enable: bool) -> bool:
     """Sum split-K tiles inside the GEMM (last contributor) instead of in a separate
     reduction kernel; the bits are the same either way.  Returns the previous setting."""
     return _set_flag(LAUNCH_INKERNEL_REDUCE, enable)
+
+
+class moe_size_classes:
+    """Context manager: MoE dispatches issued (or captured) in its body split
+    each grouped GEMM by expert size (SIMSD_LAUNCH_MOE_SIZE_CLASSES)."""
+
+    def __init__(self, enable: bool = True):
+        self.enable = enable
+
+    def __enter__(self):
+        self.prev = _set_flag(LAUNCH_MOE_SIZE_CLASSES, self.enable)
+        return self
+
+    def __exit__(self, *exc):
+        _set_flag(LAUNCH_MOE_SIZE_CLASSES, self.prev)
+        return False
 
 
 class weights_static:

@@ -126,7 +126,8 @@ def moe_route(x: torch.Tensor, w_router: torch.Tensor, bias: torch.Tensor | None
     return (ids, wts, logits) if return_logits else (ids, wts)
 
 
-def moe_dispatch(x, topk_ids, topk_weight, w_gate, w_up, w_down, add=None, shared_last: bool = False):
+def moe_dispatch(x, topk_ids, topk_weight, w_gate, w_up, w_down, add=None, shared_last: bool = False,
+                 size_classes: bool = False):
     """Drop-in for ``LLaDA2MoeSparseMoeBlock.moe_infer`` on stacked weights.
 
     x (T, H); topk_ids (T, k) int64; topk_weight (T, k) fp32;
@@ -136,6 +137,9 @@ def moe_dispatch(x, topk_ids, topk_weight, w_gate, w_up, w_down, add=None, share
     with the routed ones (moe_route(..., extra_expert=E)); its output is added
     unweighted after the routed sum is rounded, as `add` would be, but it runs
     inside the same grouped GEMMs.
+    `size_classes`: for skewed routing (a few experts take most tokens), each
+    grouped GEMM runs twice, the experts that outgrow the planned tile height
+    with 256-row tiles (SIMSD_LAUNCH_MOE_SIZE_CLASSES).
     """
     if x.ndim != 2 or topk_ids.ndim != 2 or topk_weight.shape != topk_ids.shape:
         raise ValueError("x (T,H), topk_ids (T,k) and topk_weight (T,k) expected")
@@ -174,6 +178,9 @@ def moe_dispatch(x, topk_ids, topk_weight, w_gate, w_up, w_down, add=None, share
         if add.stride(1) != 1:
             add = add.contiguous()
     L = _lib.lib()
+    if size_classes:
+        with _lib.moe_size_classes(True):
+            return moe_dispatch(x, topk_ids, topk_weight, w_gate, w_up, w_down, add, shared_last)
     if shared_last:
         if add is not None or k < 2:
             raise ValueError("shared_last takes no `add` and needs at least one routed column")
@@ -210,7 +217,7 @@ def stack_shared_expert(w_gate, w_up, w_down, shared: tuple):
 
 def moe_layer(x, w_router, router_bias, k, w_gate, w_up, w_down,
               shared: tuple | None = None, renorm: bool = True, scale: float = 1.0,
-              shared_stacked: bool = False):
+              shared_stacked: bool = False, size_classes: bool = False):
     """Router + routed experts + optional shared expert (w_gate_s, w_up_s, w_down_s).
 
     The shared expert is the dense SwiGLU `down(silu(gate(x)) * up(x))`, run as
@@ -229,7 +236,7 @@ def moe_layer(x, w_router, router_bias, k, w_gate, w_up, w_down,
         if w_gate.shape[0] != E + 1:
             raise ValueError(f"shared_stacked: {E} routed experts + 1 shared expected, got {w_gate.shape[0]}")
         ids, wts = moe_route(x, w_router, router_bias, k=k, renorm=renorm, scale=scale, extra_expert=E)
-        return moe_dispatch(x, ids, wts, w_gate, w_up, w_down, shared_last=True)
+        return moe_dispatch(x, ids, wts, w_gate, w_up, w_down, shared_last=True, size_classes=size_classes)
     add = None
     if shared is not None:
         sg, su, sd = shared
@@ -242,7 +249,7 @@ def moe_layer(x, w_router, router_bias, k, w_gate, w_up, w_down,
     if add is not None:
         main.wait_stream(side)
         add.record_stream(main)
-    return moe_dispatch(x, ids, wts, w_gate, w_up, w_down, add=add)
+    return moe_dispatch(x, ids, wts, w_gate, w_up, w_down, add=add, size_classes=size_classes)
 
 
 def stack_expert_weights(experts, free_originals: bool = True):

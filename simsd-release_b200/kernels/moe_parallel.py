@@ -149,12 +149,13 @@ class CudaOps:
 def ep_moe_layer(x: torch.Tensor, w_router: torch.Tensor, router_bias: torch.Tensor | None, k: int,
                  w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor, E: int, group=None,
                  capacity: int | None = None, shared: tuple | None = None, renorm: bool = True,
-                 scale: float = 1.0, ops=CudaOps) -> torch.Tensor:
+                 scale: float = 1.0, ops=CudaOps, size_classes: bool = False) -> torch.Tensor:
     """One expert-parallel MoE layer for this rank's tokens x [T_r, H].
 
     w_gate, w_up [E/g, I, H] and w_down [E/g, H, I] are this rank's experts;
     w_router [E, H] and router_bias [E] are replicated.  `capacity` (rows per
     peer bucket) must be the same on every rank; default T_r * k.
+    `size_classes`: as moe_dispatch's, for skewed routing.
     """
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     lo, hi = expert_range(E, rank, world)
@@ -169,7 +170,12 @@ def ep_moe_layer(x: torch.Tensor, w_router: torch.Tensor, router_bias: torch.Ten
     dist.all_to_all_single(recv, send, group=group)
     recv_e = torch.empty_like(plan["send_expert"])
     dist.all_to_all_single(recv_e, plan["send_expert"], group=group)
-    y = ops.experts(recv, recv_e, w_gate, w_up, w_down)
+    if size_classes:
+        from . import _lib
+        with _lib.moe_size_classes(True):
+            y = ops.experts(recv, recv_e, w_gate, w_up, w_down)
+    else:
+        y = ops.experts(recv, recv_e, w_gate, w_up, w_down)
     back = torch.empty_like(y)
     dist.all_to_all_single(back, y, group=group)
     add = ops.shared(x, *shared) if shared is not None else None

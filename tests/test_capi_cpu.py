@@ -73,3 +73,19 @@ def test_argument_validation_happens_before_device_work(L):
                                 p, 1 << 20, None) == _lib.SIMSD_ERR_DTYPE
     assert L.simsd_moe_dispatch(p, 1, p, p, p, p, 1, 1, p, 1, 1, p, 1, None, 0, 1, 1, 4096, 8, 8, 0,
                                 p, 1 << 20, None) == _lib.SIMSD_ERR_SHAPE
+
+
+def test_launch_flags_round_trip():
+    """Every documented launch flag is kept by simsd_set_launch_flags (no GPU needed)."""
+    from kernels import _lib
+    L = _lib.lib()
+    prev = L.simsd_get_launch_flags()
+    try:
+        for bit in (_lib.LAUNCH_PDL, _lib.LAUNCH_INKERNEL_REDUCE, _lib.LAUNCH_GROUPED_FIXUP,
+                    _lib.LAUNCH_MOE_SIZE_CLASSES):
+            L.simsd_set_launch_flags(bit)
+            assert L.simsd_get_launch_flags() == bit
+        with _lib.moe_size_classes(True):
+            assert L.simsd_get_launch_flags() & _lib.LAUNCH_MOE_SIZE_CLASSES
+    finally:
+        L.simsd_set_launch_flags(prev)

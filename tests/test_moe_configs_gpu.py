@@ -137,11 +137,14 @@ def test_config2_layer_with_stacked_shared_expert(T):
     torch.cuda.empty_cache()
 
 
+@pytest.mark.parametrize("size_classes", [False, True], ids=["one-class", "size-classes"])
 @pytest.mark.parametrize("T", [64, 256, 1024, 4096])
-def test_config4_layer_single_gpu(T):
+def test_config4_layer_single_gpu(T, size_classes):
+    """As the bench runs it: the grouped GEMMs split by expert size (the skewed
+    routing's large experts on 256-row tiles), and without the split."""
     x, wr, bias, routed, shared = cfg4_inputs(T)
     with torch.inference_mode():
-        got = moe_layer(x, wr, bias, 8, *routed, shared=shared)
+        got = moe_layer(x, wr, bias, 8, *routed, shared=shared, size_classes=size_classes)
         torch.cuda.synchronize()
         check_layer(x, wr, bias, 8, routed, shared, got)
     del routed

@@ -265,13 +265,14 @@ def test_dispatch_golden_reference_outputs():
                                             (32, 4, 16, 256, 128, None), (8, 8, 64, 512, 192, 0.05),
                                             (1024, 2, 8, 512, 256, None),     # ~256 rows per expert: 256-row tiles
                                             (600, 4, 16, 256, 192, 0.3)])     # busy experts split in 128/256-row chunks
-def test_dispatch_vs_oracle(T, k, E, H, I, conc):
+@pytest.mark.parametrize("size_classes", [False, True], ids=["one-class", "size-classes"])
+def test_dispatch_vs_oracle(T, k, E, H, I, conc, size_classes):
     ids, w = routing(T, k, E, seed=T * k + E, conc=conc)
     g = torch.Generator(device=DEV).manual_seed(E + H)
     x = torch.randn(T, H, device=DEV, generator=g).to(torch.bfloat16)
     wg, wu, wd = experts(E, H, I, torch.bfloat16, seed=I)
     with torch.inference_mode():
-        out = moe_dispatch(x, ids, w, wg, wu, wd)
+        out = moe_dispatch(x, ids, w, wg, wu, wd, size_classes=size_classes)
     args = [to_np(t) for t in (x, ids, w, wg, wu, wd)]
     acc1, _ = O.moe_dispatch(*args, mode=1)          # same rounding points as the kernel
     _, ref0 = O.moe_dispatch(*args, mode=0)          # stock moe_infer rounding
