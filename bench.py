@@ -190,6 +190,53 @@ def run_step(ws, xs, world, dist, ag=None, on_result=None):
     return res
 
 
+def sweep_parity(ws, xs) -> dict:
+    """Every sweep linear against the reference's eager path on the same device
+    (cuBLAS `F.linear`; gate_up: `silu(F.linear(x, wg)) * F.linear(x, wu)` in
+    bf16), per projection over all M: the worst max-error / tolerance
+    (2^-7 max|ref| + 1e-3) and the fraction of output elements bit-identical
+    to the reference, tracked apart from the tolerance because a one-ulp
+    difference can still flip a greedy argmax.  The fraction is given against
+    default cuBLAS (torch allows it a reduced-precision split-K reduction for
+    bf16) and against cuBLAS with fp32 split-K reduction.  gate_up rounds once
+    (SiLU and the product on the fp32 accumulators) where the eager chain
+    rounds three times, so its fraction measures the chain's rounding too."""
+    from kernels.thin_linear_fused import thin_linear, thin_linear_silu_mul
+    mm = torch.backends.cuda.matmul
+
+    def ref_of(name, x, silu, full):
+        saved = mm.allow_bf16_reduced_precision_reduction
+        mm.allow_bf16_reduced_precision_reduction = not full
+        try:
+            if silu:
+                return F.silu(F.linear(x, ws[name][0])) * F.linear(x, ws[name][1])
+            return F.linear(x, ws[name])
+        finally:
+            mm.allow_bf16_reduced_precision_reduction = saved
+
+    acc: dict = {}
+    for M in MS:
+        for name, K, N, silu in SHAPES:
+            x = xs[M][K]
+            got = thin_linear_silu_mul(x, *ws[name]) if silu else thin_linear(x, ws[name])
+            ref, ref32 = ref_of(name, x, silu, False), ref_of(name, x, silu, True)
+            err = float((got.float() - ref.float()).abs().max())
+            t = 2 ** -7 * float(ref.abs().max()) + 1e-3
+            a = acc.setdefault(name, [0.0, 0, 0, 0])
+            a[0] = max(a[0], err / t)
+            a[1] += int((got == ref).sum())
+            a[2] += int((got == ref32).sum())
+            a[3] += ref.numel()
+    out = {n: {"max_err_over_tol": round(a[0], 4), "bitexact_pct": round(100 * a[1] / a[3], 3),
+               "bitexact_pct_fp32_reduction": round(100 * a[2] / a[3], 3)} for n, a in acc.items()}
+    plain = [acc[n] for n, _, _, s in SHAPES if not s]
+    n_plain = sum(a[3] for a in plain)
+    out["plain_linears_bitexact_pct"] = round(100 * sum(a[1] for a in plain) / n_plain, 3)
+    out["plain_linears_bitexact_pct_fp32_reduction"] = round(100 * sum(a[2] for a in plain) / n_plain, 3)
+    out["reference"] = "cuBLAS F.linear on the same GPU (gate_up: eager bf16 silu*mul of two F.linear)"
+    return out
+
+
 def per_launch_timing(pool, xs, reps: int = 6):
     """Device time of every thin-linear launch, back to back behind a sleep so the
     host never gates the GPU; returns {(name, M): mean_us} and the bytes-weighted
@@ -294,9 +341,10 @@ def gpu_arm(args):
         launches_per_step = len(MS) * len(SHAPES)
 
         # per-launch device time of the dominant kernel (tc_gemm) at N=1
-        per, agg_gbs, avg_us = (None, None, None)
+        per, agg_gbs, avg_us, parity = (None, None, None, None)
         if world == 1:
             per, agg_gbs, avg_us = per_launch_timing(pool, xs)
+            parity = sweep_parity(pool[0], xs)
 
         # end to end through the public API: pinned host inputs -> device -> host outputs
         hx = {M: {K: xs[M][K].cpu().pin_memory() for K in (4096, 12288)} for M in MS}
@@ -449,6 +497,8 @@ def gpu_arm(args):
                                           "next launch); per shape in per_launch"},
         }
         line["per_launch"] = per
+    if parity is not None:
+        line["parity"] = parity
     clk_summary = clk.summary()
     line["clocks"] = clk_summary
     if world == 1 and "verify" in args.workload:
