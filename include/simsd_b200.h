@@ -296,10 +296,10 @@ int simsd_moe_dispatch_shared_last(const void* x, int64_t ldx, const int64_t* to
 /* ---- column-parallel thin linear with the all-gather fused in (no counterpart in
  * the reference).  Each rank of a node holds rows [rank*N, (rank+1)*N) of the
  * full weight and writes its output columns straight into every rank's y
- * (NVLink peer stores); the launch's last CTA then adds 1 to the arrival
- * counter of every rank's signal block.  Nothing waits inside the launch: a
- * reader of y first calls simsd_allgather_wait on the same stream.  All ranks
- * must make the same sequence of these calls with the same shapes. */
+ * (NVLink peer stores).  The launch carries no signal and nothing waits inside
+ * it: before reading y, every rank calls simsd_allgather_wait on the same
+ * stream (one sync point may cover several launches).  All ranks must make the
+ * same sequence of these calls with the same shapes. */
 
 #define SIMSD_IPC_HANDLE_BYTES 64
 #define SIMSD_SIGNAL_BYTES 256   /* one rank's signal block (zeroed by simsd_ipc_alloc) */
@@ -317,7 +317,7 @@ int simsd_ipc_close(void* dev_ptr);
  * y_r[m, col_offset + n] = (x w^T)[m, n] (+ bias[n]) for every rank r, or the
  * SiLU*mul epilogue with w_up; n < N (this rank's output columns).
  *   peer_y [world]: every rank's y (same layout, row stride ldy), this rank's
- *   own at peer_y[rank]; peer_signal [world]: every rank's signal block.
+ *   own at peer_y[rank].
  * plan_n > 0: split each output tile's K range exactly as simsd_thin_linear
  * would for an [M, plan_n] output (plan_n = the unsharded width), so every
  * element is summed in the single-GPU order and the gathered y is bit-identical
@@ -331,21 +331,25 @@ int simsd_thin_linear_allgather(const void* x, int64_t ldx_m, int64_t ldx_k, con
                                 int64_t ldw_n, int64_t ldw_k, const void* w_up, const void* bias,
                                 void* const* peer_y, int64_t ldy, int col_offset, int M, int N,
                                 int K, int dtype, int epilogue, int rank, int world,
-                                void* const* peer_signal, int plan_n, void* workspace,
-                                size_t workspace_bytes, void* stream);
+                                int plan_n, void* workspace, size_t workspace_bytes,
+                                void* stream);
 
 /*
- * Reader side of simsd_thin_linear_allgather (no counterpart in the reference):
- * one single-thread kernel on `stream` that waits until every rank has stored
- * its columns of every fused launch issued so far with this signal block (its
- * arrival counter reaches world x this rank's launch count; counters are
- * cumulative, compared modulo 2^32).  Kernels after it on `stream` read the
- * gathered outputs.  The wait is bounded (2 s): a rank that never makes its
- * launches sets SIMSD_DEV_ERR_TIMEOUT in the workspace error word instead of
- * hanging.  own_signal: this rank's signal block (peer_signal[rank]).
+ * Sync point of simsd_thin_linear_allgather (no counterpart in the reference):
+ * one single-thread kernel on `stream` that, once every earlier kernel on the
+ * stream has completed (so this rank's peer stores are performed), adds 1 with
+ * release to the arrival counter of every rank's signal block and then waits
+ * until its own counter reaches world x this rank's count of sync points: every
+ * rank has stored its columns of every fused launch it issued before the same
+ * sync point.  Kernels after it on `stream` read the gathered outputs.  Every
+ * rank calls it at the same points of the call sequence.  Counters are
+ * cumulative, compared modulo 2^32.  The wait is bounded (2 s): a rank that
+ * never arrives sets SIMSD_DEV_ERR_TIMEOUT in the workspace error word instead
+ * of hanging.  peer_signal [world]: every rank's signal block (this rank's own
+ * at peer_signal[rank]), each SIMSD_SIGNAL_BYTES zeroed bytes.
  */
-int simsd_allgather_wait(void* own_signal, int world, void* workspace, size_t workspace_bytes,
-                         void* stream);
+int simsd_allgather_wait(void* const* peer_signal, int rank, int world, void* workspace,
+                         size_t workspace_bytes, void* stream);
 
 /*
  * Greedy verify head: idx[m] = argmax_n round(x[m] . w[n] (+ bias[n])), the

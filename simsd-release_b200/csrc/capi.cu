@@ -560,7 +560,7 @@ struct CatSpec {
 
 int thin_cluster(const void* x, long long ldx_m, const void* w, long long ldw_n, const void* w_up, const void* bias,
                  void* y, long long ldy, int M, int N, int K, int dtype, bool silu, int* err, void* const* peer_y,
-                 int col_offset, int world, int rank, void* const* peer_sig, cudaStream_t s, int dev,
+                 int col_offset, int world, int rank, cudaStream_t s, int dev,
                  unsigned long long* amax_keys = nullptr, long long* amax_idx = nullptr, int* amax_count = nullptr,
                  const CatSpec* cat = nullptr, int plan_n = 0) {
   const bool f32 = dtype == SIMSD_F32;   // fp32 operands: 32-element K blocks, tf32 split on chip
@@ -617,10 +617,7 @@ int thin_cluster(const void* x, long long ldx_m, const void* w, long long ldw_n,
   a.world = world;
   a.rank = rank;
   a.col_offset = col_offset;
-  for (int r = 0; r < world && world > 1; ++r) {
-    a.peer_out[r] = peer_y[r];
-    a.peer_sig[r] = static_cast<int*>(peer_sig[r]);
-  }
+  for (int r = 0; r < world && world > 1; ++r) a.peer_out[r] = peer_y[r];
   return launch_cluster(bmax, a, cp.S, cp.C, s, dev, f32);
 }
 
@@ -778,7 +775,7 @@ int simsd_thin_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w
     // fp32, M <= 64: the same cluster kernel on tf32 hi/lo parts (three
     // products per K step, fp32 accumulate)
     const int rc = thin_cluster(x, ldx_m, w, ldw_n, w_up, bias, y, ldy_m, M, N, K, dtype, silu, err, nullptr, 0, 1,
-                                0, nullptr, s, dev);
+                                0, s, dev);
     if (rc != SIMSD_ERR_UNSUPPORTED) return rc;
   }
   const bool tc_ok = thin_tc_possible(x, ldx_m, ldx_k, w, ldw_n, ldw_k, w_up, M, N, K, dtype) != 0;
@@ -795,7 +792,7 @@ int simsd_thin_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w
   if (use_tc && M <= 64 && split == 0 && cluster_enabled()) {
     // M <= 64: split-K tiles reduced inside thread-block clusters
     const int rc = thin_cluster(x, ldx_m, w, ldw_n, w_up, bias, y, ldy_m, M, N, K, dtype, silu, err, nullptr, 0, 1,
-                                0, nullptr, s, dev);
+                                0, s, dev);
     if (rc != SIMSD_ERR_UNSUPPORTED) return rc;
   }
 
@@ -1459,17 +1456,16 @@ int simsd_ipc_close(void* dev_ptr) {
 int simsd_thin_linear_allgather(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w, int64_t ldw_n,
                                 int64_t ldw_k, const void* w_up, const void* bias, void* const* peer_y, int64_t ldy,
                                 int col_offset, int M, int N, int K, int dtype, int epilogue, int rank, int world,
-                                void* const* peer_signal, int plan_n, void* workspace, size_t workspace_bytes,
-                                void* stream) {
+                                int plan_n, void* workspace, size_t workspace_bytes, void* stream) {
   if (M < 1 || N < 1 || K < 1 || col_offset < 0 || plan_n < 0) return SIMSD_ERR_SHAPE;
   if (world < 2 || world > TC_AG_MAX_WORLD || rank < 0 || rank >= world) return SIMSD_ERR_UNSUPPORTED;
   if (dtype != SIMSD_BF16 && dtype != SIMSD_F16) return SIMSD_ERR_UNSUPPORTED;
   if (epilogue != SIMSD_EPI_NONE && epilogue != SIMSD_EPI_SILU_MUL) return SIMSD_ERR_UNSUPPORTED;
   const bool silu = epilogue == SIMSD_EPI_SILU_MUL;
   if (silu && (w_up == nullptr || bias != nullptr)) return SIMSD_ERR_UNSUPPORTED;
-  if (x == nullptr || w == nullptr || peer_y == nullptr || peer_signal == nullptr) return SIMSD_ERR_SHAPE;
+  if (x == nullptr || w == nullptr || peer_y == nullptr) return SIMSD_ERR_SHAPE;
   for (int r = 0; r < world; ++r)
-    if (peer_y[r] == nullptr || peer_signal[r] == nullptr) return SIMSD_ERR_SHAPE;
+    if (peer_y[r] == nullptr) return SIMSD_ERR_SHAPE;
   if (ldy < (long long)col_offset + N) return SIMSD_ERR_SHAPE;
   if (workspace == nullptr || workspace_bytes < (size_t)WS_COUNTER_BYTES) return SIMSD_ERR_WORKSPACE;
   if (M > 64 || K < 64 || !cluster_enabled() ||
@@ -1479,17 +1475,25 @@ int simsd_thin_linear_allgather(const void* x, int64_t ldx_m, int64_t ldx_k, con
   if (dev < 0) return SIMSD_ERR_DEVICE;
   int* err = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + WS_ERR_OFFSET);
   return thin_cluster(x, ldx_m, w, ldw_n, w_up, bias, peer_y[rank], ldy, M, N, K, dtype, silu, err, peer_y,
-                      col_offset, world, rank, peer_signal, (cudaStream_t)stream, dev, nullptr, nullptr, nullptr,
-                      nullptr, plan_n);
+                      col_offset, world, rank, (cudaStream_t)stream, dev, nullptr, nullptr, nullptr, nullptr, plan_n);
 }
 
-int simsd_allgather_wait(void* own_signal, int world, void* workspace, size_t workspace_bytes, void* stream) {
-  if (own_signal == nullptr || world < 2 || world > TC_AG_MAX_WORLD) return SIMSD_ERR_SHAPE;
+int simsd_allgather_wait(void* const* peer_signal, int rank, int world, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  if (peer_signal == nullptr || world < 2 || world > TC_AG_MAX_WORLD || rank < 0 || rank >= world)
+    return SIMSD_ERR_SHAPE;
   if (workspace == nullptr || workspace_bytes < (size_t)WS_COUNTER_BYTES) return SIMSD_ERR_WORKSPACE;
   if (current_device() < 0) return SIMSD_ERR_DEVICE;
-  int* err = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + WS_ERR_OFFSET);
-  return launch(ag_wait_kernel, dim3(1), dim3(32), 0, (cudaStream_t)stream, static_cast<int*>(own_signal), world,
-                err);
+  AgSyncArgs a;
+  memset(&a, 0, sizeof(a));
+  for (int r = 0; r < world; ++r) {
+    if (peer_signal[r] == nullptr) return SIMSD_ERR_SHAPE;
+    a.sig[r] = static_cast<int*>(peer_signal[r]);
+  }
+  a.world = world;
+  a.rank = rank;
+  a.err = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + WS_ERR_OFFSET);
+  return launch(ag_sync_kernel, dim3(1), dim3(32), 0, (cudaStream_t)stream, a);
 }
 
 int simsd_thin_linear_argmax(const void* x, int64_t ldx_m, int64_t ldx_k, const void* w, int64_t ldw_n,
@@ -1509,7 +1513,7 @@ int simsd_thin_linear_argmax(const void* x, int64_t ldx_m, int64_t ldx_k, const 
   auto* keys = reinterpret_cast<unsigned long long*>(ws + WS_ARGMAX_OFFSET);
   int* count = reinterpret_cast<int*>(ws + WS_ARGMAX_OFFSET + 64 * 8);
   return thin_cluster(x, ldx_m, w, ldw_n, nullptr, bias, nullptr, 0, M, N, K, dtype, false, err, nullptr, 0, 1, 0,
-                      nullptr, (cudaStream_t)stream, dev, keys, reinterpret_cast<long long*>(idx), count);
+                      (cudaStream_t)stream, dev, keys, reinterpret_cast<long long*>(idx), count);
 }
 
 int simsd_thin_linear_cat(const void* x, int64_t ldx_m, int64_t ldx_k, int parts, const void* const* w,
@@ -1538,7 +1542,7 @@ int simsd_thin_linear_cat(const void* x, int64_t ldx_m, int64_t ldx_k, int parts
   if (dev < 0) return SIMSD_ERR_DEVICE;
   int* err = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + WS_ERR_OFFSET);
   return thin_cluster(x, ldx_m, w[0], ldw_n[0], nullptr, nullptr, y, ldy, M, (int)N, K, dtype, false, err, nullptr,
-                      0, 1, 0, nullptr, (cudaStream_t)stream, dev, nullptr, nullptr, nullptr, &cs);
+                      0, 1, 0, (cudaStream_t)stream, dev, nullptr, nullptr, nullptr, &cs);
 }
 
 int simsd_rmsnorm(const void* x, int64_t ldx, const void* res, int64_t ldres, void* h_out, int64_t ldh,

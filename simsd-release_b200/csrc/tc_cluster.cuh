@@ -34,12 +34,11 @@ namespace simsd {
 
 constexpr int TC_CL_MAX = 8;          // largest cluster (portable)
 constexpr int TC_AG_MAX_WORLD = 8;    // ranks of a fused column-parallel all-gather
-// A rank's signal block (ints): arrivals of every rank's finished fused
-// all-gather launches (each rank adds 1 per launch, cumulative), this rank's
-// CTAs finished in the current launch, and this rank's launch count.
+// A rank's signal block (ints): arrivals of every rank at the fused
+// all-gather's sync points (each rank adds 1 per sync point, cumulative) and
+// this rank's count of sync points.
 constexpr int AG_SIG_ARRIVED = 0;
-constexpr int AG_SIG_CTAS = 1;
-constexpr int AG_SIG_LAUNCHES = 2;
+constexpr int AG_SIG_SYNCS = 2;
 constexpr int TC_CL_RED_ROWS = 144;   // >= S * rows one owner holds, for every S <= 8
 
 struct TcClusterArgs {
@@ -71,12 +70,10 @@ struct TcClusterArgs {
   unsigned long long* trace; // optional: 8 %globaltimer stamps per CTA (diagnostics)
   // column-parallel all-gather (world > 1, the AG instantiation): every output
   // element is stored at column col_offset + col of each rank's y (peer_out[r],
-  // NVLink mappings); the launch's last CTA then counts the launch on every
-  // rank's signal block (peer_sig, AG_SIG_*) and nobody waits here: a reader
-  // of y waits first (ag_wait_kernel)
+  // NVLink mappings).  The launch signals nothing and nobody waits here: after
+  // the launches whose outputs it needs, a reader runs ag_sync_kernel
   int world, rank, col_offset;
   void* peer_out[TC_AG_MAX_WORLD];
-  int* peer_sig[TC_AG_MAX_WORLD];
 };
 
 // F32: fp32 operands on the tensor cores.  A K block is then 32 elements (one
@@ -718,27 +715,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
       // aborting: give peers that may still be sending to this CTA time to land
       mbar_wait_cluster_drain(red_full_u32, done & 1, 100000000ull);
     }
-    if constexpr (AG) {
-      // Fused all-gather: count this launch as done on every rank once all of
-      // this rank's CTAs have stored.  Each CTA counts itself with a
-      // system-scope acquire-release add (after a CTA barrier, so it covers
-      // every epilogue thread's stores, local and remote); the last one resets
-      // the CTA count, advances this rank's launch count and adds 1, with
-      // release, to the arrival counter of every rank.  Nothing waits here: a
-      // reader of y first runs ag_wait_kernel, which waits until its arrival
-      // counter reaches world x its launch count.
-      griddep_wait();   // the previous launch's counter updates are visible (no-op without PDL)
-      named_bar_sync(1, 128);
-      if (row == 0) {
-        int* my_sig = p.peer_sig[p.rank];
-        if (atom_add_acq_rel_sys(my_sig + AG_SIG_CTAS, 1) == (int)gridDim.x - 1) {
-          my_sig[AG_SIG_CTAS] = 0;
-          volatile int* launches = my_sig + AG_SIG_LAUNCHES;
-          *launches = *launches + 1;
-          for (int r = 0; r < p.world; ++r) red_add_release_sys(p.peer_sig[r] + AG_SIG_ARRIVED, 1);
-        }
-      }
-    }
   }
 
   if (p.trace && tid == 0) {
@@ -754,20 +730,42 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
   if (p.trace && tid == 0) p.trace[blockIdx.x * 8 + 7] = globaltimer_ns();
 }
 
-// Reader side of the fused all-gather: one thread waits (bounded) until this
-// rank's arrival counter reaches world x its launch count, i.e. every rank has
-// stored its columns of every fused launch issued so far on this signal block
-// (counters are cumulative and compared modulo 2^32).  Launched on the stream
-// of those launches, before the kernels that read their outputs.
-__global__ void ag_wait_kernel(int* my_sig, int world, int* err) {
+// The fused all-gather's sync point, run by every rank on the stream of its
+// launches, before the kernels that read their outputs.  One thread:
+//  1. griddep_wait(): every earlier kernel on the stream has completed, so
+//     this rank's peer stores of every fused launch issued so far are
+//     performed (kernel completion flushes them, as it does stores to host
+//     memory);
+//  2. a system-scope fence, then adds 1 with release to the arrival counter
+//     of every rank (this rank's own included) and advances this rank's sync
+//     count;
+//  3. waits (bounded) until its own arrival counter reaches world x its sync
+//     count: every rank has passed step 2 of this sync point, so all their
+//     columns are in this rank's outputs.
+// Counters are cumulative and compared modulo 2^32.  The launches themselves
+// carry no signal, so a fused launch costs what a local one does, and ranks
+// meet once per sync point instead of once per launch.
+struct AgSyncArgs {
+  int* sig[TC_AG_MAX_WORLD];   // every rank's signal block (NVLink mappings; own at [rank])
+  int world, rank;
+  int* err;
+};
+
+__global__ void ag_sync_kernel(const __grid_constant__ AgSyncArgs a) {
   if (threadIdx.x != 0) return;
   griddep_launch_dependents();   // the reader may launch and set up; its own wait covers this kernel
   griddep_wait();
-  const unsigned target = (unsigned)*reinterpret_cast<volatile int*>(my_sig + AG_SIG_LAUNCHES) * (unsigned)world;
+  __threadfence_system();
+  int* mine = a.sig[a.rank];
+  volatile int* syncs = mine + AG_SIG_SYNCS;
+  const unsigned count = (unsigned)*syncs + 1u;
+  *syncs = (int)count;
+  for (int r = 0; r < a.world; ++r) red_add_release_sys(a.sig[r] + AG_SIG_ARRIVED, 1);
+  const unsigned target = count * (unsigned)a.world;
   const uint64_t t0 = globaltimer_ns();
-  while ((int)((unsigned)ld_acquire_sys(my_sig + AG_SIG_ARRIVED) - target) < 0) {
+  while ((int)((unsigned)ld_acquire_sys(mine + AG_SIG_ARRIVED) - target) < 0) {
     if (globaltimer_ns() - t0 > SIMSD_WAIT_LIMIT_NS) {
-      atomicOr(err, SIMSD_DEV_ERR_TIMEOUT);
+      atomicOr(a.err, SIMSD_DEV_ERR_TIMEOUT);
       break;
     }
   }

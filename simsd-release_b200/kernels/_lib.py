@@ -79,9 +79,9 @@ SIGNATURES: dict[str, tuple] = {
     "simsd_qk_norm_rope": (_I, [_P, _L, _I, _I, _I, _I, _P, _P, _P, _P, _F, _P, _P, _P, _L, _I, _I, _P]),
     "simsd_verify_attention_workspace_size": (_S, [_I, _I, _I, _I]),
     "simsd_verify_attention": (_I, [_P, _P, _P, _L, _I, _I, _I, _I, _P, _L, _F, _P, _I, _P, _S, _P]),
-    "simsd_allgather_wait": (_I, [_P, _I, _P, _S, _P]),
+    "simsd_allgather_wait": (_I, [_P, _I, _I, _P, _S, _P]),
     "simsd_thin_linear_allgather": (_I, [_P, _L, _L, _P, _L, _L, _P, _P, _P, _L, _I, _I, _I, _I, _I, _I, _I, _I,
-                                         _P, _I, _P, _S, _P]),
+                                         _I, _P, _S, _P]),
     "simsd_moe_ep_plan": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
     "simsd_moe_gather_rows": (_I, [_P, _L, _P, _I, _I, _I, _I, _P, _L, _P]),
     "simsd_moe_combine": (_I, [_P, _L, _P, _P, _P, _L, _P, _L, _I, _I, _I, _I, _P]),

@@ -157,10 +157,10 @@ class SymmetricBlock:
 class FusedAllGather:
     """Column-parallel thin linears whose all-gather is fused into the GEMM
     (simsd_thin_linear_allgather): each rank stores its columns straight into
-    every rank's output over NVLink and counts the launch on every rank's
-    signal block; a reader waits for the counts (simsd_allgather_wait) before
-    it reads.  No rank waits for the others at the end of a launch, so ranks
-    only meet where an output is actually read.
+    every rank's output over NVLink.  The launches carry no signal; at a sync
+    point (`wait`, simsd_allgather_wait) every rank counts itself on every
+    rank's signal block and waits for the others, so ranks only meet where an
+    output is actually read, and one sync point covers every launch before it.
 
     `linear(x, w_local, w_up_local=None, bias_local=None, wait=True)` returns
     the full [M, world * n] output; with `wait=False` the output is complete
@@ -211,7 +211,7 @@ class FusedAllGather:
             x.data_ptr(), x.stride(0), x.stride(1), w.data_ptr(), w.stride(0), w.stride(1),
             w_up.data_ptr() if w_up is not None else None, bias.data_ptr() if bias is not None else None,
             peers, N, self.rank * n, M, n, K, code, _lib.EPI_SILU_MUL if w_up is not None else _lib.EPI_NONE,
-            self.rank, self.world, self._sig_arr, plan_n, ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
+            self.rank, self.world, plan_n, ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
         if rc == _lib.SIMSD_ERR_UNSUPPORTED:
             local = thin_linear_silu_mul(x, w, w_up) if w_up is not None else thin_linear(x, w, bias)
             return gather_columns(local, self.group)
@@ -222,11 +222,13 @@ class FusedAllGather:
 
     def wait(self, dev: torch.device | None = None) -> None:
         """Make every fused output issued so far on the current stream complete
-        on this rank (one bounded device-side wait; no host synchronisation)."""
+        on this rank (one bounded device-side sync point; no host
+        synchronisation).  Collective: every rank calls it at the same point
+        of the call sequence."""
         dev = dev or torch.device("cuda", torch.cuda.current_device())
         ws = _lib.workspace(dev, _lib.lib().simsd_workspace_header_bytes())
-        _lib.check(_lib.lib().simsd_allgather_wait(self.sig.own, self.world, ws.data_ptr(), ws.numel(),
-                                                   _lib.stream_ptr(dev)), "allgather_wait")
+        _lib.check(_lib.lib().simsd_allgather_wait(self._sig_arr, self.rank, self.world, ws.data_ptr(),
+                                                   ws.numel(), _lib.stream_ptr(dev)), "allgather_wait")
 
     def close(self) -> None:
         for blk in self.outs.values():

@@ -59,7 +59,7 @@ def case_ep(dev):
 
 
 def case_fused(dev):
-    """All-gather fused into the GEMM (NVLink peer stores + device counters):
+    """All-gather fused into the GEMM (NVLink peer stores + a sync point):
     equal to the single-GPU thin linear within tolerance, stable over repeated
     calls (both output buffers, many counter slots) and inside a CUDA graph."""
     from kernels.parallel import FusedAllGather, column_shard
@@ -67,30 +67,38 @@ def case_fused(dev):
     rank, world = dist.get_rank(), dist.get_world_size()
     g = torch.Generator(device=dev).manual_seed(2)
     bf = torch.bfloat16
-    x = torch.randn(16, 4096, generator=g, device=dev).to(bf)
+    # NX different inputs in turn (NX odd): an output buffer is reused every
+    # second call, so a read that saw a peer's columns of an earlier call
+    # instead of this one's would not match this call's reference
+    NX = 5
+    xs = [torch.randn(16, 4096, generator=g, device=dev).to(bf) for _ in range(NX)]
     w = (torch.randn(4096, 4096, generator=g, device=dev) * 0.02).to(bf)
     wg, wu = [(torch.randn(2048, 4096, generator=g, device=dev) * 0.02).to(bf) for _ in range(2)]
-    x64 = torch.randn(64, 12288, generator=g, device=dev).to(bf)
+    x64s = [torch.randn(64, 12288, generator=g, device=dev).to(bf) for _ in range(NX)]
     wd = (torch.randn(4096, 12288, generator=g, device=dev) * 0.02).to(bf)
+    x = xs[0]
     ag = FusedAllGather()
     try:
         with torch.inference_mode():
-            ref = thin_linear(x, w)
-            ref_h = thin_linear_silu_mul(x, wg, wu)
-            ref_d = thin_linear(x64, wd)
+            refs = [thin_linear(v, w) for v in xs]
+            refs_h = [thin_linear_silu_mul(v, wg, wu) for v in xs]
+            refs_d = [thin_linear(v, wd) for v in x64s]
+            ref_h = refs_h[0]
             wl, wgl, wul, wdl = (column_shard(t, rank, world) for t in (w, wg, wu, wd))
-            for _ in range(40):          # many launches on the cumulative counters
-                y = ag.linear(x, wl)
-                h = ag.linear(x, wgl, wul)
-                d = ag.linear(x64, wdl)
-                assert _close(y, ref) and _close(h, ref_h) and _close(d, ref_d)
-            # deferred: three launches, one wait
-            for _ in range(5):
-                y = ag.linear(x, wl, wait=False)
-                h = ag.linear(x, wgl, wul, wait=False)
-                d = ag.linear(x64, wdl, wait=False)
+            for i in range(40):          # many launches on the cumulative counters
+                j = i % NX
+                y = ag.linear(xs[j], wl)
+                h = ag.linear(xs[j], wgl, wul)
+                d = ag.linear(x64s[j], wdl)
+                assert _close(y, refs[j]) and _close(h, refs_h[j]) and _close(d, refs_d[j]), i
+            # deferred: three launches, one sync point
+            for i in range(10):
+                j = i % NX
+                y = ag.linear(xs[j], wl, wait=False)
+                h = ag.linear(xs[j], wgl, wul, wait=False)
+                d = ag.linear(x64s[j], wdl, wait=False)
                 ag.wait()
-                assert _close(y, ref) and _close(h, ref_h) and _close(d, ref_d)
+                assert _close(y, refs[j]) and _close(h, refs_h[j]) and _close(d, refs_d[j]), i
             torch.cuda.synchronize()
             first = ag.linear(x, wl).clone()
             assert torch.equal(first, ag.linear(x, wl))          # bit-identical across calls
