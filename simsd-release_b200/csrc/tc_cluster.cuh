@@ -570,7 +570,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
       // -- 2. bytes this CTA receives for the tile: its rows from every peer
       if (row == 0) mbar_arrive_expect_tx(red_full_u32, (uint32_t)((S - 1) * ro.rows_of(q) * nb * 64));
       // -- 3. drain the accumulator: keep own rows, send the others to their owners
-      float mine[BMAX];
+      // this CTA's own rows go straight into its own slot of the receive
+      // buffer (slot q: no peer writes it, and every thread finished reading
+      // it for the previous tile before the barrier that ended that tile)
+      float4* const own_dst = reinterpret_cast<float4*>(red + ((q * slot_rows) + lr) * BMAX);
       const uint32_t dst_row = mapa_shared(red_u32 + (uint32_t)(((q * slot_rows) + lr) * BMAX * 4), (uint32_t)own);
       // 16-byte column group j of a received row sits at group swz(j): the XOR
       // spreads the rows that one quarter-warp touches over all 32 banks
@@ -583,7 +586,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
           tmem_wait_ld();
           if (own == q) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) mine[ch * 16 + j] = v[j];
+            for (int u = 0; u < 4; ++u)
+              own_dst[swz(lr, ch * 4 + u)] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
           } else {
 #pragma unroll
             for (int u = 0; u < 4; ++u)
@@ -599,21 +603,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
           (ep_active && !ep_silu && p.bias && ep_col < ep_rows_out) ? load_f(p.bias, ep_col, odt) : 0.0f;
       // -- 4. every peer's rows for this CTA have landed
       if (!named_bar_and(1, 128, mbar_wait_cluster(red_full_u32, i & 1, abort_flag, p.err))) break;
-      // -- 5. park this CTA's own rows in its (otherwise unused) slot, then all
-      // 128 threads share the owned outputs: each sums one (row, activation
-      // row) over the S slots in rank (= K) order and writes it to y
-      if (own == q) {
-        float4* dst = reinterpret_cast<float4*>(red + ((q * slot_rows) + lr) * BMAX);
-#pragma unroll
-        for (int ch = 0; ch < BMAX / 16; ++ch) {
-          if (ch >= nb) break;
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            dst[swz(lr, ch * 4 + u)] = make_float4(mine[ch * 16 + 4 * u], mine[ch * 16 + 4 * u + 1],
-                                                   mine[ch * 16 + 4 * u + 2], mine[ch * 16 + 4 * u + 3]);
-        }
-      }
-      named_bar_sync(1, 128);
+      // -- 5. all 128 threads share the owned outputs: each sums one (row,
+      // activation row) over the S slots in rank (= K) order and writes it to
+      // y (the barrier of step 4 ordered every thread's own-slot writes)
       {
         // Each thread sums its unit's outputs for up to EP_JMAX groups over the
         // S slots in rank (= K) order.  Group indices are clamped so every slot
