@@ -163,7 +163,9 @@ def run_step(ws, xs, world, dist, ag=None, on_result=None):
     """One sweep step.  world > 1: each linear is column-parallel, its output
     all-gathered by `ag` (FusedAllGather: fused into the GEMM over NVLink) or,
     without it, by an NCCL all-gather after the local GEMM.  `on_result(j, y)`
-    is called right after the j-th linear is launched."""
+    is called once the j-th linear's output is complete on the stream: right
+    after its launch, or with the fused gather after the sync point that
+    covers it."""
     from kernels.parallel import gather_columns
     from kernels.thin_linear_fused import thin_linear, thin_linear_silu_mul
     res = []
@@ -172,8 +174,8 @@ def run_step(ws, xs, world, dist, ag=None, on_result=None):
         for name, K, N, silu in SHAPES:
             x = xs[M][K]
             if fused:
-                # the 20 linears of a step are independent: their gathers
-                # complete together at the one wait below
+                # independent linears: their gathers complete together at a
+                # later sync point
                 y = ag.linear(x, *ws[name], wait=False) if silu else ag.linear(x, ws[name], wait=False)
             else:
                 y = thin_linear_silu_mul(x, *ws[name]) if silu else thin_linear(x, ws[name])
@@ -182,11 +184,15 @@ def run_step(ws, xs, world, dist, ag=None, on_result=None):
                 if on_result is not None:
                     on_result(len(res), y)
             res.append(y)
-    if fused:
-        ag.wait()
-        if on_result is not None:
-            for j, y in enumerate(res):
-                on_result(j, y)
+        if fused and on_result is not None:
+            # a consumer of the results (the end-to-end step's copies to the
+            # host): one sync point per activation height, so each height's
+            # results leave while the next height's linears run
+            ag.wait()
+            for j in range(len(res) - len(SHAPES), len(res)):
+                on_result(j, res[j])
+    if fused and on_result is None:
+        ag.wait()      # the step's one sync point
     return res
 
 
@@ -388,11 +394,6 @@ def gpu_arm(args):
                     houts[j].copy_(y, non_blocking=True)     # into pinned host buffers
 
             main.wait_event(ready[MS[0]])
-            if ag is not None:
-                # the fused gathers hand results over after the step's one wait,
-                # so every input is in place before the first launch
-                for M in MS[1:]:
-                    main.wait_event(ready[M])
             run_step(pool[p], sx, world, dist, ag, on_result=out)
             main.wait_stream(cs)
             main.wait_stream(hs)
