@@ -508,7 +508,8 @@ def gpu_arm(args):
         line["verify"] = verify_tp_bench(dev, rank, world, dist, args.steps)
     if "ep" in args.workload.split(","):
         line["ep_moe"] = ep_moe_bench(dev, rank, world, dist, args.steps,
-                                      None if (args.no_cpu_baseline or rank != 0) else min(5.0, args.cpu_seconds))
+                                      None if (args.no_cpu_baseline or rank != 0) else min(5.0, args.cpu_seconds),
+                                      nccl=args.nccl_ep)
     if world == 1 and "moe" in args.workload:
         line["moe"] = moe_bench(dev, args.steps, None if args.no_cpu_baseline else min(5.0, args.cpu_seconds))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -547,11 +548,13 @@ def tc_peaks() -> dict:
     return {"burst": 1.59e15, "sustained": 1.4e15, "src": "fallback"}
 
 
-def ep_moe_bench(dev, rank: int, world: int, dist, steps: int, cpu_seconds: float | None = None) -> dict:
+def ep_moe_bench(dev, rank: int, world: int, dist, steps: int, cpu_seconds: float | None = None,
+                 nccl: bool = False) -> dict:
     """Expert-parallel MoE layer: E/world experts per rank, T/world tokens per
-    rank, all-to-all exchange (NCCL); at world 1 the single-GPU layer."""
+    rank, buckets exchanged by NVLink peer stores (PeerExchange) or, with
+    `nccl`, NCCL all-to-alls; at world 1 the single-GPU layer."""
     from kernels.moe_dispatch_fused import moe_layer, moe_route
-    from kernels.moe_parallel import ep_moe_layer, expert_range
+    from kernels.moe_parallel import PeerExchange, ep_moe_layer, expert_range
     H, E, k, I = EP["H"], EP["E"], EP["k"], EP["I"]
     bf = torch.bfloat16
     g0 = torch.Generator(device=dev).manual_seed(77)            # replicated: router
@@ -580,10 +583,13 @@ def ep_moe_bench(dev, rank: int, world: int, dist, steps: int, cpu_seconds: floa
 
             # the N(0, 0.5) router bias concentrates the tokens on a few dozen
             # experts: the grouped GEMMs split the experts by size
+            xch = PeerExchange(Tr * k, H, bf) if world > 1 and not nccl else None
+
             def layer():
                 if world == 1:
                     return moe_layer(x, wr, bias, k, wg, wu, wd, shared=shared, size_classes=True)
-                return ep_moe_layer(x, wr, bias, k, wg, wu, wd, E, shared=shared, size_classes=True)
+                return ep_moe_layer(x, wr, bias, k, wg, wu, wd, E, shared=shared, size_classes=True,
+                                    exchange=xch)
 
             for _ in range(3):
                 layer()
@@ -610,6 +616,9 @@ def ep_moe_bench(dev, rank: int, world: int, dist, steps: int, cpu_seconds: floa
             ms = e0.elapsed_time(e1) / n
             del gr
             torch.cuda.synchronize()
+            if xch is not None:
+                dist.barrier()
+                xch.close()
             if world > 1:
                 t = torch.tensor([ms], device=dev)
                 dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -633,8 +642,9 @@ def ep_moe_bench(dev, rank: int, world: int, dist, steps: int, cpu_seconds: floa
     return {"cpu_baseline": res_cpu,
             "workload": "EP MoE layer, BASELINE configs[4]: H=4096, E=256 (E/N per GPU), top-8 sigmoid+bias(N(0,0.5)), "
                         "I=1536 SiLU*mul experts + 1 shared expert, bf16, T tokens split over N GPUs, "
-                        "all-to-all in fixed-capacity buckets, CUDA-graph replay; grouped GEMMs split by "
-                        "expert size (size_classes, for the skewed routing)",
+                        "fixed-capacity buckets exchanged by " + ("NCCL all-to-all" if nccl else
+                        "NVLink peer stores of the occupied entries") + ", CUDA-graph replay; grouped GEMMs split "
+                        "by expert size (size_classes, for the skewed routing)",
             "metric": "MoE layer HBM GB/s, all GPUs (algorithmic bytes: active experts + per-GPU shared/router + "
                       "activations); frac_roofline = max(bytes / HBM peak, flops / sustained bf16 peak) / time",
             "n_gpus": world, "per_T": out}
@@ -1240,6 +1250,8 @@ def main():
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--nccl-gather", action="store_true",
                     help="N > 1: all-gather each linear's columns with NCCL instead of the fused kernel")
+    ap.add_argument("--nccl-ep", action="store_true",
+                    help="N > 1: exchange the expert-parallel buckets with NCCL all-to-alls instead of peer stores")
     ap.add_argument("--workload", default="thin,moe,verify,ep",
                     help="comma list of legs: thin (headline), moe and verify (N=1), ep (expert-parallel MoE, any N)")
     args = ap.parse_args()

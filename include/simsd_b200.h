@@ -457,6 +457,33 @@ int simsd_moe_combine(const void* ys, int64_t ldys, const int32_t* slot_row,
                       const float* topk_weight, void* out, int64_t ld_out, const void* add,
                       int64_t ld_add, int T, int k, int H, int dtype, void* stream);
 
+/*
+ * The expert-parallel layer's exchanges as plain stores into every rank's
+ * blocks (NVLink peer mappings from simsd_ipc_open; no counterpart in the
+ * reference, which runs its MoE layer on one GPU).  Replaces the two
+ * all-to-alls of fixed-capacity buckets: only occupied bucket entries move a
+ * row, and nothing is staged in a send buffer.  Entry e = p * capacity + i of
+ * this rank's buckets (send_slot / send_expert from simsd_moe_ep_plan) lands in
+ * row rank * capacity + i of rank p's blocks.
+ *
+ * simsd_moe_ep_send: row x[send_slot[e] / k] into peer_rows[p] ([world *
+ *   capacity, H], row stride H) for send_slot[e] >= 0, and send_expert[e]
+ *   (the local expert id on p, -1 = empty) into peer_ids[p] for every e.
+ * simsd_moe_ep_return: row y[e] ([world * capacity, H], row stride ldy) back
+ *   into peer_back[p] at row rank * capacity + i for recv_expert[e] >= 0, where
+ *   recv_expert is this rank's id block as the sends filled it.
+ * Asynchronous: a sync point (simsd_allgather_wait on a signal block of the
+ * same ranks) after each call makes every rank's stores complete before its
+ * blocks are read.  Rows need 16-byte aligned bases and a row size (and ldx,
+ * ldy in bytes) that is a multiple of 16 bytes; otherwise SIMSD_ERR_ALIGN
+ * (use the all-to-all exchange).  world <= 8.
+ */
+int simsd_moe_ep_send(const void* x, int64_t ldx, const int32_t* send_slot, const int32_t* send_expert,
+                      int k, int H, int capacity, int rank, int world, void* const* peer_rows,
+                      void* const* peer_ids, int dtype, void* stream);
+int simsd_moe_ep_return(const void* y, int64_t ldy, const int32_t* recv_expert, int H, int capacity,
+                        int rank, int world, void* const* peer_back, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1393,6 +1393,57 @@ int simsd_moe_gather_rows(const void* x, int64_t ldx, const int32_t* slots, int 
                 (const int*)slots, out, (long long)ld_out, R, k, H, esize(dtype));
 }
 
+namespace {
+int ep_exchange(const void* src, int64_t ld_src, const int32_t* sel, const int32_t* expert, int k, int H,
+                int capacity, int rank, int world, void* const* rows, void* const* ids, int dtype, int mode,
+                void* stream) {
+  if (H < 1 || capacity < 1 || ld_src < H || world < 1 || world > EP_XCH_MAX_WORLD || rank < 0 || rank >= world ||
+      (mode == 0 && k < 1))
+    return SIMSD_ERR_SHAPE;
+  if (dtype != SIMSD_BF16 && dtype != SIMSD_F16 && dtype != SIMSD_F32) return SIMSD_ERR_DTYPE;
+  if (src == nullptr || sel == nullptr || rows == nullptr || (mode == 0 && (expert == nullptr || ids == nullptr)))
+    return SIMSD_ERR_SHAPE;
+  const long long entries = (long long)world * capacity;
+  if (entries >= (1LL << 31)) return SIMSD_ERR_SHAPE;
+  const long long rb = (long long)H * esize(dtype);
+  auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  if (!al(src) || (rb & 15) != 0 || ((ld_src * esize(dtype)) & 15) != 0 || rb >= (1LL << 31)) return SIMSD_ERR_ALIGN;
+  EpExchangeArgs a;
+  memset(&a, 0, sizeof(a));
+  for (int r = 0; r < world; ++r) {
+    if (rows[r] == nullptr || (mode == 0 && ids[r] == nullptr)) return SIMSD_ERR_SHAPE;
+    if (!al(rows[r])) return SIMSD_ERR_ALIGN;
+    a.rows[r] = rows[r];
+    if (mode == 0) a.ids[r] = static_cast<int*>(ids[r]);
+  }
+  if (current_device() < 0) return SIMSD_ERR_DEVICE;
+  a.src = src;
+  a.src_row_bytes = ld_src * esize(dtype);
+  a.sel = sel;
+  a.expert = expert;
+  a.entries = (int)entries;
+  a.cap = capacity;
+  a.k = k;
+  a.rank = rank;
+  a.mode = mode;
+  a.row_bytes = (int)rb;
+  return launch(ep_exchange_kernel, dim3((unsigned)((entries + 7) / 8)), dim3(256), 0, (cudaStream_t)stream, a);
+}
+}  // namespace
+
+int simsd_moe_ep_send(const void* x, int64_t ldx, const int32_t* send_slot, const int32_t* send_expert, int k, int H,
+                      int capacity, int rank, int world, void* const* peer_rows, void* const* peer_ids, int dtype,
+                      void* stream) {
+  return ep_exchange(x, ldx, send_slot, send_expert, k, H, capacity, rank, world, peer_rows, peer_ids, dtype, 0,
+                     stream);
+}
+
+int simsd_moe_ep_return(const void* y, int64_t ldy, const int32_t* recv_expert, int H, int capacity, int rank,
+                        int world, void* const* peer_back, int dtype, void* stream) {
+  return ep_exchange(y, ldy, recv_expert, nullptr, 1, H, capacity, rank, world, peer_back, nullptr, dtype, 1,
+                     stream);
+}
+
 int simsd_moe_combine(const void* ys, int64_t ldys, const int32_t* slot_row, const float* topk_weight, void* out,
                       int64_t ld_out, const void* add, int64_t ld_add, int T, int k, int H, int dtype, void* stream) {
   if (T < 0 || k < 1 || H < 1 || ldys < H || ld_out < H || (add && ld_add < H)) return SIMSD_ERR_SHAPE;

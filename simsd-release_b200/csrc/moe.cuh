@@ -677,6 +677,48 @@ __global__ void gather_rows_kernel(const void* x, long long ldx, const int* sort
   }
 }
 
+// ------------------------------------------------------------------ expert-parallel exchange
+// The expert-parallel layer's two exchanges as plain stores into every rank's
+// receive blocks (NVLink peer mappings; the own rank's block is local).
+// Bucket entry e = p * cap + i of this rank (p: the rank it goes to, i: its
+// position in the fixed-capacity bucket) lands in row rank * cap + i of rank
+// p's block, the layout an all-to-all of [world * cap] rows gives.
+//   send   (mode 0): row x[sel[e] / k] when sel[e] >= 0 (sel = the bucket's
+//          slots), and the local expert id expert[e] for every entry (-1 for
+//          an empty one), so the receiver's ids are all rewritten each call;
+//   return (mode 1): row y[e] when sel[e] >= 0 (sel = the received expert
+//          ids), back to the rank p it came from.
+// Only occupied entries move a row.  One warp per entry, 16-byte stores.
+constexpr int EP_XCH_MAX_WORLD = 8;   // ranks of a peer-store exchange (a node)
+struct EpExchangeArgs {
+  const void* src;            // x (send) or the experts' output y (return)
+  long long src_row_bytes;    // row stride of src in bytes
+  const int* sel;             // [entries]
+  const int* expert;          // [entries] (send only)
+  void* rows[EP_XCH_MAX_WORLD];   // every rank's row block [world * cap, H]
+  int* ids[EP_XCH_MAX_WORLD];     // every rank's id block [world * cap] (send only)
+  int entries, cap, k, rank, mode, row_bytes;
+};
+
+__global__ void __launch_bounds__(256) ep_exchange_kernel(const __grid_constant__ EpExchangeArgs a) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const int e = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (e >= a.entries) return;
+  const int p = e / a.cap;
+  const long long drow = (long long)a.rank * a.cap + (e - p * a.cap);
+  const int s = a.sel[e];
+  if (a.mode == 0 && lane == 0) a.ids[p][drow] = a.expert[e];
+  if (s < 0) return;
+  const long long srow = a.mode == 0 ? s / a.k : e;
+  const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.src) + srow * a.src_row_bytes);
+  uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.rows[p]) + drow * a.row_bytes);
+  const int n16 = a.row_bytes >> 4;
+#pragma unroll 4
+  for (int c = lane; c < n16; c += 32) dst[c] = src[c];
+}
+
 // ------------------------------------------------------------------ combine
 // out[t, h] = cast( sum_j  fp32(ys[row(t,j), h]) * w[t, j] )  (j in order, each
 // product rounded to fp32 before the add, as `.mul_(w).sum(dim=1)` does:

@@ -85,6 +85,8 @@ SIGNATURES: dict[str, tuple] = {
     "simsd_moe_ep_plan": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
     "simsd_moe_gather_rows": (_I, [_P, _L, _P, _I, _I, _I, _I, _P, _L, _P]),
     "simsd_moe_combine": (_I, [_P, _L, _P, _P, _P, _L, _P, _L, _I, _I, _I, _I, _P]),
+    "simsd_moe_ep_send": (_I, [_P, _L, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P]),
+    "simsd_moe_ep_return": (_I, [_P, _L, _P, _I, _I, _I, _I, _P, _I, _P]),
 }
 
 _lib = None

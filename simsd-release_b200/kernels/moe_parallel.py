@@ -17,8 +17,11 @@ holds experts [r E/g, (r+1) E/g)); every rank owns T_r tokens.  One layer:
    owner (simsd_moe_combine): out[t] = cast(sum_j fp32(y[t, j]) * w[t, j]) in j
    order, plus the shared expert (computed data-parallel on the owner).
 
-Fixed capacities make the exchange shape static, so the whole layer can be
-captured in a CUDA graph.  The default capacity T_r * k never drops a slot; a
+With a PeerExchange, steps 3 and 5 are plain NVLink peer stores of the
+occupied bucket entries only (simsd_moe_ep_send / simsd_moe_ep_return), each
+followed by a sync point, instead of all-to-alls of the whole fixed-capacity
+buckets.  Fixed capacities make the exchange shape static, so the whole layer
+can be captured in a CUDA graph.  The default capacity T_r * k never drops a slot; a
 smaller one may, which raises SIMSD_DEV_ERR_CAPACITY in the device error word.
 The reference runs its MoE layer on one GPU (kernels/moe_dispatch_fused.py,
 moe_infer's per-expert loop); this layer reproduces that computation's
@@ -29,6 +32,8 @@ collective plumbing can be exercised with CPU stand-ins under gloo; the default
 ops are the CUDA kernels (no CPU fallback).
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -146,16 +151,88 @@ class CudaOps:
         return thin_linear(thin_linear_silu_mul(x, w_gate, w_up), w_down)
 
 
+class PeerExchange:
+    """The layer's two exchanges as NVLink peer stores (simsd_moe_ep_send /
+    simsd_moe_ep_return) instead of all-to-alls of the fixed-capacity buckets.
+
+    Every rank maps every rank's row, id and return blocks ([world * capacity]
+    entries, cudaIpc mappings): a send stores each occupied bucket entry's
+    token row straight from x into the receiving rank's row block (no send
+    buffer) and every entry's expert id into its id block; a return stores
+    each received row's expert output back into its owner's return block.  A
+    sync point (simsd_allgather_wait on this object's signal block) follows
+    each, so only occupied entries cross NVLink and the layer stays capturable
+    (no sizes reach the host).  The blocks are reused by every call: a call's
+    sends overwrite rows the ranks read in the previous call only after every
+    rank has passed that call's second sync point, which it reaches only after
+    its reads.  Collective: every rank constructs it with the same capacity,
+    and every rank calls `send` and `give_back` at the same points.
+    """
+
+    def __init__(self, capacity: int, H: int, dtype: torch.dtype = torch.bfloat16, group=None):
+        from .parallel import SymmetricBlock, _group_info
+        self.rank, self.world = _group_info(group)
+        self.cap, self.H, self.dtype = capacity, H, dtype
+        n = self.world * capacity
+        esz = torch.empty((), dtype=dtype).element_size()
+        self.rows = SymmetricBlock(n * H * esz, group)
+        self.back = SymmetricBlock(n * H * esz, group)
+        self.ids = SymmetricBlock(n * 4, group)
+        self.sig = SymmetricBlock(_lib.SIGNAL_BYTES, group)
+        arr = lambda blk: (ctypes.c_void_p * self.world)(*blk.ptrs)
+        self._rows, self._back, self._ids, self._sig = arr(self.rows), arr(self.back), arr(self.ids), arr(self.sig)
+        self.recv = self.rows.tensor.view(dtype).view(n, H)
+        self.recv_expert = self.ids.tensor.view(torch.int32)[:n]
+        self.returned = self.back.tensor.view(dtype).view(n, H)
+
+    def _sync(self, dev) -> None:
+        ws = _lib.workspace(dev, _lib.lib().simsd_workspace_header_bytes())
+        _lib.check(_lib.lib().simsd_allgather_wait(self._sig, self.rank, self.world, ws.data_ptr(), ws.numel(),
+                                                   _lib.stream_ptr(dev)), "moe_ep sync")
+
+    def send(self, x: torch.Tensor, plan: dict, k: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """Rows and local expert ids of every rank's buckets for this rank:
+        views [world * capacity, H] and [world * capacity] of this rank's blocks."""
+        dev = _lib.require_cuda(x)
+        if x.stride(-1) != 1:
+            x = x.contiguous()
+        with _lib.device_guard(dev):
+            _lib.check(_lib.lib().simsd_moe_ep_send(
+                x.data_ptr(), x.stride(0), plan["send_slot"].data_ptr(), plan["send_expert"].data_ptr(), k,
+                self.H, self.cap, self.rank, self.world, self._rows, self._ids, _lib.dtype_code(x.dtype),
+                _lib.stream_ptr(dev)), "moe_ep_send")
+            self._sync(dev)
+        return self.recv, self.recv_expert
+
+    def give_back(self, y: torch.Tensor) -> torch.Tensor:
+        """Expert outputs of this rank's sent slots, laid out as the buckets
+        (view [world * capacity, H] of this rank's return block)."""
+        dev = _lib.require_cuda(y)
+        with _lib.device_guard(dev):
+            _lib.check(_lib.lib().simsd_moe_ep_return(
+                y.data_ptr(), y.stride(0), self.recv_expert.data_ptr(), self.H, self.cap, self.rank, self.world,
+                self._back, _lib.dtype_code(y.dtype), _lib.stream_ptr(dev)), "moe_ep_return")
+            self._sync(dev)
+        return self.returned
+
+    def close(self) -> None:
+        for blk in (self.rows, self.back, self.ids, self.sig):
+            blk.close()
+
+
 def ep_moe_layer(x: torch.Tensor, w_router: torch.Tensor, router_bias: torch.Tensor | None, k: int,
                  w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor, E: int, group=None,
                  capacity: int | None = None, shared: tuple | None = None, renorm: bool = True,
-                 scale: float = 1.0, ops=CudaOps, size_classes: bool = False) -> torch.Tensor:
+                 scale: float = 1.0, ops=CudaOps, size_classes: bool = False,
+                 exchange: PeerExchange | None = None) -> torch.Tensor:
     """One expert-parallel MoE layer for this rank's tokens x [T_r, H].
 
     w_gate, w_up [E/g, I, H] and w_down [E/g, H, I] are this rank's experts;
     w_router [E, H] and router_bias [E] are replicated.  `capacity` (rows per
     peer bucket) must be the same on every rank; default T_r * k.
-    `size_classes`: as moe_dispatch's, for skewed routing.
+    `size_classes`: as moe_dispatch's, for skewed routing.  `exchange`: a
+    PeerExchange of this capacity and H (NVLink peer stores); without it the
+    buckets cross with all_to_all_single.
     """
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     lo, hi = expert_range(E, rank, world)
@@ -165,18 +242,27 @@ def ep_moe_layer(x: torch.Tensor, w_router: torch.Tensor, router_bias: torch.Ten
     cap = capacity if capacity is not None else T * k
     ids, w = ops.route(x, w_router, router_bias, k, renorm, scale)
     plan = ops.plan(ids, E, world, cap)
-    send = ops.gather(x, plan["send_slot"], k)
-    recv = torch.empty_like(send)
-    dist.all_to_all_single(recv, send, group=group)
-    recv_e = torch.empty_like(plan["send_expert"])
-    dist.all_to_all_single(recv_e, plan["send_expert"], group=group)
+    if exchange is not None:
+        if exchange.cap != cap or exchange.H != H or exchange.world != world:
+            raise ValueError(f"exchange holds {exchange.world} x {exchange.cap} rows of {exchange.H}; "
+                             f"this layer needs {world} x {cap} rows of {H}")
+        recv, recv_e = exchange.send(x, plan, k)
+    else:
+        send = ops.gather(x, plan["send_slot"], k)
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=group)
+        recv_e = torch.empty_like(plan["send_expert"])
+        dist.all_to_all_single(recv_e, plan["send_expert"], group=group)
     if size_classes:
         from . import _lib
         with _lib.moe_size_classes(True):
             y = ops.experts(recv, recv_e, w_gate, w_up, w_down)
     else:
         y = ops.experts(recv, recv_e, w_gate, w_up, w_down)
-    back = torch.empty_like(y)
-    dist.all_to_all_single(back, y, group=group)
+    if exchange is not None:
+        back = exchange.give_back(y)
+    else:
+        back = torch.empty_like(y)
+        dist.all_to_all_single(back, y, group=group)
     add = ops.shared(x, *shared) if shared is not None else None
     return ops.combine(back, plan["slot_pos"], w, add)

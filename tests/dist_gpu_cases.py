@@ -56,6 +56,35 @@ def case_ep(dev):
         ref = moe_layer(x, wr, bias, k, wg, wu, wd)
         torch.cuda.synchronize()
     assert _close(got, ref), (rank, float((got.float() - ref.float()).abs().max()))
+    # the buckets exchanged by NVLink peer stores: the same rows reach the same
+    # experts, so the output is the all-to-all layer's bit for bit, call after
+    # call with different tokens (the blocks are reused) and inside a CUDA graph
+    from kernels.moe_parallel import PeerExchange
+    xch = PeerExchange(T * k, H, bf)
+    try:
+        with torch.inference_mode():
+            for i in range(4):
+                xi = torch.randn(T, H, generator=gx, device=dev).to(bf)
+                a2a = ep_moe_layer(xi, wr, bias, k, wg[lo:hi], wu[lo:hi], wd[lo:hi], E)
+                p2p = ep_moe_layer(xi, wr, bias, k, wg[lo:hi], wu[lo:hi], wd[lo:hi], E, exchange=xch)
+                torch.cuda.synchronize()
+                assert torch.equal(p2p, a2a), (rank, i, float((p2p.float() - a2a.float()).abs().max()))
+            xs = torch.randn(T, H, generator=gx, device=dev).to(bf)
+            want = ep_moe_layer(xs, wr, bias, k, wg[lo:hi], wu[lo:hi], wd[lo:hi], E)
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                yg = ep_moe_layer(xs, wr, bias, k, wg[lo:hi], wu[lo:hi], wd[lo:hi], E, exchange=xch)
+            for _ in range(3):
+                gr.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(yg, want), rank
+            del gr
+            torch.cuda.synchronize()
+        dist.barrier()
+        from kernels import _lib
+        assert _lib.device_error(dev) == 0
+    finally:
+        xch.close()
 
 
 def case_fused(dev):
