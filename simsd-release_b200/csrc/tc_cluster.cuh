@@ -475,19 +475,39 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
         for (int r = 0; r < p.world; ++r) store_f(p.peer_out[r], t * p.ld_out + p.col_offset + col, v, odt);
       }
     };
-    // Owner sums (step 5): thread `row` takes the owned unit (row, or gate/up
-    // pair) ep_l for activation-row groups ep_g0, ep_g0 + ep_P, ... (4 rows a
-    // group); fixed for the launch, so no division per tile.
-    constexpr int EP_JMAX = BMAX / 8;   // groups per thread: BMAX / 4 groups, >= 2 threads per unit
-    constexpr int EP_JC = EP_JMAX < 4 ? EP_JMAX : 4;   // groups summed at once (registers)
+    // Owner sums (step 5).  The CTA's owned outputs are a grid of units (rows,
+    // or gate/up pairs: output columns) x groups of 4 activation rows.  A work
+    // item is a block of EP_CW consecutive units (BMAX / 16 of them: 1, 2 or 4)
+    // and one group; items are numbered so that a quarter-warp's 8 lanes take
+    // 8 / EP_CW column blocks x EP_CW groups: their slot reads (16-byte group
+    // swz(l, g) of row l) fall on 8 different bank groups, and a lane's EP_CW
+    // results of one activation row are adjacent in y, so they leave as one
+    // 2-, 4- or 8-byte store.  Thread `row` takes items row, row + 128, ...;
+    // its first item is fixed for the launch.
+    constexpr int EP_CW = BMAX >= 64 ? 4 : (BMAX >= 32 ? 2 : 1);
     const int ep_units = S > 1 ? (p.silu ? ro.rows_of(q) / 2 : ro.rows_of(q)) : 0;
-    const int ep_P = ep_units > 0 ? 128 / ep_units : 0;
-    const int ep_l = ep_units > 0 ? row % ep_units : 0;
-    const int ep_g0 = ep_units > 0 ? row / ep_units : 0;
+    const int ep_ncb = (ep_units + EP_CW - 1) / EP_CW;                  // column blocks
     const int ep_groups = (nrows_all + 3) >> 2;
-    const bool ep_active = ep_units > 0 && ep_g0 < ep_P;
-    // plain stores into y (AG: into every rank's y)
+    const int ep_gsup = (ep_groups + EP_CW - 1) / EP_CW;                 // groups / EP_CW, rounded up
+    const int ep_items = ep_ncb * ep_gsup * EP_CW;
+    auto ep_item = [&](int it, int& cb, int& g) {
+      const int lo = it % EP_CW, rest = it / EP_CW;
+      cb = rest % ep_ncb;
+      g = (rest / ep_ncb) * EP_CW + lo;
+    };
+    int ep_cb0 = 0, ep_g0 = 0;
+    if (ep_ncb > 0) ep_item(row, ep_cb0, ep_g0);
+    // plain stores into y (AG: into every rank's y); 8- and 4-byte stores need
+    // every target base aligned to them
     const bool ep_fast = p.amax_keys == nullptr && (AG || p.world <= 1);
+    int ep_base_al = 8;
+    {
+      const int nt = AG ? p.world : 1;
+      for (int r = 0; r < nt; ++r) {
+        const uintptr_t b = reinterpret_cast<uintptr_t>(AG ? p.peer_out[r] : p.out);
+        ep_base_al = min(ep_base_al, (b & 7) == 0 ? 8 : ((b & 3) == 0 ? 4 : 2));
+      }
+    }
     const long long ep_ld = p.ld_out;
     const int ep_silu = p.silu;
     const int ep_rows_out = p.rows_out;
@@ -598,73 +618,113 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_cluster_kernel(const __grid_
       }
       tc_fence_before();
       mbar_arrive(smem_u32(&acce_bar[a]));
-      const int ep_col = out_col0 + q * ro.per + ep_l;
-      const float ep_bias =
-          (ep_active && !ep_silu && p.bias && ep_col < ep_rows_out) ? load_f(p.bias, ep_col, odt) : 0.0f;
+      // first output column this CTA owns; the bias of the first item's
+      // columns, fetched before the wait
+      const int ep_c0 = out_col0 + q * ro.per;
+      float ep_bias[EP_CW];
+#pragma unroll
+      for (int u = 0; u < EP_CW; ++u) {
+        const int c = ep_cb0 * EP_CW + u;
+        ep_bias[u] = (row < ep_items && !ep_silu && p.bias && c < ep_units && ep_c0 + c < ep_rows_out)
+                         ? load_f(p.bias, ep_c0 + c, odt) : 0.0f;
+      }
       // -- 4. every peer's rows for this CTA have landed
       if (!named_bar_and(1, 128, mbar_wait_cluster(red_full_u32, i & 1, abort_flag, p.err))) break;
-      // -- 5. all 128 threads share the owned outputs: each sums one (row,
-      // activation row) over the S slots in rank (= K) order and writes it to
-      // y (the barrier of step 4 ordered every thread's own-slot writes)
+      // -- 5. all 128 threads share the owned outputs: each item's sums run
+      // over the S slots in rank (= K) order (the barrier of step 4 ordered
+      // every thread's own-slot writes); slot rows are clamped so every load
+      // is in range and none waits on a branch; only the stores are predicated
       {
-        // Each thread sums its unit's outputs for up to EP_JMAX groups over the
-        // S slots in rank (= K) order.  Group indices are clamped so every slot
-        // load is in range and none waits on a branch (all loads of a slot are
-        // independent); only the stores are predicated.
-        if (ep_active && ep_col < ep_rows_out) {
-          auto slot4 = [&](int r, int l, int g) -> float4 {
-            return reinterpret_cast<const float4*>(red + ((r * slot_rows) + l) * BMAX)[swz(l, g)];
-          };
-          uint16_t* const yc = reinterpret_cast<uint16_t*>(outp) + ep_col;
+        auto slot4 = [&](int r, int l, int g) -> float4 {
+          return reinterpret_cast<const float4*>(red + ((r * slot_rows) + l) * BMAX)[swz(l, g)];
+        };
 #pragma unroll 1
-          for (int jc = 0; jc < EP_JMAX; jc += EP_JC) {
-            if (ep_g0 + jc * ep_P >= ep_groups) break;
-            float4 a[EP_JC], b[EP_JC];
+        for (int it = row; it < ep_items; it += 128) {
+          int cb = ep_cb0, g = ep_g0;
+          if (it != row) ep_item(it, cb, g);
+          const int u0 = cb * EP_CW;
+          const int ncol = min(min(EP_CW, ep_units - u0), ep_rows_out - (ep_c0 + u0));
+          if (g >= ep_groups || ncol <= 0) continue;
+          float4 a[EP_CW], b[EP_CW];
 #pragma unroll
-            for (int j = 0; j < EP_JC; ++j) a[j] = b[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          for (int u = 0; u < EP_CW; ++u) a[u] = b[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
-            for (int r = 0; r < TC_CL_MAX; ++r) {
-              if (r >= S) break;
+          for (int r = 0; r < TC_CL_MAX; ++r) {
+            if (r >= S) break;
 #pragma unroll
-              for (int j = 0; j < EP_JC; ++j) {
-                const int g = min(ep_g0 + (jc + j) * ep_P, ep_groups - 1);
-                const float4 f = slot4(r, ep_l, g);
-                a[j].x = __fadd_rn(a[j].x, f.x);
-                a[j].y = __fadd_rn(a[j].y, f.y);
-                a[j].z = __fadd_rn(a[j].z, f.z);
-                a[j].w = __fadd_rn(a[j].w, f.w);
-                if (ep_silu) {
-                  const float4 h = slot4(r, ro.per + ep_l, g);
-                  b[j].x = __fadd_rn(b[j].x, h.x);
-                  b[j].y = __fadd_rn(b[j].y, h.y);
-                  b[j].z = __fadd_rn(b[j].z, h.z);
-                  b[j].w = __fadd_rn(b[j].w, h.w);
-                }
+            for (int u = 0; u < EP_CW; ++u) {
+              const int l = u0 + min(u, ncol - 1);
+              const float4 f = slot4(r, l, g);
+              a[u].x = __fadd_rn(a[u].x, f.x);
+              a[u].y = __fadd_rn(a[u].y, f.y);
+              a[u].z = __fadd_rn(a[u].z, f.z);
+              a[u].w = __fadd_rn(a[u].w, f.w);
+              if (ep_silu) {
+                const float4 h = slot4(r, ro.per + l, g);
+                b[u].x = __fadd_rn(b[u].x, h.x);
+                b[u].y = __fadd_rn(b[u].y, h.y);
+                b[u].z = __fadd_rn(b[u].z, h.z);
+                b[u].w = __fadd_rn(b[u].w, h.w);
               }
             }
+          }
+          float bias[EP_CW];
 #pragma unroll
-            for (int j = 0; j < EP_JC; ++j) {
-              const int g = ep_g0 + (jc + j) * ep_P;
-              if (g < ep_groups) {
-                const float va[4] = {a[j].x, a[j].y, a[j].z, a[j].w};
-                const float vb[4] = {b[j].x, b[j].y, b[j].z, b[j].w};
+          for (int u = 0; u < EP_CW; ++u)
+            bias[u] = it == row ? ep_bias[u]
+                                : ((!ep_silu && p.bias && u < ncol) ? load_f(p.bias, ep_c0 + u0 + u, odt) : 0.0f);
+          const int col = ep_c0 + u0;
 #pragma unroll
-                for (int k4 = 0; k4 < 4; ++k4) {
-                  const int t = 4 * g + k4;
-                  if (t < nrows_all) {
-                    const float v = ep_silu ? silu_mul(va[k4], vb[k4]) : __fadd_rn(va[k4], ep_bias);
-                    if (!ep_fast) {
-                      put(t, ep_col, v);
-                    } else if constexpr (F32) {
-                      reinterpret_cast<float*>(outp)[(long long)t * ep_ld + ep_col] = v;
-                    } else if constexpr (AG) {
-                      const uint16_t bits = f32_to_16bit(v, odt);
-                      const long long at = (long long)t * ep_ld + p.col_offset + ep_col;
-                      for (int r = 0; r < p.world; ++r) reinterpret_cast<uint16_t*>(p.peer_out[r])[at] = bits;
-                    } else {
-                      yc[(long long)t * ep_ld] = f32_to_16bit(v, odt);
-                    }
+          for (int k4 = 0; k4 < 4; ++k4) {
+            const int t = 4 * g + k4;
+            if (t >= nrows_all) break;
+            float v[EP_CW];
+#pragma unroll
+            for (int u = 0; u < EP_CW; ++u) {
+              const float x = k4 == 0 ? a[u].x : k4 == 1 ? a[u].y : k4 == 2 ? a[u].z : a[u].w;
+              const float y = k4 == 0 ? b[u].x : k4 == 1 ? b[u].y : k4 == 2 ? b[u].z : b[u].w;
+              v[u] = ep_silu ? silu_mul(x, y) : __fadd_rn(x, bias[u]);
+            }
+            if (!ep_fast) {
+#pragma unroll
+              for (int u = 0; u < EP_CW; ++u)
+                if (u < ncol) put(t, col + u, v[u]);
+            } else if constexpr (F32) {
+              float* dst = reinterpret_cast<float*>(outp) + (long long)t * ep_ld + col;
+#pragma unroll
+              for (int u = 0; u < EP_CW; ++u)
+                if (u < ncol) dst[u] = v[u];
+            } else {
+              // 16-bit outputs, packed two to a word where the columns allow
+              uint32_t pk[(EP_CW + 1) / 2] = {};
+#pragma unroll
+              for (int u = 0; u + 1 < EP_CW; u += 2)
+                pk[u / 2] = (uint32_t)f32_to_16bit(v[u], odt) | ((uint32_t)f32_to_16bit(v[u + 1], odt) << 16);
+              const long long e = (long long)t * ep_ld + (AG ? (long long)p.col_offset : 0ll) + col;
+              const int nt = AG ? p.world : 1;
+              for (int r = 0; r < nt; ++r) {
+                uint16_t* dst = reinterpret_cast<uint16_t*>(AG ? p.peer_out[r] : outp) + e;
+                bool done_st = false;
+                if constexpr (EP_CW == 4) {
+                  if (ncol == 4 && ep_base_al >= 8 && (e & 3) == 0) {
+                    *reinterpret_cast<uint2*>(dst) = make_uint2(pk[0], pk[1]);
+                    done_st = true;
                   }
+                }
+                if constexpr (EP_CW >= 2) {
+                  if (!done_st && ep_base_al >= 4 && (e & 1) == 0) {
+#pragma unroll
+                    for (int u = 0; u < EP_CW; u += 2) {
+                      if (u + 1 < ncol) *reinterpret_cast<uint32_t*>(dst + u) = pk[u / 2];
+                      else if (u < ncol) dst[u] = f32_to_16bit(v[u], odt);
+                    }
+                    done_st = true;
+                  }
+                }
+                if (!done_st) {
+#pragma unroll
+                  for (int u = 0; u < EP_CW; ++u)
+                    if (u < ncol) dst[u] = f32_to_16bit(v[u], odt);
                 }
               }
             }
