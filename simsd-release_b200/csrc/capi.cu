@@ -1003,7 +1003,12 @@ int simsd_moe_route_ex(const void* x, int64_t ldx, int x_dtype, const void* wr, 
                     al16(wr) && ((w_dtype != SIMSD_F32 && ldw % 8 == 0) || (w_dtype == SIMSD_F32 && ldw % 4 == 0));
   if (fast) {
     const int sms = sm_count_of(dev) > 0 ? sm_count_of(dev) : 148;
-    int tt = T >= 16 * sms ? 16 : T >= 4 * sms ? 8 : 4;
+    // tokens per block: 16 from 16 per SM, else 8 (measured on the MoE layer
+    // of H = 2048, E = 256: 4-token blocks were 3-4 us slower at T = 16..256
+    // even with the experts split over blocks; 16-token blocks slower at
+    // T = 1024).  SIMSD_ROUTE_TT (4, 8 or 16) pins it.
+    static const int tt_pin = env_choice("SIMSD_ROUTE_TT", {0, 4, 8, 16}, 0);
+    int tt = tt_pin > 0 ? tt_pin : (T >= 16 * sms ? 16 : 8);
     auto smem_for = [&](int t) { return (size_t)t * H * 4 + (size_t)2 * t * E * sizeof(float); };
     while (tt > 4 && smem_for(tt) > 200 * 1024) tt >>= 1;
     if (smem_for(tt) <= 200 * 1024) {
