@@ -45,7 +45,11 @@ import torch.nn.functional as F  # noqa: E402
 METRIC = "thin-M linear & MoE grouped-GEMM HBM GB/s (% peak); synthetic verify tok/s"
 SHAPES = [("qkv", 4096, 6144, False), ("o", 4096, 4096, False),
           ("gate_up", 4096, 24576, True), ("down", 12288, 4096, False)]
-MS = [4, 8, 16, 32, 64]
+# Activation heights of a step, in launch order.  The linears of a step are
+# independent; in the end-to-end step only the first height's inputs (copied
+# before its linears) and the last height's outputs (copied after them) are not
+# hidden behind other linears, so the step starts and ends with small heights.
+MS = [4, 64, 32, 16, 8]
 POOL = 2
 
 
@@ -459,7 +463,7 @@ def gpu_arm(args):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights; no dataset exists for this path)",
         "config": {"workload": "SDAR-8B thin-M linear sweep (BASELINE configs[1])",
-                   "shapes": {n: [K, N] for n, K, N, _ in SHAPES}, "M": MS,
+                   "shapes": {n: [K, N] for n, K, N, _ in SHAPES}, "M": sorted(MS), "step_order": MS,
                    "gate_up_epilogue": "SiLU(gate)*up -> [M,12288]",
                    "parallelism": f"column-parallel x{world}" + ((" + NCCL all-gather" if args.nccl_gather else
                                                                   " + all-gather fused into the GEMM (NVLink peer stores)")
@@ -1109,7 +1113,7 @@ def reference_arm(args):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
         "config": {"workload": "SDAR-8B thin-M linear sweep (BASELINE configs[1])",
-                   "shapes": {n: [K, N] for n, K, N, _ in SHAPES}, "M": MS,
+                   "shapes": {n: [K, N] for n, K, N, _ in SHAPES}, "M": sorted(MS), "step_order": MS,
                    "parallelism": "host CPU (rank 0 only)"},
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
                          "sample": "each step = the full sweep (20 bf16 F.linear + silu*mul), torch eager CPU"},
