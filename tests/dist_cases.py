@@ -101,6 +101,39 @@ class CpuEpOps:
         return F.linear(F.silu(F.linear(x, w_gate)) * F.linear(x, w_up), w_down)
 
 
+class CpuExchange:
+    """CPU stand-in with PeerExchange's contract: persistent receive and return
+    blocks of [world * capacity] rows in which only occupied bucket entries are
+    rewritten (the rest keep whatever an earlier call left there), and an id
+    block rewritten in full by every send (-1 = empty)."""
+
+    def __init__(self, capacity, H, world):
+        self.cap, self.H, self.world = capacity, H, world
+        n = world * capacity
+        self.recv = torch.full((n, H), float("nan"))
+        self.recv_expert = torch.full((n,), -7, dtype=torch.int32)
+        self.returned = torch.full((n, H), float("nan"))
+
+    def send(self, x, plan, k):
+        rows = CpuEpOps.gather(x, plan["send_slot"], k)
+        rows[plan["send_slot"] < 0] = float("nan")          # what an empty entry would carry
+        got = torch.empty_like(rows)
+        dist.all_to_all_single(got, rows)
+        dist.all_to_all_single(self.recv_expert, plan["send_expert"].to(torch.int32))
+        occ = self.recv_expert >= 0
+        self.recv[occ] = got[occ]
+        return self.recv, self.recv_expert
+
+    def give_back(self, y):
+        sent = y.clone()
+        sent[self.recv_expert < 0] = float("nan")
+        got = torch.empty_like(sent)
+        dist.all_to_all_single(got, sent)
+        keep = ~torch.isnan(got).any(dim=1)
+        self.returned[keep] = got[keep]
+        return self.returned
+
+
 def case_ep_moe():
     """Expert-parallel layer (2 ranks, CPU ops) == the same computation done
     token by token on one process, for every rank's tokens; plus the bucket
@@ -130,6 +163,21 @@ def case_ep_moe():
         if shared is not None:
             ref = ref + CpuEpOps.shared(xs[rank], *shared)
         assert torch.equal(out, ref), (rank, capacity, (out - ref).abs().max())
+    # the peer-store exchange's contract (only occupied entries rewritten, the
+    # rest stale): the same output as the all-to-all layer, call after call
+    xch = CpuExchange(T * k, H, world)
+    for i in range(3):
+        xi = torch.randn(T, H, generator=g) * (i + 1)
+        want = MP.ep_moe_layer(xi, wr, bias, k, wg[lo:hi], wu[lo:hi], wd[lo:hi], E, shared=sh, ops=CpuEpOps)
+        got = MP.ep_moe_layer(xi, wr, bias, k, wg[lo:hi], wu[lo:hi], wd[lo:hi], E, shared=sh, ops=CpuEpOps,
+                              exchange=xch)
+        assert torch.equal(got, want), (rank, i, (got - want).abs().max())
+    try:
+        MP.ep_moe_layer(xs[rank], wr, bias, k, wg[lo:hi], wu[lo:hi], wd[lo:hi], E, capacity=T * k + 1,
+                        ops=CpuEpOps, exchange=xch)
+        raise AssertionError("a capacity other than the exchange's must be refused")
+    except ValueError:
+        pass
     # plan invariants: every slot sent once, to the rank holding its expert, in slot order
     ids = torch.randint(0, E, (T, k), generator=g)
     p = O.ep_plan(ids.numpy(), E, world, T * k)
